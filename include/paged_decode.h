@@ -1,0 +1,190 @@
+/*
+ * paged_decode.h -- C ABI of the B200 (sm_100a) paged-KV decode path.
+ *
+ * This is the drop-in boundary for the block-table decode path of RAIN-LOJK/llm-serving.
+ * The reference implements the path in Python + one Triton kernel; every entry point
+ * below replaces one piece of it and names the reference interface it stands for
+ * (paths are relative to the reference project root).
+ *
+ * Conventions
+ *  - Plain pointers to device memory, element strides (not bytes), int32/int64 sizes.
+ *    The head-dim stride of every tensor is 1.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Every function returns PD_OK (0) or a PD_ERR_* status; nothing aborts the process.
+ *    Argument errors are detected on the host before any launch. Device-side problems
+ *    (a bounded wait that ran out, an out-of-range slot or block id in the append path)
+ *    never fault or trap: the kernel skips the access and records a bit in a per-device
+ *    error word that pd_device_error() reads.
+ *  - dtype codes: PD_F32, PD_F16, PD_BF16. q, K, V and out share one dtype.
+ *  - K/V pools have the reference layout (n_blocks, block_size, n_kv_head, head_dim)
+ *    (model/paged.py:115-123); block tables are int32 (B, max_blocks) with a unit
+ *    column stride; seqlen is int32 (B,) (model/triton_decode.py:17-26).
+ */
+#ifndef PAGED_DECODE_H
+#define PAGED_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status / dtypes */
+#define PD_OK 0
+#define PD_ERR_INVALID 1     /* bad argument (shape, stride, alignment, range)          */
+#define PD_ERR_UNSUPPORTED 2 /* shape the library has no kernel for (e.g. head_dim 512) */
+#define PD_ERR_CUDA 3        /* a CUDA runtime call or launch failed                     */
+#define PD_ERR_WORKSPACE 4   /* workspace pointer missing or smaller than required      */
+
+#define PD_F32 0
+#define PD_F16 1
+#define PD_BF16 2
+
+/* Device error word bits (pd_device_error). */
+#define PD_DEVERR_WAIT_TIMEOUT 1u  /* an mbarrier wait exceeded its time limit          */
+#define PD_DEVERR_APPEND_RANGE 2u  /* append skipped a slot / block id outside the pool  */
+
+/* Human-readable name of a status code (static storage). */
+const char* pd_status_string(int status);
+
+/* Library ABI version (increments on any signature change). */
+int pd_abi_version(void);
+
+/* Reads the calling thread's current device's error word into *bits and, if `clear`,
+ * resets it. Synchronises the device. No reference counterpart: the Triton kernel has no
+ * device-side status (model/triton_decode.py:63-66 trusts the table instead). */
+int pd_device_error(unsigned int* bits, int clear);
+
+/* ---------------------------------------------------------------- decode
+ *
+ * pd_decode replaces `paged_decode(q, k_cache, v_cache, block_table, seqlen, *, scale)`
+ * (model/triton_decode.py:250-328) after its validation: one launch of the decode kernel.
+ *
+ *   q        (B, H, D)       strides q_sb, q_sh (elements); 16-byte aligned rows
+ *   k_cache  (n_blocks, block_size, H_kv, D) strides k_strides[0..2] (block, token, head)
+ *   v_cache  same geometry, strides v_strides[0..2]
+ *   block_table (B, max_blocks) int32, row stride bt_stride, unit column stride
+ *   seqlen   (B,) int32; values are clamped to [0, max_blocks * block_size] on device
+ *   out      (B, H, D)       strides o_sb, o_sh
+ *   scale_log2 = scale * log2(e)  (model/triton_decode.py:291-292)
+ *   workspace: device memory of at least pd_decode_workspace_bytes(...) bytes whose
+ *     first pd_decode_counter_bytes(...) bytes are zero before the first call; the kernel
+ *     leaves them zero again. One workspace must not be used by two launches that may
+ *     run concurrently.
+ *
+ * Row b, head h reads only the first ceil(seqlen[b] / block_size) table entries;
+ * zero-length rows produce exact zeros (model/triton_decode.py:639).
+ */
+size_t pd_decode_counter_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim);
+size_t pd_decode_workspace_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head,
+                                 int32_t head_dim, int32_t dtype);
+
+int pd_decode(const void* q, int64_t q_sb, int64_t q_sh,
+              const void* k_cache, const void* v_cache, int64_t n_blocks, int32_t block_size,
+              const int64_t* k_strides, const int64_t* v_strides,
+              const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+              const int32_t* seqlen, void* out, int64_t o_sb, int64_t o_sh,
+              int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
+              int32_t dtype, float scale_log2, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/* ---------------------------------------------------------------- decode plan
+ *
+ * pd_plan_* replaces `PagedDecodePlan` / `paged_decode_plan` (model/triton_decode.py:
+ * 331-538): every layer's pool is validated and its two TMA descriptors are encoded once;
+ * pd_plan_run(layer, q, out) is the per-layer launch (model/triton_decode.py:500-520).
+ * The block table and seqlen are held by address, so in-place updates are seen by the next
+ * run (the reference's invariant, model/triton_decode.py:357-363). q and out of every run
+ * are contiguous (B, H, D). The plan owns no device memory: `workspace` is the caller's
+ * (same contract as pd_decode). The handle is host memory released by pd_plan_destroy.
+ */
+typedef struct pd_plan pd_plan;
+
+int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
+                   const void* const* v_caches, int64_t n_blocks, int32_t block_size,
+                   const int64_t* k_strides, const int64_t* v_strides,
+                   const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+                   const int32_t* seqlen, int32_t batch, int32_t n_head, int32_t n_kv_head,
+                   int32_t head_dim, int32_t dtype, float scale_log2, void* workspace,
+                   size_t workspace_bytes);
+int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, void* stream);
+void pd_plan_destroy(pd_plan* plan);
+
+/* ---------------------------------------------------------------- split-KV partials
+ *
+ * The split-KV variant for long contexts and for context-parallel decode across GPUs.
+ * No reference counterpart: split-K is "the documented next step" of the reference
+ * (model/triton_decode.py:44-47). pd_decode_partials computes the same attention as
+ * pd_decode but, instead of the normalised output, writes per (row, q head) the fp32 triple
+ *   m[b, h]       running max of the log2-scaled scores (-inf for an empty range)
+ *   l[b, h]       sum of exp2(score - m)
+ *   acc[b, h, :]  sum of exp2(score - m) * v   (unnormalised)
+ * for the tokens [0, seqlen[b]) of the given table. All three are contiguous: m and l are
+ * (B, H), acc is (B, H, D). pd_lse_merge combines n_parts such triples -- part p's m and l
+ * start at m_parts + p * ml_part_stride (resp. l_parts), its acc at acc_parts +
+ * p * acc_part_stride, each (B, H[, D]) contiguous -- into out = sum_p 2^(m_p-M) acc_p /
+ * max(sum_p 2^(m_p-M) l_p, 1) with M = max_p m_p, which is the reference's normalisation
+ * acc / max(l, 1) (model/triton_decode.py:639) applied to the union of the parts.
+ */
+int pd_decode_partials(const void* q, int64_t q_sb, int64_t q_sh,
+                       const void* k_cache, const void* v_cache, int64_t n_blocks,
+                       int32_t block_size, const int64_t* k_strides, const int64_t* v_strides,
+                       const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+                       const int32_t* seqlen, float* m_out, float* l_out, float* acc_out,
+                       int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
+                       int32_t dtype, float scale_log2, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+int pd_lse_merge(const float* m_parts, const float* l_parts, const float* acc_parts,
+                 int64_t ml_part_stride, int64_t acc_part_stride, int32_t n_parts,
+                 int32_t batch, int32_t n_head, int32_t head_dim, void* out, int64_t o_sb,
+                 int64_t o_sh, int32_t dtype, void* stream);
+
+/* ---------------------------------------------------------------- paged-KV append
+ *
+ * pd_kv_append_slots replaces the body of `PagedPool.write_slots(layer, slot_ids, k, v)`
+ * (model/paged.py:188-239): token i of k/v (n_tokens, H_kv, D) is copied into flat pool row
+ * slot_ids[i] (= block_id * block_size + offset) of both pools, converting the source dtype
+ * to the pool dtype with round-to-nearest-even (torch's Tensor.to). slot_dtype is PD_SLOT_I32
+ * or PD_SLOT_I64. Slots outside [0, n_blocks * block_size) are skipped and flagged with
+ * PD_DEVERR_APPEND_RANGE.
+ *
+ * pd_kv_append_table is the fused decode append behind `PagedKV.write(layer, k, v)`
+ * (model/paged.py:503-520 with the slot map of _refresh_slots, 474-501): row b's token goes
+ * to slot block_table[b, pos[b] / bs] * bs + pos[b] % bs, computed in the kernel from the
+ * int32 block table and the int64 position vector, so no slot map is materialised.
+ *
+ * Source strides are element strides of (token/row, head, d) with unit d stride.
+ */
+#define PD_SLOT_I32 0
+#define PD_SLOT_I64 1
+
+int pd_kv_append_slots(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                       const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                       int32_t pool_dtype, const void* slot_ids, int32_t slot_dtype,
+                       const void* k, const int64_t* k_strides, const void* v,
+                       const int64_t* v_strides, int32_t src_dtype, int64_t n_tokens,
+                       int32_t n_kv_head, int32_t head_dim, void* stream);
+
+int pd_kv_append_table(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                       const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                       int32_t pool_dtype, const int32_t* block_table, int64_t bt_stride,
+                       int32_t max_blocks, const int64_t* pos, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       int32_t src_dtype, int32_t batch, int32_t n_kv_head, int32_t head_dim,
+                       void* stream);
+
+/* ---------------------------------------------------------------- tuning / introspection
+ * Launch shape of the decode kernel: warps per CTA, pipeline stages per warp, CTAs per SM
+ * and the minimum number of KV tiles a warp is given before fewer warps are used. Values
+ * <= 0 keep the current setting. Changing them changes pd_decode_workspace_bytes. */
+int pd_set_decode_tuning(int32_t warps_per_cta, int32_t stages, int32_t ctas_per_sm,
+                         int32_t min_tiles_per_warp);
+int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_per_sm,
+                         int32_t* min_tiles_per_warp);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PAGED_DECODE_H */

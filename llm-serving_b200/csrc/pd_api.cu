@@ -1,0 +1,630 @@
+// pd_api.cu -- the extern "C" boundary declared in include/paged_decode.h.
+//
+// Host-side argument checks, TMA descriptor encoding for the paged pools, workspace layout,
+// launch-shape selection and the plan handle. All device work is in pd_decode_*.cu,
+// pd_append.cu and pd_merge.cu.
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "../../include/paged_decode.h"
+#include "pd_internal.h"
+
+namespace pd {
+
+__device__ unsigned g_error_word = 0;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSmemPerBlock = 232448;  // 227 KB opt-in limit on sm_100
+
+struct Tuning {
+  int warps = 8;
+  int stages = 3;
+  int ctas_per_sm = 1;
+  int min_tiles = 4;
+};
+Tuning g_tuning;
+std::mutex g_mutex;
+
+int g_sm_count[kMaxDevices] = {0};
+unsigned* g_err_ptr[kMaxDevices] = {nullptr};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int elem_size(int dtype) { return dtype == PD_F32 ? 4 : 2; }
+bool valid_dtype(int dtype) { return dtype == PD_F32 || dtype == PD_F16 || dtype == PD_BF16; }
+bool pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+int ilog2_host(int64_t x) {
+  int r = 0;
+  while ((int64_t(1) << (r + 1)) <= x) ++r;
+  return r;
+}
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= kMaxDevices) return PD_ERR_CUDA;
+  return PD_OK;
+}
+
+int sm_count(int dev) {
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return 0;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+unsigned* error_word(int dev) {
+  if (g_err_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<unsigned*>(p);
+  }
+  return g_err_ptr[dev];
+}
+
+int load_encoder() {
+  if (g_encode) return PD_OK;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_encode) return PD_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return PD_ERR_CUDA;
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return PD_OK;
+}
+
+// Decode-kernel geometry that the host needs (mirrors DecodeCfg in pd_decode_kernel.cuh).
+struct Geometry {
+  int d_index;   // 0..5 for head_dim 8..256
+  int gt;        // q heads per worker item
+  int gt_index;  // 0..3 for gt 1, 2, 4, 8
+  int n_gchunks;
+  int tile;        // tokens per stage
+  int box_tokens;  // tokens per TMA box
+  int stage_bytes;
+};
+
+int geometry(int n_head, int n_kv_head, int head_dim, int block_size, int dtype, Geometry* g) {
+  if (!valid_dtype(dtype)) return PD_ERR_INVALID;
+  if (n_kv_head < 1 || n_head < 1 || n_head % n_kv_head != 0) return PD_ERR_INVALID;
+  if (!pow2(head_dim) || !pow2(block_size)) return PD_ERR_INVALID;
+  if (head_dim < 8 || head_dim > 256) return PD_ERR_UNSUPPORTED;
+  const int group = n_head / n_kv_head;
+  int gt = 8;
+  while (group % gt != 0) gt >>= 1;
+  g->gt = gt;
+  g->gt_index = ilog2_host(gt);
+  g->n_gchunks = group / gt;
+  g->d_index = ilog2_host(head_dim) - 3;
+  const int row_bytes = head_dim * elem_size(dtype);
+  g->tile = 4096 / row_bytes;
+  g->box_tokens = block_size < g->tile ? block_size : g->tile;
+  g->stage_bytes = 2 * 4096;
+  return PD_OK;
+}
+
+DecodeLaunchFn launcher_for(int dtype, const Geometry& g) {
+  switch (dtype) {
+    case PD_F32: return decode_launcher_f32(g.d_index, g.gt_index);
+    case PD_F16: return decode_launcher_f16(g.d_index, g.gt_index);
+    case PD_BF16: return decode_launcher_bf16(g.d_index, g.gt_index);
+  }
+  return nullptr;
+}
+
+struct Launch {
+  int grid;
+  int warps;
+  int stages;
+  int min_tiles;
+  int rows_per_launch;  // batch chunk that fits the shared-memory prefix arrays
+  int arrays_off;
+  int stage_off;
+  size_t smem;
+};
+
+size_t smem_for(int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
+  const size_t bars = round_up(size_t(warps) * stages * 8, 16);
+  const size_t arrays = round_up(size_t(32 + 2 * rows + 1) * 4, 16);
+  *arrays_off = int(bars);
+  *stage_off = int(bars + arrays);
+  return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(warps) * stages * stage_bytes;
+}
+
+int launch_shape(int dev, int batch, const Geometry& g, Launch* L) {
+  Tuning t;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    t = g_tuning;
+  }
+  const int sms = sm_count(dev);
+  if (sms <= 0) return PD_ERR_CUDA;
+  L->warps = t.warps;
+  L->stages = t.stages;
+  L->min_tiles = t.min_tiles;
+  L->grid = sms * t.ctas_per_sm;
+  int rows = batch < 1 ? 1 : batch;
+  if (rows > 4096) rows = 4096;
+  for (;;) {
+    L->smem = smem_for(L->warps, L->stages, rows, g.stage_bytes, &L->arrays_off, &L->stage_off);
+    if (L->smem * size_t(t.ctas_per_sm) <= size_t(kMaxSmemPerBlock)) break;
+    if (rows <= 256) return PD_ERR_INVALID;  // tuning asks for more shared memory than exists
+    rows /= 2;
+  }
+  L->rows_per_launch = rows;
+  return PD_OK;
+}
+
+struct WorkspaceLayout {
+  size_t counters;  // bytes
+  size_t ml_off, acc_off, total;
+};
+
+WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, int head_dim,
+                                 const Launch& L) {
+  WorkspaceLayout w;
+  const int rows = batch < L.rows_per_launch ? batch : L.rows_per_launch;
+  w.counters = round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 4, 256);
+  const size_t workers = size_t(L.grid) * L.warps;
+  w.ml_off = w.counters;
+  w.acc_off = w.ml_off + round_up(workers * 2 * 2 * g.gt * 4, 256);
+  w.total = w.acc_off + round_up(workers * 2 * size_t(g.gt) * head_dim * 4, 256);
+  return w;
+}
+
+int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_size, int n_kv_head,
+                int head_dim, const int64_t* strides, int dtype, int box_tokens) {
+  if (load_encoder() != PD_OK) return PD_ERR_CUDA;
+  const int es = elem_size(dtype);
+  if (!aligned16(base)) return PD_ERR_INVALID;
+  for (int i = 0; i < 3; ++i) {
+    if (strides[i] <= 0 || (strides[i] * es) % 16 != 0 || strides[i] * es >= (int64_t(1) << 40))
+      return PD_ERR_INVALID;
+  }
+  CUtensorMapDataType t = dtype == PD_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : dtype == PD_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[4] = {cuuint64_t(head_dim), cuuint64_t(n_kv_head), cuuint64_t(block_size),
+                              cuuint64_t(n_blocks)};
+  // Byte strides of dims 1..3: head, token-in-block, block.
+  const cuuint64_t gstr[3] = {cuuint64_t(strides[2] * es), cuuint64_t(strides[1] * es),
+                              cuuint64_t(strides[0] * es)};
+  const cuuint32_t box[4] = {cuuint32_t(head_dim), 1u, cuuint32_t(box_tokens), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = g_encode(map, t, 4, const_cast<void*>(base), dims, gstr, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PD_OK : PD_ERR_INVALID;
+}
+
+// Everything fixed for one (pool layout, table, seqlen, batch) -- shared by pd_decode,
+// pd_decode_partials and the plan.
+struct Prepared {
+  Geometry g;
+  Launch L;
+  WorkspaceLayout ws;
+  DecodeLaunchFn fn;
+  DecodeParams base;  // q/out/partials pointers filled per launch
+};
+
+int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* block_table,
+            int64_t bt_stride, int32_t max_blocks, const int32_t* seqlen, int32_t batch,
+            int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t dtype, float scale_log2,
+            void* workspace, size_t workspace_bytes) {
+  if (batch < 0 || max_blocks < 0 || n_blocks < 1) return PD_ERR_INVALID;
+  int st = geometry(n_head, n_kv_head, head_dim, block_size, dtype, &P->g);
+  if (st != PD_OK) return st;
+  P->fn = launcher_for(dtype, P->g);
+  if (P->fn == nullptr) return PD_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
+  st = launch_shape(dev, batch, P->g, &P->L);
+  if (st != PD_OK) return st;
+  P->ws = workspace_layout(batch, n_kv_head, P->g, head_dim, P->L);
+  if (batch > 0) {
+    if (workspace == nullptr || workspace_bytes < P->ws.total) return PD_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PD_ERR_WORKSPACE;
+    if (block_table == nullptr && max_blocks > 0) return PD_ERR_INVALID;
+    if (seqlen == nullptr) return PD_ERR_INVALID;
+  }
+  if (max_blocks > 0 && bt_stride < max_blocks) return PD_ERR_INVALID;
+  const int64_t capacity = int64_t(max_blocks) * block_size;
+  if (capacity > (int64_t(1) << 30)) return PD_ERR_INVALID;
+  unsigned* err = error_word(dev);
+  if (err == nullptr) return PD_ERR_CUDA;
+
+  DecodeParams& p = P->base;
+  p = DecodeParams{};
+  p.table = block_table;
+  p.bt_stride = bt_stride;
+  p.seqlen = seqlen;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  p.counters = reinterpret_cast<int*>(ws);
+  p.ws_ml = reinterpret_cast<float*>(ws + P->ws.ml_off);
+  p.ws_acc = reinterpret_cast<float*>(ws + P->ws.acc_off);
+  p.err = err;
+  p.max_blocks = max_blocks;
+  p.capacity = int32_t(capacity);
+  p.batch = batch;
+  p.n_head = n_head;
+  p.n_kv_head = n_kv_head;
+  p.group = n_head / n_kv_head;
+  p.n_gchunks = P->g.n_gchunks;
+  p.block_size = block_size;
+  p.log2_bs = ilog2_host(block_size);
+  p.box_tokens = P->g.box_tokens;
+  p.log2_box = ilog2_host(P->g.box_tokens);
+  p.stages = P->L.stages;
+  p.min_tiles = P->L.min_tiles;
+  p.smem_arrays_off = P->L.arrays_off;
+  p.smem_stage_off = P->L.stage_off;
+  p.scale_log2 = scale_log2;
+  return PD_OK;
+}
+
+int check_rows(const void* ptr, int64_t sb, int64_t sh, int dtype) {
+  const int es = elem_size(dtype);
+  if (ptr == nullptr || !aligned16(ptr)) return PD_ERR_INVALID;
+  if ((sb * es) % 16 != 0 || (sh * es) % 16 != 0) return PD_ERR_INVALID;
+  return PD_OK;
+}
+
+// Launches the decode kernel over the batch in chunks of rows_per_launch rows.
+int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& vmap, const void* q,
+                 int64_t q_sb, int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float* pm,
+                 float* pl, float* pacc, int mode, int dtype, cudaStream_t stream) {
+  const int batch = P.base.batch;
+  const int es = elem_size(dtype);
+  for (int b0 = 0; b0 < batch; b0 += P.L.rows_per_launch) {
+    const int rows = batch - b0 < P.L.rows_per_launch ? batch - b0 : P.L.rows_per_launch;
+    DecodeParams p = P.base;
+    p.batch = rows;
+    p.mode = mode;
+    p.q = static_cast<const unsigned char*>(q) + int64_t(b0) * q_sb * es;
+    p.q_sb = q_sb;
+    p.q_sh = q_sh;
+    if (mode == 0) {
+      p.out = static_cast<unsigned char*>(out) + int64_t(b0) * o_sb * es;
+      p.o_sb = o_sb;
+      p.o_sh = o_sh;
+    } else {
+      // m, l are (B, H) and acc is (B, H, D), all contiguous: offset by b0 rows.
+      const int64_t head_dim = int64_t(8) << P.g.d_index;
+      p.part_m = pm + int64_t(b0) * p.n_head;
+      p.part_l = pl + int64_t(b0) * p.n_head;
+      p.part_acc = pacc + int64_t(b0) * p.n_head * head_dim;
+    }
+    if (P.base.table) p.table = P.base.table + int64_t(b0) * P.base.bt_stride;
+    p.seqlen = P.base.seqlen + b0;
+    const size_t smem = smem_for(P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
+                                 &p.smem_stage_off);
+    cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream);
+    if (e != cudaSuccess) return PD_ERR_CUDA;
+  }
+  return PD_OK;
+}
+
+int decode_common(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache, const void* v_cache,
+                  int64_t n_blocks, int32_t block_size, const int64_t* k_strides,
+                  const int64_t* v_strides, const int32_t* block_table, int64_t bt_stride,
+                  int32_t max_blocks, const int32_t* seqlen, void* out, int64_t o_sb, int64_t o_sh,
+                  float* pm, float* pl, float* pacc, int mode, int32_t batch, int32_t n_head,
+                  int32_t n_kv_head, int32_t head_dim, int32_t dtype, float scale_log2,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (k_strides == nullptr || v_strides == nullptr) return PD_ERR_INVALID;
+  Prepared P;
+  int st = prepare(&P, n_blocks, block_size, block_table, bt_stride, max_blocks, seqlen, batch,
+                   n_head, n_kv_head, head_dim, dtype, scale_log2, workspace, workspace_bytes);
+  if (st != PD_OK) return st;
+  if (batch == 0) return PD_OK;
+  if (check_rows(q, q_sb, q_sh, dtype) != PD_OK) return PD_ERR_INVALID;
+  if (mode == 0 && check_rows(out, o_sb, o_sh, dtype) != PD_OK) return PD_ERR_INVALID;
+  if (mode == 1 && (pm == nullptr || pl == nullptr || pacc == nullptr || !aligned16(pacc)))
+    return PD_ERR_INVALID;
+  CUtensorMap kmap, vmap;
+  st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype,
+                   P.g.box_tokens);
+  if (st != PD_OK) return st;
+  st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype,
+                   P.g.box_tokens);
+  if (st != PD_OK) return st;
+  return run_prepared(P, kmap, vmap, q, q_sb, q_sh, out, o_sb, o_sh, pm, pl, pacc, mode, dtype,
+                      static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace pd
+
+using namespace pd;
+
+struct pd_plan {
+  Prepared P;
+  int32_t n_layer;
+  int32_t dtype;
+  int64_t q_sb, q_sh;
+  std::vector<CUtensorMap> kmaps;
+  std::vector<CUtensorMap> vmaps;
+};
+
+extern "C" {
+
+const char* pd_status_string(int status) {
+  switch (status) {
+    case PD_OK: return "ok";
+    case PD_ERR_INVALID: return "invalid argument";
+    case PD_ERR_UNSUPPORTED: return "unsupported shape";
+    case PD_ERR_CUDA: return "CUDA error";
+    case PD_ERR_WORKSPACE: return "workspace missing or too small";
+  }
+  return "unknown status";
+}
+
+int pd_abi_version(void) { return kAbiVersion; }
+
+int pd_device_error(unsigned int* bits, int clear) {
+  if (bits == nullptr) return PD_ERR_INVALID;
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return PD_ERR_CUDA;
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_error_word, sizeof(v)) != cudaSuccess) return PD_ERR_CUDA;
+  *bits = v;
+  if (clear && v != 0) {
+    unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) != cudaSuccess) return PD_ERR_CUDA;
+  }
+  return PD_OK;
+}
+
+size_t pd_decode_counter_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim) {
+  Geometry g;
+  if (geometry(n_head, n_kv_head, head_dim, 16, PD_BF16, &g) != PD_OK) return 0;
+  const int rows = batch < 1 ? 1 : (batch > 4096 ? 4096 : batch);
+  return round_up(size_t(rows) * n_kv_head * g.n_gchunks * 4, 256);
+}
+
+size_t pd_decode_workspace_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
+                                 int32_t dtype) {
+  Geometry g;
+  if (geometry(n_head, n_kv_head, head_dim, 16, dtype, &g) != PD_OK) return 0;
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return 0;
+  Launch L;
+  if (launch_shape(dev, batch, g, &L) != PD_OK) return 0;
+  return workspace_layout(batch, n_kv_head, g, head_dim, L).total;
+}
+
+int pd_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache, const void* v_cache,
+              int64_t n_blocks, int32_t block_size, const int64_t* k_strides,
+              const int64_t* v_strides, const int32_t* block_table, int64_t bt_stride,
+              int32_t max_blocks, const int32_t* seqlen, void* out, int64_t o_sb, int64_t o_sh,
+              int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t dtype,
+              float scale_log2, void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_common(q, q_sb, q_sh, k_cache, v_cache, n_blocks, block_size, k_strides, v_strides,
+                       block_table, bt_stride, max_blocks, seqlen, out, o_sb, o_sh, nullptr, nullptr,
+                       nullptr, 0, batch, n_head, n_kv_head, head_dim, dtype, scale_log2, workspace,
+                       workspace_bytes, stream);
+}
+
+int pd_decode_partials(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache,
+                       const void* v_cache, int64_t n_blocks, int32_t block_size,
+                       const int64_t* k_strides, const int64_t* v_strides,
+                       const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+                       const int32_t* seqlen, float* m_out, float* l_out, float* acc_out,
+                       int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
+                       int32_t dtype, float scale_log2, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return decode_common(q, q_sb, q_sh, k_cache, v_cache, n_blocks, block_size, k_strides, v_strides,
+                       block_table, bt_stride, max_blocks, seqlen, nullptr, 0, 0, m_out, l_out,
+                       acc_out, 1, batch, n_head, n_kv_head, head_dim, dtype, scale_log2, workspace,
+                       workspace_bytes, stream);
+}
+
+int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
+                   const void* const* v_caches, int64_t n_blocks, int32_t block_size,
+                   const int64_t* k_strides, const int64_t* v_strides, const int32_t* block_table,
+                   int64_t bt_stride, int32_t max_blocks, const int32_t* seqlen, int32_t batch,
+                   int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t dtype,
+                   float scale_log2, void* workspace, size_t workspace_bytes) {
+  if (plan == nullptr) return PD_ERR_INVALID;
+  *plan = nullptr;
+  if (n_layer < 1 || k_caches == nullptr || v_caches == nullptr || batch < 1) return PD_ERR_INVALID;
+  if (k_strides == nullptr || v_strides == nullptr) return PD_ERR_INVALID;
+  pd_plan* h = new (std::nothrow) pd_plan;
+  if (h == nullptr) return PD_ERR_INVALID;
+  int st = prepare(&h->P, n_blocks, block_size, block_table, bt_stride, max_blocks, seqlen, batch,
+                   n_head, n_kv_head, head_dim, dtype, scale_log2, workspace, workspace_bytes);
+  if (st != PD_OK) {
+    delete h;
+    return st;
+  }
+  h->n_layer = n_layer;
+  h->dtype = dtype;
+  h->q_sh = head_dim;
+  h->q_sb = int64_t(n_head) * head_dim;
+  h->kmaps.resize(n_layer);
+  h->vmaps.resize(n_layer);
+  for (int layer = 0; layer < n_layer; ++layer) {
+    st = encode_pool(&h->kmaps[layer], k_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
+                     k_strides, dtype, h->P.g.box_tokens);
+    if (st == PD_OK)
+      st = encode_pool(&h->vmaps[layer], v_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
+                       v_strides, dtype, h->P.g.box_tokens);
+    if (st != PD_OK) {
+      delete h;
+      return st;
+    }
+  }
+  *plan = h;
+  return PD_OK;
+}
+
+int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, void* stream) {
+  if (plan == nullptr || layer < 0 || layer >= plan->n_layer) return PD_ERR_INVALID;
+  if (check_rows(q, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  if (check_rows(out, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
+                      plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
+                      static_cast<cudaStream_t>(stream));
+}
+
+void pd_plan_destroy(pd_plan* plan) { delete plan; }
+
+int pd_lse_merge(const float* m_parts, const float* l_parts, const float* acc_parts,
+                 int64_t ml_part_stride, int64_t acc_part_stride, int32_t n_parts, int32_t batch,
+                 int32_t n_head, int32_t head_dim, void* out, int64_t o_sb, int64_t o_sh,
+                 int32_t dtype, void* stream) {
+  if (!valid_dtype(dtype) || n_parts < 1 || batch < 0 || n_head < 1) return PD_ERR_INVALID;
+  if (head_dim < 4 || head_dim % 4 != 0) return PD_ERR_UNSUPPORTED;
+  if (batch == 0) return PD_OK;
+  if (m_parts == nullptr || l_parts == nullptr || acc_parts == nullptr || out == nullptr ||
+      !aligned16(acc_parts) || acc_part_stride % 4 != 0)
+    return PD_ERR_INVALID;
+  if (ml_part_stride < int64_t(batch) * n_head || acc_part_stride < int64_t(batch) * n_head * head_dim)
+    return PD_ERR_INVALID;
+  MergeParams p;
+  p.m = m_parts;
+  p.l = l_parts;
+  p.acc = acc_parts;
+  p.out = out;
+  p.o_sb = o_sb;
+  p.o_sh = o_sh;
+  p.ml_stride = ml_part_stride;
+  p.acc_stride = acc_part_stride;
+  p.n_parts = n_parts;
+  p.batch = batch;
+  p.n_head = n_head;
+  p.head_dim = head_dim;
+  return launch_merge(p, dtype, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PD_OK
+                                                                                  : PD_ERR_CUDA;
+}
+
+static int append_common(AppendParams& p, int32_t pool_dtype, int32_t src_dtype,
+                         const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                         const int64_t* k_strides, const int64_t* v_strides, void* stream) {
+  if (!valid_dtype(pool_dtype) || !valid_dtype(src_dtype)) return PD_ERR_INVALID;
+  if (p.n_tokens < 0 || p.n_kv_head < 1 || p.head_dim < 1 || p.block_size < 1 || p.n_blocks < 1)
+    return PD_ERR_INVALID;
+  if (p.n_tokens == 0) return PD_OK;
+  if (!k_pool_strides || !v_pool_strides || !k_strides || !v_strides) return PD_ERR_INVALID;
+  if (!p.k_pool || !p.v_pool || !p.k || !p.v) return PD_ERR_INVALID;
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
+  p.err = error_word(dev);
+  if (p.err == nullptr) return PD_ERR_CUDA;
+  p.kp_sb = k_pool_strides[0];
+  p.kp_sn = k_pool_strides[1];
+  p.kp_sh = k_pool_strides[2];
+  p.vp_sb = v_pool_strides[0];
+  p.vp_sn = v_pool_strides[1];
+  p.vp_sh = v_pool_strides[2];
+  p.k_s0 = k_strides[0];
+  p.k_s1 = k_strides[1];
+  p.v_s0 = v_strides[0];
+  p.v_s1 = v_strides[1];
+  // 8-wide vector path when every row start of every tensor is 16-byte aligned for both
+  // element sizes involved.
+  const int es_s = elem_size(src_dtype), es_d = elem_size(pool_dtype);
+  auto ok_src = [&](const void* base, int64_t s0, int64_t s1) {
+    return aligned16(base) && (s0 * es_s) % 16 == 0 && (s1 * es_s) % 16 == 0;
+  };
+  auto ok_dst = [&](const void* base, int64_t a, int64_t b, int64_t c) {
+    return aligned16(base) && (a * es_d) % 16 == 0 && (b * es_d) % 16 == 0 && (c * es_d) % 16 == 0;
+  };
+  const bool vec = p.head_dim % 8 == 0 && ok_src(p.k, p.k_s0, p.k_s1) && ok_src(p.v, p.v_s0, p.v_s1) &&
+                   ok_dst(p.k_pool, p.kp_sb, p.kp_sn, p.kp_sh) &&
+                   ok_dst(p.v_pool, p.vp_sb, p.vp_sn, p.vp_sh);
+  cudaError_t e = launch_append(p, src_dtype, pool_dtype, vec, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PD_OK : PD_ERR_CUDA;
+}
+
+int pd_kv_append_slots(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                       const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                       int32_t pool_dtype, const void* slot_ids, int32_t slot_dtype, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       int32_t src_dtype, int64_t n_tokens, int32_t n_kv_head, int32_t head_dim,
+                       void* stream) {
+  if (slot_dtype != PD_SLOT_I32 && slot_dtype != PD_SLOT_I64) return PD_ERR_INVALID;
+  if (slot_ids == nullptr && n_tokens > 0) return PD_ERR_INVALID;
+  AppendParams p{};
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.n_blocks = n_blocks;
+  p.slots = slot_ids;
+  p.k = k;
+  p.v = v;
+  p.n_tokens = n_tokens;
+  p.block_size = block_size;
+  p.n_kv_head = n_kv_head;
+  p.head_dim = head_dim;
+  p.use_table = 0;
+  p.slot_i64 = slot_dtype == PD_SLOT_I64;
+  return append_common(p, pool_dtype, src_dtype, k_pool_strides, v_pool_strides, k_strides,
+                       v_strides, stream);
+}
+
+int pd_kv_append_table(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                       const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                       int32_t pool_dtype, const int32_t* block_table, int64_t bt_stride,
+                       int32_t max_blocks, const int64_t* pos, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       int32_t src_dtype, int32_t batch, int32_t n_kv_head, int32_t head_dim,
+                       void* stream) {
+  if (batch > 0 && (block_table == nullptr || pos == nullptr || max_blocks < 1)) return PD_ERR_INVALID;
+  AppendParams p{};
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.n_blocks = n_blocks;
+  p.table = block_table;
+  p.bt_stride = bt_stride;
+  p.max_blocks = max_blocks;
+  p.pos = pos;
+  p.k = k;
+  p.v = v;
+  p.n_tokens = batch;
+  p.block_size = block_size;
+  p.n_kv_head = n_kv_head;
+  p.head_dim = head_dim;
+  p.use_table = 1;
+  return append_common(p, pool_dtype, src_dtype, k_pool_strides, v_pool_strides, k_strides,
+                       v_strides, stream);
+}
+
+int pd_set_decode_tuning(int32_t warps_per_cta, int32_t stages, int32_t ctas_per_sm,
+                         int32_t min_tiles_per_warp) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  Tuning t = g_tuning;
+  if (warps_per_cta > 0) t.warps = warps_per_cta;
+  if (stages > 0) t.stages = stages;
+  if (ctas_per_sm > 0) t.ctas_per_sm = ctas_per_sm;
+  if (min_tiles_per_warp > 0) t.min_tiles = min_tiles_per_warp;
+  if (t.warps > 8 || t.stages < 2 || t.stages > 16 || t.ctas_per_sm > 8) return PD_ERR_INVALID;
+  if (size_t(t.warps) * t.stages * 8192 + 4096 > size_t(kMaxSmemPerBlock)) return PD_ERR_INVALID;
+  g_tuning = t;
+  return PD_OK;
+}
+
+int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_per_sm,
+                         int32_t* min_tiles_per_warp) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (warps_per_cta) *warps_per_cta = g_tuning.warps;
+  if (stages) *stages = g_tuning.stages;
+  if (ctas_per_sm) *ctas_per_sm = g_tuning.ctas_per_sm;
+  if (min_tiles_per_warp) *min_tiles_per_warp = g_tuning.min_tiles;
+  return PD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,251 @@
+// pd_common.cuh -- device helpers shared by the paged-decode kernels (sm_100a).
+//
+// PTX wrappers for mbarrier / TMA (cp.async.bulk.tensor), element conversions and the
+// parameter blocks the host launchers fill. Nothing here allocates or synchronises.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pd {
+
+constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// Device error word bits (mirrors PD_DEVERR_* in include/paged_decode.h).
+constexpr unsigned DEVERR_WAIT_TIMEOUT = 1u;
+constexpr unsigned DEVERR_APPEND_RANGE = 2u;
+
+// A bounded mbarrier wait gives up after this many nanoseconds of %globaltimer.
+constexpr unsigned long long WAIT_LIMIT_NS = 1000000000ull;      // 1 s
+constexpr unsigned long long DRAIN_LIMIT_NS = 100000000ull;      // 0.1 s per stage
+
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x >> 1); }
+
+// ------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Warp-collective bounded wait: returns true once every lane has observed the phase with
+// the given parity complete, false (uniformly) once `limit_ns` has elapsed.
+__device__ __forceinline__ bool warp_wait_phase(uint32_t bar, uint32_t parity,
+                                                unsigned long long limit_ns) {
+  bool done = mbar_try_wait(bar, parity);
+  if (__all_sync(FULL_MASK, done)) return true;
+  unsigned long long start = global_timer_ns();
+  for (unsigned iter = 1;; ++iter) {
+    if (!done) done = mbar_try_wait(bar, parity);
+    if (__all_sync(FULL_MASK, done)) return true;
+    if ((iter & 63u) == 0) {
+      unsigned long long now = __shfl_sync(FULL_MASK, global_timer_ns(), 0);
+      unsigned long long t0 = __shfl_sync(FULL_MASK, start, 0);
+      if (now - t0 > limit_ns) return false;
+    }
+  }
+}
+
+// 4-D tiled TMA load into shared memory, completing `bytes` on the mbarrier.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------------ element conversion
+// A "chunk" is 16 bytes of one row: 8 bf16/fp16 or 4 fp32 elements.
+
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static constexpr int PER_CHUNK = 4;
+  __device__ __forceinline__ static void unpack(const uint4& r, float* f) {
+    f[0] = __uint_as_float(r.x);
+    f[1] = __uint_as_float(r.y);
+    f[2] = __uint_as_float(r.z);
+    f[3] = __uint_as_float(r.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+  __device__ __forceinline__ static float to_float(float x) { return x; }
+  __device__ __forceinline__ static float from_float(float x) { return x; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int PER_CHUNK = 8;
+  // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 pattern.
+  __device__ __forceinline__ static void unpack2(uint32_t w, float* f) {
+    f[0] = __uint_as_float(w << 16);
+    f[1] = __uint_as_float(w & 0xffff0000u);
+  }
+  __device__ __forceinline__ static void unpack(const uint4& r, float* f) {
+    unpack2(r.x, f + 0);
+    unpack2(r.y, f + 2);
+    unpack2(r.z, f + 4);
+    unpack2(r.w, f + 6);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // round to nearest even
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ __forceinline__ static __nv_bfloat16 from_float(float x) {
+    return __float2bfloat16_rn(x);
+  }
+};
+
+template <>
+struct Elem<__half> {
+  static constexpr int PER_CHUNK = 8;
+  __device__ __forceinline__ static void unpack2(uint32_t w, float* f) {
+    float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    f[0] = v.x;
+    f[1] = v.y;
+  }
+  __device__ __forceinline__ static void unpack(const uint4& r, float* f) {
+    unpack2(r.x, f + 0);
+    unpack2(r.y, f + 2);
+    unpack2(r.z, f + 4);
+    unpack2(r.w, f + 6);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  __device__ __forceinline__ static float to_float(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
+};
+
+// ------------------------------------------------------------------ parameter blocks
+
+// Everything the decode kernel reads besides the two TMA descriptors. Element strides.
+struct DecodeParams {
+  const void* q;
+  int64_t q_sb, q_sh;
+  void* out;  // mode 0: (B, H, D) in the input dtype
+  int64_t o_sb, o_sh;
+  float* part_m;    // mode 1: (B, H)
+  float* part_l;    // mode 1: (B, H)
+  float* part_acc;  // mode 1: (B, H, D)
+  const int32_t* table;
+  int64_t bt_stride;
+  const int32_t* seqlen;
+  int* counters;    // (B * H_kv * n_gchunks) arrival counters, zero between launches
+  float* ws_ml;     // (workers * 2, 2 * GT) partial m | l
+  float* ws_acc;    // (workers * 2, GT * D) partial accumulators
+  unsigned* err;    // device error word
+  int32_t max_blocks;
+  int32_t capacity;  // max_blocks * block_size (seqlen clamp)
+  int32_t batch;
+  int32_t n_head;
+  int32_t n_kv_head;
+  int32_t group;      // n_head / n_kv_head
+  int32_t n_gchunks;  // group / GT
+  int32_t block_size;
+  int32_t log2_bs;
+  int32_t box_tokens;  // tokens per TMA box = min(TILE, block_size)
+  int32_t log2_box;
+  int32_t mode;        // 0: normalised output, 1: (m, l, acc) partials
+  int32_t stages;      // pipeline depth per warp
+  int32_t min_tiles;   // minimum tiles per active warp
+  int32_t smem_arrays_off;
+  int32_t smem_stage_off;
+  float scale_log2;
+};
+
+struct AppendParams {
+  void* k_pool;
+  void* v_pool;
+  int64_t kp_sb, kp_sn, kp_sh;
+  int64_t vp_sb, vp_sn, vp_sh;
+  int64_t n_blocks;
+  const void* slots;  // slot-id variant (int32 or int64)
+  const int32_t* table;
+  int64_t bt_stride;
+  const int64_t* pos;
+  const void* k;
+  const void* v;
+  int64_t k_s0, k_s1, v_s0, v_s1;
+  unsigned* err;
+  int64_t n_tokens;
+  int32_t max_blocks;
+  int32_t block_size;
+  int32_t n_kv_head;
+  int32_t head_dim;
+  int32_t use_table;  // 1: slot from block table + pos, 0: from slots
+  int32_t slot_i64;
+};
+
+struct MergeParams {
+  const float* m;
+  const float* l;
+  const float* acc;
+  void* out;
+  int64_t o_sb, o_sh;
+  int64_t ml_stride;   // elements between parts of m (and of l)
+  int64_t acc_stride;  // elements between parts of acc
+  int32_t n_parts;
+  int32_t batch;
+  int32_t n_head;
+  int32_t head_dim;
+};
+
+// Host-side launcher signatures (one instantiation per dtype / head_dim / group tile).
+typedef cudaError_t (*DecodeLaunchFn)(const DecodeParams&, const CUtensorMap&, const CUtensorMap&,
+                                      dim3, dim3, size_t, cudaStream_t);
+
+}  // namespace pd

@@ -1,0 +1,20 @@
+// pd_decode_f32.cu -- decode kernel instantiations for float K/V (one file per dtype so the
+// build compiles them in parallel). Head dims 8..256, q-head chunks of 1, 2, 4 or 8.
+#include "pd_decode_kernel.cuh"
+
+namespace pd {
+
+#define PD_ROW(D) \
+  {launch_decode<float, D, 1>, launch_decode<float, D, 2>, launch_decode<float, D, 4>, \
+   launch_decode<float, D, 8>}
+
+static const DecodeLaunchFn kTable[6][4] = {PD_ROW(8),  PD_ROW(16),  PD_ROW(32),
+                                            PD_ROW(64), PD_ROW(128), PD_ROW(256)};
+#undef PD_ROW
+
+DecodeLaunchFn decode_launcher_f32(int d_index, int gt_index) {
+  if (d_index < 0 || d_index >= 6 || gt_index < 0 || gt_index >= 4) return nullptr;
+  return kTable[d_index][gt_index];
+}
+
+}  // namespace pd

@@ -1,0 +1,714 @@
+// pd_decode_kernel.cuh -- paged GQA decode attention for sm_100a.
+//
+// What it computes (model/triton_decode.py:544-643 of the reference): for every row b and
+// query head h, out[b, h] = softmax(q[b, h] . K^T * scale) V over the first seqlen[b]
+// logical tokens of the row, token t living at pool block block_table[b, t / bs], slot
+// t % bs. Scores are formed in fp32 and scaled by scale * log2(e) so the online softmax
+// uses exp2; the result is acc / max(l, 1), which makes a zero-length row exactly zero.
+//
+// How (B200 design, not the reference's):
+//  * Work unit = one KV tile of TILE tokens of one (row, kv head, q-head chunk) item;
+//    TILE * head_dim * sizeof(T) = 4 KB for K (and again for V). The units of all items
+//    are laid end to end (row-major, kv head, q-head chunk, tile) and cut into equal
+//    contiguous ranges, one per worker. Every worker gets the same number of KV bytes
+//    (+-1 tile) whatever the length skew, and a long row is spread over many workers.
+//  * Worker = one warp. It owns a private ring of `stages` shared-memory stages, each
+//    filled by two 4-D TMA tile loads (K and V, box = head_dim x 1 head x box_tokens x 1
+//    block) that complete on the stage's mbarrier. Lane 0 issues; the warp consumes tile
+//    k while tiles k+1 .. k+stages-1 are in flight, then refills the stage it just read.
+//    There is no block-level synchronisation after the prologue.
+//  * q.K: lanes span head_dim (16 B per lane per row), a warp-wide load covers 32/LPR
+//    rows. Partial dot products for all (token, q head) pairs of the tile are finished by
+//    a butterfly reduce-scatter, so each shuffle carries useful sums. Online softmax in
+//    fp32 per q head, then every lane fetches the probabilities of its own rows by
+//    shuffle and accumulates P.V in fp32 registers. No tensor cores: with a group of 2
+//    heads this is a GEMV at 2 flop/byte and the HBM stream is the roof.
+//  * A worker whose range covers a whole item writes the output directly. A split item
+//    leaves (m, l, acc) in the workspace; the last of its workers to finish (arrival
+//    counter, __threadfence) merges the pieces with the log-sum-exp rule and resets the
+//    counter, so split-KV costs no extra launch.
+//  * Block-table entries are fetched 32 at a time into one register per lane (plus the
+//    next 32 prefetched), so a TMA issue never waits on a dependent global load inside a
+//    row. Table entries past ceil(seqlen / bs) are never read; an entry outside the pool
+//    makes TMA fill zeros instead of faulting.
+//  * Every mbarrier wait is bounded (1 s of %globaltimer). On expiry the warp records
+//    DEVERR_WAIT_TIMEOUT, drains its in-flight copies (bounded again) and returns.
+#pragma once
+
+#include "pd_common.cuh"
+
+namespace pd {
+
+template <typename T, int D, int GT>
+struct DecodeCfg {
+  static constexpr int ES = int(sizeof(T));
+  static constexpr int ROW_BYTES = D * ES;
+  static constexpr int CHUNKS = ROW_BYTES / 16;  // 16 B chunks per K/V row
+  static_assert(CHUNKS >= 1, "head_dim * sizeof(T) must be at least 16 bytes");
+  static constexpr int LPR = CHUNKS >= 32 ? 32 : CHUNKS;  // lanes per row
+  static constexpr int LOG_LPR = ilog2(LPR);
+  static constexpr int CPL = CHUNKS / LPR;  // chunks per lane per row
+  static constexpr int EPC = 16 / ES;       // elements per chunk
+  static constexpr int EPL = CPL * EPC;     // elements per lane per row
+  static constexpr int RPL = 32 / LPR;      // rows covered by one warp-wide load
+  static constexpr int LOG_RPL = ilog2(RPL);
+  static constexpr int TILE_BYTES = 4096;   // K bytes per stage (same again for V)
+  static constexpr int TILE = TILE_BYTES / ROW_BYTES;  // tokens per stage
+  static constexpr int LOG_TILE = ilog2(TILE);
+  static constexpr int NT = TILE / RPL;  // row slots per lane
+  static constexpr int NV = NT * GT;     // partial scores per lane before reduction
+  static constexpr int LOG_NV = ilog2(NV);
+  static constexpr int SL = LOG_LPR < LOG_NV ? LOG_LPR : LOG_NV;  // scatter levels
+  static constexpr int AL = LOG_LPR - SL;                          // all-reduce levels
+  static constexpr int R = NV >> SL;  // reduced scores held per lane
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static_assert(TILE >= RPL, "tile smaller than one warp load");
+  static_assert((1 << LOG_TILE) == TILE, "tile must be a power of two");
+};
+
+// Position of a worker inside the unit sequence.
+struct Cursor {
+  int b;      // row
+  int item;   // kv head * n_gchunks + q-head chunk within the row
+  int h;      // kv head (= item / n_gchunks)
+  int gc;     // q-head chunk (= item % n_gchunks)
+  int tile;   // tile within the item
+  int ntile;  // tiles of this row's items
+  int len;    // clamped seqlen of the row
+};
+
+__device__ __forceinline__ void cursor_advance(Cursor& c, const int* pre, const int* lens, int batch,
+                                               int items_per_row, int n_gchunks) {
+  if (++c.tile < c.ntile) return;
+  c.tile = 0;
+  if (++c.gc == n_gchunks) {
+    c.gc = 0;
+    ++c.h;
+  }
+  if (++c.item < items_per_row) return;
+  c.item = 0;
+  c.h = 0;
+  c.gc = 0;
+  do {
+    ++c.b;
+  } while (c.b < batch && pre[c.b + 1] == pre[c.b]);
+  if (c.b < batch) {
+    c.ntile = pre[c.b + 1] - pre[c.b];
+    c.len = lens[c.b];
+  }
+}
+
+// Worker that owns unit u when `units` units are cut into `workers` ranges
+// [w*units/workers, (w+1)*units/workers).
+__device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) {
+  return int(((u + 1) * int64_t(workers) - 1) / units);
+}
+
+template <typename T, int D, int GT>
+__global__ void __launch_bounds__(256, 1)
+    pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap) {
+  using C = DecodeCfg<T, D, GT>;
+  using E = Elem<T>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int S = p.stages;
+  const int B = p.batch;
+
+  // Dynamic shared memory: [mbarriers | warp_sums[32] | lens[B] | pre[B+1] | pad | stages].
+  // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off);
+  int* lens = warp_sums + 32;
+  int* pre = lens + B;  // B + 1 entries: exclusive prefix of tiles per row
+  const uint32_t smem_base = smem_addr(smem);
+  unsigned char* stage_base =
+      smem + (((smem_base + uint32_t(p.smem_stage_off) + 1023u) & ~1023u) - smem_base);
+
+  if (tid == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+
+  // ---- prologue: clamp lengths, tiles per row, block-wide exclusive scan -------------
+  {
+    const int per = (B + blockDim.x - 1) / blockDim.x;
+    const int b0 = min(B, tid * per);
+    const int b1 = min(B, b0 + per);
+    int local = 0;
+    for (int b = b0; b < b1; ++b) {
+      int len = __ldg(p.seqlen + b);
+      len = len < 0 ? 0 : (len > p.capacity ? p.capacity : len);
+      lens[b] = len;
+      local += (len + C::TILE - 1) >> C::LOG_TILE;
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(FULL_MASK, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < nwarps ? warp_sums[lane] : 0;
+      int vi = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(FULL_MASK, vi, o);
+        if (lane >= o) vi += y;
+      }
+      warp_sums[lane] = vi - v;  // exclusive warp offsets
+      if (lane == 31) pre[B] = vi;
+    }
+    __syncthreads();
+    int run = warp_sums[warp] + incl - local;
+    for (int b = b0; b < b1; ++b) {
+      pre[b] = run;
+      run += (lens[b] + C::TILE - 1) >> C::LOG_TILE;
+    }
+    __syncthreads();
+  }
+
+  const int items_per_row = p.n_kv_head * p.n_gchunks;
+  const int64_t units = int64_t(items_per_row) * pre[B];
+
+  // ---- zero-length rows: exact zeros (mode 0) or an empty triple (mode 1) -------------
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    if (lens[b] != 0) continue;
+    for (int i = tid; i < p.n_head * D; i += blockDim.x) {
+      const int h = i / D, d = i - h * D;
+      if (p.mode == 0) {
+        T* o = reinterpret_cast<T*>(p.out) + int64_t(b) * p.o_sb + int64_t(h) * p.o_sh + d;
+        *o = E::from_float(0.f);
+      } else {
+        p.part_acc[(int64_t(b) * p.n_head + h) * D + d] = 0.f;
+        if (d == 0) {
+          p.part_m[int64_t(b) * p.n_head + h] = -INFINITY;
+          p.part_l[int64_t(b) * p.n_head + h] = 0.f;
+        }
+      }
+    }
+  }
+  if (units == 0) return;
+
+  // ---- this warp's unit range ----------------------------------------------------------
+  // Never more workers than units: every worker range must be non-empty, because a split
+  // item is merged when all workers overlapping it have arrived.
+  int workers = int(gridDim.x) * nwarps;
+  if (int64_t(workers) > units) workers = int(units);
+  if (p.min_tiles > 1) {
+    const int64_t want = (units + p.min_tiles - 1) / p.min_tiles;
+    if (want < workers) workers = int(want < 1 ? 1 : want);
+  }
+  const int w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
+  if (w >= workers) return;
+  const int64_t u0 = int64_t(w) * units / workers;
+  const int64_t u1 = int64_t(w + 1) * units / workers;
+  if (u0 >= u1) return;
+  const int64_t nunits = u1 - u0;
+
+  uint64_t* my_bars = bars + warp * S;
+  unsigned char* my_stages = stage_base + size_t(warp) * S * C::STAGE_BYTES;
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(smem_addr(my_bars + s), 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  // Locate u0: the last row whose first unit is <= u0 (rows with no tiles are skipped).
+  Cursor cur;
+  {
+    int lo = 0, hi = B;  // find first i with items_per_row * pre[i] > u0
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (int64_t(items_per_row) * pre[mid] > u0) hi = mid; else lo = mid + 1;
+    }
+    cur.b = lo - 1;
+    cur.ntile = pre[cur.b + 1] - pre[cur.b];
+    cur.len = lens[cur.b];
+    const int64_t r = u0 - int64_t(items_per_row) * pre[cur.b];
+    cur.item = int(r / cur.ntile);
+    cur.tile = int(r - int64_t(cur.item) * cur.ntile);
+    cur.h = cur.item / p.n_gchunks;
+    cur.gc = cur.item - cur.h * p.n_gchunks;
+  }
+
+  // ---- producer: block-table window + TMA issue ---------------------------------------
+  const int bs = p.block_size;
+  const int box_tokens = p.box_tokens;
+  const int log2_box = p.log2_box;
+  const int nbox = C::TILE >> log2_box;
+  const uint32_t box_bytes = uint32_t(box_tokens) * C::ROW_BYTES;
+  int win_row = -1, win_base = 0, win_cur = 0, win_nxt = 0;
+
+  auto table_entry = [&](int row, int page, int npages) -> int {
+    if (page < npages && page < p.max_blocks) return __ldg(p.table + int64_t(row) * p.bt_stride + page);
+    return 0;
+  };
+  // Warp-collective: all lanes call with the same (row, page).
+  auto block_of = [&](int row, int page, int npages) -> int {
+    if (row != win_row || page < win_base || page >= win_base + 32) {
+      if (row == win_row && page >= win_base + 32 && page < win_base + 64) {
+        win_cur = win_nxt;
+        win_base += 32;
+      } else {
+        win_row = row;
+        win_base = page & ~31;
+        win_cur = table_entry(row, win_base + lane, npages);
+      }
+      win_nxt = table_entry(row, win_base + 32 + lane, npages);
+    }
+    return __shfl_sync(FULL_MASK, win_cur, page - win_base);
+  };
+
+  auto issue = [&](const Cursor& c, int s) {
+    const int h = c.h;
+    const int tok0 = c.tile << C::LOG_TILE;
+    const int remain = c.len - tok0;  // >= 1
+    const int nvalid = min(nbox, (remain + box_tokens - 1) >> log2_box);
+    const int npages = (c.len + bs - 1) >> p.log2_bs;
+    const uint32_t bar = smem_addr(my_bars + s);
+    const uint32_t kdst = smem_addr(my_stages + size_t(s) * C::STAGE_BYTES);
+    const uint32_t vdst = kdst + C::TILE_BYTES;
+    if (lane == 0) mbar_arrive_expect_tx(bar, 2u * uint32_t(nvalid) * box_bytes);
+    for (int j = 0; j < nvalid; ++j) {
+      const int tok = tok0 + j * box_tokens;
+      const int page = tok >> p.log2_bs;
+      const int off = tok & (bs - 1);
+      const int blk = block_of(c.b, page, npages);
+      if (lane == 0) {
+        tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, h, off, blk);
+        tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, h, off, blk);
+      }
+    }
+  };
+
+  Cursor pc = cur;
+  int64_t issued = 0;
+  {
+    const int64_t first = nunits < S ? nunits : S;
+    for (; issued < first; ++issued) {
+      issue(pc, int(issued));
+      cursor_advance(pc, pre, lens, B, items_per_row, p.n_gchunks);
+    }
+  }
+
+  // ---- consumer state -----------------------------------------------------------------
+  const int rg = lane >> C::LOG_LPR;        // row group of this lane
+  const int pl = lane & (C::LPR - 1);       // position within the row group
+  const int hold_q = pl >> C::AL;           // reduced-score block held by this lane
+  const bool primary = (pl & ((1 << C::AL) - 1)) == 0;
+  // Held score j of this lane is (tile row hold_row[j], q head hold_g[j]): index
+  // j + R * hold_q = (row slot i) * GT + g, row = i * RPL + rg. Lane constants.
+  int hold_row[C::R], hold_g[C::R];
+#pragma unroll
+  for (int j = 0; j < C::R; ++j) {
+    const int idx = j + C::R * hold_q;
+    hold_row[j] = (idx / GT) * C::RPL + rg;
+    hold_g[j] = idx % GT;
+  }
+
+  float qf[GT][C::EPL];
+  float acc[GT][C::EPL];
+  float m_run[GT], l_run[GT];
+  int seg_first_tile = 0;
+  bool first_segment = true;
+
+  // Phase A of a tile: q.K for every (row, q head) of the stage, reduce-scattered so this
+  // lane ends with its R held scores, scaled to log2 units and masked past valid_rows.
+  auto tile_scores = [&](int stage, int valid_rows, float (&sc)[C::R]) {
+    const unsigned char* ks = my_stages + size_t(stage) * C::STAGE_BYTES;
+    float sv[C::NV];
+#pragma unroll
+    for (int i = 0; i < C::NT; ++i) {
+      const int row = i * C::RPL + rg;
+      float kf[C::EPL];
+#pragma unroll
+      for (int c = 0; c < C::CPL; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
+        E::unpack(raw, &kf[c * C::EPC]);
+      }
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < C::EPL; ++e) a = fmaf(qf[g][e], kf[e], a);
+        sv[i * GT + g] = a;
+      }
+    }
+#pragma unroll
+    for (int lv = 0; lv < C::SL; ++lv) {  // butterfly reduce-scatter over the row group
+      const int o = C::LPR >> (lv + 1);
+      const int half = C::NV >> (lv + 1);
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int j = 0; j < half; ++j) {
+        const float send = up ? sv[j] : sv[j + half];
+        const float keep = up ? sv[j + half] : sv[j];
+        sv[j] = keep + __shfl_xor_sync(FULL_MASK, send, o);
+      }
+    }
+#pragma unroll
+    for (int lv = C::SL; lv < C::LOG_LPR; ++lv) sv[0] += __shfl_xor_sync(FULL_MASK, sv[0], C::LPR >> (lv + 1));
+#pragma unroll
+    for (int j = 0; j < C::R; ++j) {
+      const float x = sv[j] * p.scale_log2;
+      sc[j] = hold_row[j] < valid_rows ? x : -INFINITY;
+    }
+  };
+
+  // Phase B, part 1: the online-softmax max update. m' = max(m, tile max) and
+  // alpha = exp2(m - m') is the identity when no score of the tile exceeds the running max,
+  // so the warp max and the rescale run only when one does (same arithmetic as always).
+  auto tile_max_update = [&](const float (&sc)[C::R]) {
+    bool exceeds = false;
+#pragma unroll
+    for (int j = 0; j < C::R; ++j) {
+#pragma unroll
+      for (int g = 0; g < GT; ++g)
+        if (hold_g[j] == g) exceeds |= sc[j] > m_run[g];
+    }
+    if (__builtin_expect(__any_sync(FULL_MASK, exceeds), 0)) {
+      float tmax[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) tmax[g] = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < C::R; ++j) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+          if (hold_g[j] == g) tmax[g] = fmaxf(tmax[g], sc[j]);
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(FULL_MASK, tmax[g], o));
+      }
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        const float mn = fmaxf(m_run[g], tmax[g]);  // finite: the tile has a live row
+        const float alpha = exp2f(m_run[g] - mn);
+        m_run[g] = mn;
+        l_run[g] *= alpha;
+#pragma unroll
+        for (int e = 0; e < C::EPL; ++e) acc[g][e] *= alpha;
+      }
+    }
+  };
+
+  // Phase B, part 2: probabilities, their shuffle to the lanes that own each row's V chunk,
+  // and P.V into the fp32 accumulators. Rows at or past valid_rows contribute exact zeros
+  // (their V is zeroed too, so stale bytes -- even NaN patterns -- never reach acc).
+  auto tile_pv = [&](int stage, const float (&sc)[C::R], int valid_rows, bool full) {
+    float pj[C::R];
+#pragma unroll
+    for (int j = 0; j < C::R; ++j) {
+      float mj = m_run[0];
+#pragma unroll
+      for (int g = 1; g < GT; ++g)
+        if (hold_g[j] == g) mj = m_run[g];
+      pj[j] = exp2f(sc[j] - mj);
+      if (primary) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+          if (hold_g[j] == g) l_run[g] += pj[j];
+      }
+    }
+    const unsigned char* vs = my_stages + size_t(stage) * C::STAGE_BYTES + C::TILE_BYTES;
+#pragma unroll
+    for (int i = 0; i < C::NT; ++i) {
+      const int row = i * C::RPL + rg;
+      float vf[C::EPL];
+#pragma unroll
+      for (int c = 0; c < C::CPL; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
+        E::unpack(raw, &vf[c * C::EPC]);
+      }
+      if (!full) {
+        const bool live = row < valid_rows;
+#pragma unroll
+        for (int e = 0; e < C::EPL; ++e) vf[e] = live ? vf[e] : 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        const int idx = i * GT + g;
+        const int src = (rg << C::LOG_LPR) + ((idx / C::R) << C::AL);
+        const float pv = __shfl_sync(FULL_MASK, pj[idx % C::R], src);
+#pragma unroll
+        for (int e = 0; e < C::EPL; ++e) acc[g][e] = fmaf(pv, vf[e], acc[g][e]);
+      }
+    }
+  };
+
+  auto start_segment = [&](const Cursor& c) {
+    const int hq = c.h * p.group + c.gc * GT;
+    const T* qrow = reinterpret_cast<const T*>(p.q) + int64_t(c.b) * p.q_sb;
+#pragma unroll
+    for (int g = 0; g < GT; ++g) {
+#pragma unroll
+      for (int cc = 0; cc < C::CPL; ++cc) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qrow + int64_t(hq + g) * p.q_sh +
+                                                                 (cc * C::LPR + pl) * C::EPC));
+        E::unpack(raw, &qf[g][cc * C::EPC]);
+      }
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.f;
+#pragma unroll
+      for (int e = 0; e < C::EPL; ++e) acc[g][e] = 0.f;
+    }
+  };
+
+  auto fail_and_drain = [&](int64_t from) {
+    if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
+    for (int64_t j = from; j < issued; ++j)
+      warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), DRAIN_LIMIT_NS);
+  };
+
+  // ---- pipelined tile loop: scores of tile k+1 overlap softmax + P.V of tile k ---------
+  int s = 0;              // stage of tile k (= k % S)
+  uint32_t parity = 0u;   // mbarrier phase parity of tile k (= (k / S) & 1)
+  float sc_cur[C::R], sc_nxt[C::R];
+  if (!warp_wait_phase(smem_addr(my_bars), 0u, WAIT_LIMIT_NS)) {
+    fail_and_drain(0);
+    return;
+  }
+  start_segment(cur);
+  seg_first_tile = cur.tile;
+  tile_scores(0, cur.len - (cur.tile << C::LOG_TILE), sc_cur);
+
+  for (int64_t k = 0; k < nunits; ++k) {
+    const bool has_next = k + 1 < nunits;
+    Cursor nxt = cur;
+    cursor_advance(nxt, pre, lens, B, items_per_row, p.n_gchunks);
+    const int s_n = s + 1 == S ? 0 : s + 1;
+    const uint32_t parity_n = s + 1 == S ? parity ^ 1u : parity;
+    if (has_next && !warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
+      fail_and_drain(k + 1);
+      return;
+    }
+    const int tok0 = cur.tile << C::LOG_TILE;
+    const int valid_rows = cur.len - tok0;  // rows [0, valid_rows) of tile k are live
+    const bool full_tile = valid_rows >= C::TILE;
+    const int hq0 = cur.h * p.group + cur.gc * GT;  // first q head of this item
+
+    tile_max_update(sc_cur);
+    // Straight-line region: phase A of tile k+1 (when it exists; its stage is not being
+    // written otherwise) and phase B of tile k are independent chains.
+    tile_scores(s_n, nxt.len - (nxt.tile << C::LOG_TILE), sc_nxt);
+    if (__builtin_expect(full_tile, 1)) {
+      tile_pv(s, sc_cur, valid_rows, true);
+    } else {
+      tile_pv(s, sc_cur, valid_rows, false);
+    }
+    __syncwarp();
+
+    // Refill the stage just consumed with the tile `stages` ahead.
+    if (issued < nunits) {
+      issue(pc, s);
+      cursor_advance(pc, pre, lens, B, items_per_row, p.n_gchunks);
+      ++issued;
+    }
+
+    // ---- segment end ---------------------------------------------------------------------
+    const bool seg_end = (k == nunits - 1) || (cur.tile == cur.ntile - 1);
+    if (__builtin_expect(seg_end, 0)) {
+      float l_tot[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        float x = l_run[g];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(FULL_MASK, x, o);
+        l_tot[g] = x;
+      }
+#pragma unroll
+      for (int o = C::LPR; o < 32; o <<= 1) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+#pragma unroll
+          for (int e = 0; e < C::EPL; ++e) acc[g][e] += __shfl_xor_sync(FULL_MASK, acc[g][e], o);
+        }
+      }
+      const bool whole = seg_first_tile == 0 && cur.tile == cur.ntile - 1;
+      if (whole) {
+        if (p.mode == 0) {
+          if (rg == 0) {
+            T* orow = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb;
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+              const float inv = 1.f / fmaxf(l_tot[g], 1.f);
+#pragma unroll
+              for (int c = 0; c < C::CPL; ++c) {
+                float o[C::EPC];
+#pragma unroll
+                for (int e = 0; e < C::EPC; ++e) o[e] = acc[g][c * C::EPC + e] * inv;
+                *reinterpret_cast<uint4*>(orow + int64_t(hq0 + g) * p.o_sh + (c * C::LPR + pl) * C::EPC) =
+                    E::pack(o);
+              }
+            }
+          }
+        } else {
+          const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
+          if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+              p.part_m[hrow + g] = m_run[g];
+              p.part_l[hrow + g] = l_tot[g];
+            }
+          }
+          if (rg == 0) {
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+#pragma unroll
+              for (int c = 0; c < C::CPL; ++c) {
+                float* dst = p.part_acc + (hrow + g) * D + (c * C::LPR + pl) * C::EPC;
+#pragma unroll
+                for (int e = 0; e < C::EPC; e += 4)
+                  *reinterpret_cast<float4*>(dst + e) =
+                      make_float4(acc[g][c * C::EPC + e], acc[g][c * C::EPC + e + 1],
+                                  acc[g][c * C::EPC + e + 2], acc[g][c * C::EPC + e + 3]);
+              }
+            }
+          }
+        }
+      } else {
+        // Split item: park (m, l, acc) in this worker's slot, then the last arrival merges.
+        const int64_t slot = int64_t(w) * 2 + (first_segment ? 0 : 1);
+        float* ml = p.ws_ml + slot * (2 * GT);
+        float* wa = p.ws_acc + slot * (GT * D);
+        if (lane == 0) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            ml[g] = m_run[g];
+            ml[GT + g] = l_tot[g];
+          }
+        }
+        if (rg == 0) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+#pragma unroll
+            for (int c = 0; c < C::CPL; ++c) {
+              float* dst = wa + g * D + (c * C::LPR + pl) * C::EPC;
+#pragma unroll
+              for (int e = 0; e < C::EPC; e += 4)
+                *reinterpret_cast<float4*>(dst + e) =
+                    make_float4(acc[g][c * C::EPC + e], acc[g][c * C::EPC + e + 1],
+                                acc[g][c * C::EPC + e + 2], acc[g][c * C::EPC + e + 3]);
+            }
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        const int64_t item_global = int64_t(cur.b) * items_per_row + cur.item;
+        const int64_t us = int64_t(items_per_row) * pre[cur.b] + int64_t(cur.item) * cur.ntile;
+        const int64_t ue = us + cur.ntile;
+        const int c_first = worker_of(us, units, workers);
+        const int c_last = worker_of(ue - 1, units, workers);
+        int ticket = 0;
+        if (lane == 0) ticket = atomicAdd(p.counters + item_global, 1);
+        ticket = __shfl_sync(FULL_MASK, ticket, 0);
+        if (ticket == c_last - c_first) {
+          __threadfence();
+          // Merge the (c_last - c_first + 1) pieces of this item.
+          const int64_t first_start = int64_t(c_first) * units / workers;
+          const int64_t first_slot = int64_t(c_first) * 2 + (first_start == us ? 0 : 1);
+          auto slot_of = [&](int c) -> int64_t { return c == c_first ? first_slot : int64_t(c) * 2; };
+          float M[GT];
+#pragma unroll
+          for (int g = 0; g < GT; ++g) M[g] = -INFINITY;
+          for (int c = c_first + lane; c <= c_last; c += 32) {
+            const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
+#pragma unroll
+            for (int g = 0; g < GT; ++g) M[g] = fmaxf(M[g], __ldcg(sm + g));
+          }
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int g = 0; g < GT; ++g) M[g] = fmaxf(M[g], __shfl_xor_sync(FULL_MASK, M[g], o));
+          }
+          float Lsum[GT];
+#pragma unroll
+          for (int g = 0; g < GT; ++g) Lsum[g] = 0.f;
+          for (int c = c_first + lane; c <= c_last; c += 32) {
+            const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
+#pragma unroll
+            for (int g = 0; g < GT; ++g) Lsum[g] += __ldcg(sm + GT + g) * exp2f(__ldcg(sm + g) - M[g]);
+          }
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int g = 0; g < GT; ++g) Lsum[g] += __shfl_xor_sync(FULL_MASK, Lsum[g], o);
+          }
+          const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
+          for (int q4 = lane; q4 < GT * (D / 4); q4 += 32) {
+            const int g = q4 / (D / 4);
+            const int d = (q4 - g * (D / 4)) * 4;
+            float Mg = M[0], Lg = Lsum[0];
+#pragma unroll
+            for (int gg = 1; gg < GT; ++gg)
+              if (g == gg) { Mg = M[gg]; Lg = Lsum[gg]; }
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = c_first; c <= c_last; ++c) {
+              const int64_t sl = slot_of(c);
+              const float f = exp2f(__ldcg(p.ws_ml + sl * (2 * GT) + g) - Mg);
+              const float4 x = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D) + g * D + d));
+              a.x = fmaf(f, x.x, a.x);
+              a.y = fmaf(f, x.y, a.y);
+              a.z = fmaf(f, x.z, a.z);
+              a.w = fmaf(f, x.w, a.w);
+            }
+            if (p.mode == 0) {
+              const float inv = 1.f / fmaxf(Lg, 1.f);
+              T* o = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb + int64_t(hq0 + g) * p.o_sh + d;
+              o[0] = E::from_float(a.x * inv);
+              o[1] = E::from_float(a.y * inv);
+              o[2] = E::from_float(a.z * inv);
+              o[3] = E::from_float(a.w * inv);
+            } else {
+              *reinterpret_cast<float4*>(p.part_acc + (hrow + g) * D + d) = a;
+              if (d == 0) {
+                p.part_m[hrow + g] = Mg;
+                p.part_l[hrow + g] = Lg;
+              }
+            }
+          }
+          if (lane == 0) p.counters[item_global] = 0;  // ready for the next launch
+        }
+      }
+      first_segment = false;
+    }
+    if (has_next && __builtin_expect(nxt.tile == 0, 0)) {
+      // Tile k+1 opens a new item: its scores above used the old q. Reload and redo.
+      start_segment(nxt);
+      seg_first_tile = 0;
+      tile_scores(s_n, nxt.len, sc_nxt);
+    }
+#pragma unroll
+    for (int j = 0; j < C::R; ++j) sc_cur[j] = sc_nxt[j];
+    cur = nxt;
+    s = s_n;
+    parity = parity_n;
+  }
+}
+
+template <typename T, int D, int GT>
+cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                          dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
+  auto fn = pd_decode_kernel<T, D, GT>;
+  static int attr_smem[64] = {0};  // per-device dynamic-smem opt-in already granted
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 64 && attr_smem[dev] < int(smem)) {
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    attr_smem[dev] = int(smem);
+  }
+  fn<<<grid, block, smem, stream>>>(p, kmap, vmap);
+  return cudaGetLastError();
+}
+
+}  // namespace pd

@@ -1,0 +1,19 @@
+// pd_internal.h -- host-side declarations shared by the translation units of the library.
+#pragma once
+
+#include "pd_common.cuh"
+
+namespace pd {
+
+DecodeLaunchFn decode_launcher_f32(int d_index, int gt_index);
+DecodeLaunchFn decode_launcher_f16(int d_index, int gt_index);
+DecodeLaunchFn decode_launcher_bf16(int d_index, int gt_index);
+
+// Append: copies K and V rows into their pool slots. src/dst dtype codes as PD_F32/F16/BF16.
+cudaError_t launch_append(const AppendParams& p, int src_dtype, int dst_dtype, bool vec16,
+                          cudaStream_t stream);
+
+// Log-sum-exp merge of n_parts (m, l, acc) triples into the normalised output.
+cudaError_t launch_merge(const MergeParams& p, int dtype, cudaStream_t stream);
+
+}  // namespace pd

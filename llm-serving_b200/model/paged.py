@@ -1,0 +1,392 @@
+"""Paged KV storage and the decode container, written over the sm_100a append/decode kernels.
+
+Drop-in for the reference's ``model/paged.py`` (``PagedPool`` 82-306, ``PagedKV`` 309-586):
+same constructor arguments, attributes, step protocol and error messages, so the engine,
+scheduler and model layers call it unchanged. What changed is underneath:
+
+* ``PagedPool.write_slots`` (prefill and decode writes) is one launch of the append kernel
+  (``pd_kv_append_slots``) that moves K and V together, instead of two ``index_copy_``.
+* ``PagedKV.write`` is one launch of the fused append (``pd_kv_append_table``): the kernel
+  derives each row's slot ``table[row, pos // bs] * bs + pos % bs`` itself from the int32
+  block table and the int64 ``pos`` vector, so no device slot map is built per step.
+* ``PagedKV.attend`` launches the decode plan of :mod:`model.triton_decode`.
+
+Layout (unchanged): one ``(n_blocks, block_size, n_kv_head, head_dim)`` K and V tensor per
+layer, allocated once and never replaced; token ``t`` of a request lives at block
+``block_table[t // block_size]``, slot ``t % block_size``; every layer shares the block table.
+
+Step order the model relies on (reference ``model/paged.py:37-46``)::
+
+    paged.build_mask(next_token=True)   # seqlen := pos + 1 (int32, in place)
+    for layer in layers:
+        paged.write(layer, k, v)        # this step's token at pos[row]
+        y = paged.attend(layer, q)      # block-table decode
+    paged.advance()                     # pos += active
+
+A pool may be created on the CPU (its host-side checks work there), but every write and the
+decode container need CUDA: there is no CPU kernel path and no fallback. The CPU oracle used
+by the tests lives in ``oracle/``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from model import _native
+from model.triton_decode import TRITON_AVAILABLE
+
+__all__ = ["PagedPool", "PagedKV"]
+
+
+def _positive(name: str, value) -> int:
+    if isinstance(value, bool) or not isinstance(value, int) or value < 1:
+        raise ValueError(f"{name} must be a positive int, got {value!r}")
+    return value
+
+
+def _same_device(a: torch.device, b: torch.device) -> bool:
+    """``cuda`` (current device) and ``cuda:N`` name the same device unless both are explicit."""
+    return a.type == b.type and (a.index is None or b.index is None or a.index == b.index)
+
+
+def _unit_last_stride(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+class PagedPool:
+    """Physical KV blocks: one ``(n_blocks, block_size, n_kv_head, head_dim)`` K and V per layer."""
+
+    def __init__(self, n_layer: int, n_blocks: int, block_size: int, n_kv_head: int, head_dim: int,
+                 *, dtype: torch.dtype = torch.float32, device="cpu", n_head: int | None = None):
+        self.n_layer = _positive("n_layer", n_layer)
+        self.n_blocks = _positive("n_blocks", n_blocks)
+        self.block_size = _positive("block_size", block_size)
+        self.n_kv_head = _positive("n_kv_head", n_kv_head)
+        self.head_dim = _positive("head_dim", head_dim)
+        n_head = self.n_kv_head if n_head is None else int(n_head)
+        if n_head % self.n_kv_head != 0:
+            raise ValueError(f"n_head ({n_head}) must be a multiple of n_kv_head ({self.n_kv_head})")
+        self.n_head = n_head
+        self.n_group = n_head // self.n_kv_head
+        self.dtype = dtype
+        self.device = torch.device(device)
+        shape = (self.n_blocks, self.block_size, self.n_kv_head, self.head_dim)
+        self.keys = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
+        self.values = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
+        # Flat (n_blocks * block_size, n_kv_head, head_dim) views: a slot id is a row of these.
+        self._keys_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self.keys]
+        self._values_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self.values]
+        # One-entry cache of the prefill slot map keyed by (table, start, length).
+        self._prefill_key: tuple | None = None
+        self._prefill_slots: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------ checks
+    def _check_layer(self, layer: int) -> int:
+        if not 0 <= int(layer) < self.n_layer:
+            raise IndexError(f"layer {layer} outside the pool's {self.n_layer} layers")
+        return int(layer)
+
+    def _check_block_ids(self, block_ids, needed: int) -> None:
+        for block_id in block_ids:
+            if isinstance(block_id, bool) or not isinstance(block_id, int):
+                raise ValueError(f"block ids must be ints, got {block_id!r}")
+            if not 0 <= block_id < self.n_blocks:
+                raise IndexError(f"block id {block_id} outside the pool's {self.n_blocks} blocks")
+        if len(block_ids) < needed:
+            raise IndexError(f"block table has {len(block_ids)} blocks, needs {needed} to address this write")
+
+    def _check_rows(self, what: str, k: torch.Tensor, v: torch.Tensor) -> None:
+        if k.dim() != 3 or v.dim() != 3:
+            raise ValueError(f"{what} needs (length, n_kv_head, head_dim), got {tuple(k.shape)} / {tuple(v.shape)}")
+        if tuple(k.shape) != tuple(v.shape):
+            raise ValueError(f"k/v shapes differ: {tuple(k.shape)} vs {tuple(v.shape)}")
+        if k.shape[1:] != (self.n_kv_head, self.head_dim):
+            raise ValueError(
+                f"{what} needs head shape {(self.n_kv_head, self.head_dim)}, got {tuple(k.shape[1:])}"
+            )
+
+    def _require_cuda(self, what: str) -> None:
+        if self.device.type != "cuda":
+            raise RuntimeError(
+                f"PagedPool.{what} requires a CUDA pool (this one is on {self.device}): the paged "
+                "append is the sm_100a kernel and has no CPU path"
+            )
+        if not TRITON_AVAILABLE:
+            raise RuntimeError(f"PagedPool.{what} requires the sm_100a library: {_native.LOAD_ERROR}")
+
+    # ------------------------------------------------------------------ slot maps
+    def _slot_ids(self, block_table, start: int, length: int) -> torch.Tensor:
+        """``(length,)`` flat slots of logical tokens ``[start, start + length)``, cached."""
+        key = (tuple(block_table), start, length)
+        if key == self._prefill_key and self._prefill_slots is not None:
+            return self._prefill_slots
+        bs = self.block_size
+        slots = [block_table[t // bs] * bs + t % bs for t in range(start, start + length)]
+        tensor = torch.tensor(slots, dtype=torch.long, device=self.device)
+        self._prefill_key = key
+        self._prefill_slots = tensor
+        return tensor
+
+    def slot_ids(self, block_table, start: int, length: int) -> torch.Tensor:
+        """Public slot-map builder for a caller that writes the same map to every layer."""
+        start, length = int(start), int(length)
+        if start < 0:
+            raise ValueError(f"start must be >= 0, got {start}")
+        if length < 0:
+            raise ValueError(f"length must be >= 0, got {length}")
+        self._check_block_ids(block_table, (start + length + self.block_size - 1) // self.block_size)
+        return self._slot_ids(block_table, start, length)
+
+    # ------------------------------------------------------------------ writes
+    def write_slots(self, layer: int, slot_ids: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Copy token ``i`` of k/v ``(n, n_kv_head, head_dim)`` into flat pool row ``slot_ids[i]``.
+
+        One append-kernel launch for K and V together (the reference issues two
+        ``index_copy_``). Slots must be distinct and inside the pool, as in the reference; the
+        kernel skips one outside the pool and records it in the device error word instead of
+        faulting. No host-side scan of the slots (that would be a sync per layer).
+        """
+        layer = self._check_layer(layer)
+        self._check_rows("write_slots", k, v)
+        if slot_ids.dim() != 1 or slot_ids.numel() != k.shape[0]:
+            raise ValueError(
+                f"slot_ids must be 1-D with one entry per token ({k.shape[0]}), got {tuple(slot_ids.shape)}"
+            )
+        if slot_ids.dtype not in (torch.int32, torch.int64):
+            raise ValueError(f"slot_ids must be an integer tensor, got {slot_ids.dtype}")
+        if not _same_device(slot_ids.device, self.device):
+            raise ValueError(f"slot_ids on {slot_ids.device} but the pool is on {self.device}")
+        self._require_cuda("write_slots")
+        for name, t in (("k", k), ("v", v)):
+            if not _same_device(t.device, self.device):
+                raise ValueError(f"{name} on {t.device} but the pool is on {self.device}")
+            if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+                raise ValueError(f"{name} dtype must be fp32, fp16 or bf16, got {t.dtype}")
+        if k.shape[0] == 0:
+            return
+        with torch.cuda.device(self.keys[layer].device):
+            _native.append_slots(self.keys[layer], self.values[layer], slot_ids.contiguous(),
+                                 _unit_last_stride(k), _unit_last_stride(v.to(k.dtype)))
+
+    def write_prefill_slots(self, layer: int, slot_ids: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Named prefill entry point (``PagedWriteSink``): :meth:`write_slots` with a prebuilt map."""
+        self.write_slots(layer, slot_ids, k, v)
+
+    def write_prefill(self, layer: int, block_table, start: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Write logical tokens ``[start, start + len(k))`` of one request through its table."""
+        layer = self._check_layer(layer)
+        self._check_rows("write_prefill", k, v)
+        start = int(start)
+        if start < 0:
+            raise ValueError(f"start must be >= 0, got {start}")
+        length = k.shape[0]
+        if length == 0:
+            return
+        self._check_block_ids(block_table, (start + length + self.block_size - 1) // self.block_size)
+        self.write_prefill_slots(layer, self._slot_ids(block_table, start, length), k, v)
+
+    # ------------------------------------------------------------------ accounting
+    def bytes(self) -> int:
+        """Physical KV bytes of the pool (K + V, all layers)."""
+        return 2 * self.n_layer * self.n_blocks * self.block_size * self.n_kv_head * self.head_dim * self.dtype.itemsize
+
+    def mb(self) -> float:
+        return self.bytes() / 2**20
+
+
+class PagedKV:
+    """Decode-time container over a :class:`PagedPool` (the ``KvSlab`` step protocol).
+
+    Rows are the active requests; ``seats[row]`` is the engine seat. ``pos``/``valid``/
+    ``active`` are device tensors updated in place with Python mirrors; ``max_len`` is the
+    run's position bound (the RoPE table length). The padded int32 block table is built once
+    per container and never mutated; the int32 ``seqlen`` is refreshed in place by
+    :meth:`build_mask` and read by the decode plan by reference.
+    """
+
+    decode_container = True
+    block_table_decode = True
+
+    def __init__(self, pool: PagedPool, block_tables, lengths, *, rope_len: int, seats=None,
+                 n_head: int | None = None, check_bounds: bool = True) -> None:
+        if not isinstance(pool, PagedPool):
+            raise TypeError(f"PagedKV needs a PagedPool, got {type(pool).__name__}")
+        if pool.device.type != "cuda":
+            raise ValueError(
+                "paged decode is the sm_100a CUDA block-table kernel; the gather control arm was "
+                f"deleted. The pool is on {pool.device}. Run the paged arm on CUDA, or use the seat "
+                "arm on CPU. The dense numeric oracle lives in oracle/."
+            )
+        if not TRITON_AVAILABLE:
+            raise RuntimeError(
+                "paged decode requires the sm_100a library that replaces the Triton kernel, but it "
+                f"could not be loaded ({_native.LOAD_ERROR}); there is no eager fallback."
+            )
+        n_rows = len(block_tables)
+        if n_rows < 1:
+            raise ValueError("PagedKV needs at least one row")
+        if len(lengths) != n_rows:
+            raise ValueError(f"PagedKV needs one length per block table, got {len(lengths)} for {n_rows}")
+        rope_len = int(rope_len)
+        if rope_len < 1:
+            raise ValueError(f"rope_len (the run's position bound) must be >= 1, got {rope_len}")
+
+        self.pool = pool
+        self.n_layer = pool.n_layer
+        self.n_kv_head = pool.n_kv_head
+        self.head_dim = pool.head_dim
+        self.n_head = pool.n_kv_head if n_head is None else int(n_head)
+        if self.n_head % self.n_kv_head != 0:
+            raise ValueError(f"n_head ({self.n_head}) must be a multiple of n_kv_head ({self.n_kv_head})")
+        self.n_group = self.n_head // self.n_kv_head
+        self.dtype = pool.dtype
+        self.device = pool.device
+        self.check_bounds = bool(check_bounds)
+        self.block_tables = [list(bt) for bt in block_tables]
+        self.seats = list(range(n_rows)) if seats is None else list(seats)
+        if len(self.seats) != n_rows:
+            raise ValueError(f"PagedKV needs one seat per row, got {len(self.seats)} for {n_rows}")
+        self.row_of_seat = {seat: row for row, seat in enumerate(self.seats)}
+        self.batch = n_rows
+        self.max_len = rope_len
+
+        lengths = [int(n) for n in lengths]
+        for row, (table, length) in enumerate(zip(self.block_tables, lengths)):
+            if length < 0:
+                raise ValueError(f"row {row}: length must be >= 0, got {length}")
+            if length > len(table) * pool.block_size:
+                raise IndexError(
+                    f"row {row}: length {length} exceeds its block table's capacity "
+                    f"({len(table)} blocks x {pool.block_size})"
+                )
+            if length > rope_len:
+                raise IndexError(f"row {row}: length {length} exceeds the run's position bound {rope_len}")
+
+        self.pos = torch.tensor(lengths, dtype=torch.long, device=self.device)
+        self.valid = torch.tensor(lengths, dtype=torch.long, device=self.device)
+        self.active = torch.ones(n_rows, dtype=torch.bool, device=self.device)
+        self._host_pos = list(lengths)
+        self._host_valid = list(lengths)
+        self._host_active = [True] * n_rows
+
+        width = max((len(t) for t in self.block_tables), default=1) or 1
+        host_table = torch.zeros((n_rows, width), dtype=torch.int32)
+        for row, table in enumerate(self.block_tables):
+            if not table:
+                continue
+            pool._check_block_ids(table, (max(lengths[row], 1) + pool.block_size - 1) // pool.block_size)
+            host_table[row, : len(table)] = torch.tensor(table, dtype=torch.int32)
+        self._block_table_tensor = host_table.to(self.device)
+        self._seqlen = torch.zeros(n_rows, dtype=torch.int32, device=self.device)
+        self._slot_error: tuple[int, int, int, int] | None = None
+        self._slot_cache: torch.Tensor | None = None
+        self._refresh_slots()
+        self._decode_plan = None
+        self._step_written = False
+        self._seqlen_ready = False
+
+    # ---------------------------------------------------------------- step hooks
+    def build_mask(self, *, next_token: bool = False) -> None:
+        """Step boundary: ``seqlen := pos + next_token`` as int32, in place (no mask/bias)."""
+        longest = max(n + int(next_token) for n in self._host_valid)
+        if self.check_bounds and longest > self.max_len:
+            raise IndexError(f"PagedKV overflow: needs {longest} positions, run position bound is {self.max_len}")
+        self._seqlen.copy_((self.pos + int(next_token)).to(torch.int32))
+        self._step_written = False
+        self._seqlen_ready = True
+        return None
+
+    def _refresh_slots(self) -> None:
+        """Host bound check of the next write position of every row (no device work).
+
+        A row whose position needs a block beyond its table parks the container in an error
+        state that :meth:`write` reports; the fused append computes the slots on device.
+        """
+        bs = self.pool.block_size
+        self._slot_error = None
+        self._slot_cache = None
+        for row, position in enumerate(self._host_pos):
+            block_index = position // bs
+            if block_index >= len(self.block_tables[row]):
+                self._slot_error = (row, position, block_index, len(self.block_tables[row]))
+                break
+
+    @property
+    def _slot_ids(self) -> torch.Tensor | None:
+        """Flat slot each row writes next (``None`` past a row's table); built on demand."""
+        if self._slot_error is not None:
+            return None
+        if self._slot_cache is None:
+            bs = self.pool.block_size
+            blocks = self._block_table_tensor.to(torch.int64).gather(1, (self.pos // bs).view(-1, 1)).squeeze(1)
+            self._slot_cache = blocks * bs + self.pos % bs
+        return self._slot_cache
+
+    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Append this step's token of every row at its own position (one fused launch)."""
+        expected = (self.batch, self.n_kv_head, 1, self.head_dim)
+        if tuple(k.shape) != expected or tuple(v.shape) != expected:
+            raise ValueError(f"write needs {expected}, got {tuple(k.shape)} / {tuple(v.shape)}")
+        layer = self.pool._check_layer(layer)
+        if self.check_bounds and max(self._host_pos) >= self.max_len:
+            raise IndexError(f"PagedKV overflow: write position {max(self._host_pos)} >= max_len {self.max_len}")
+        if self._slot_error is not None:
+            row, position, block_index, have = self._slot_error
+            raise IndexError(
+                f"row {row}: position {position} needs block {block_index}, but its block table has {have} blocks"
+            )
+        for name, t in (("k", k), ("v", v)):
+            if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+                raise ValueError(f"{name} dtype must be fp32, fp16 or bf16, got {t.dtype}")
+            if not _same_device(t.device, self.device):
+                raise ValueError(f"{name} on {t.device} but the pool is on {self.device}")
+        with torch.cuda.device(self.pool.keys[layer].device):
+            _native.append_table(self.pool.keys[layer], self.pool.values[layer], self._block_table_tensor,
+                                 self.pos, _unit_last_stride(k[:, :, 0, :]),
+                                 _unit_last_stride(v[:, :, 0, :].to(k.dtype)))
+        self._step_written = True
+
+    def attend(self, layer: int, q: torch.Tensor, *, dropout_p: float = 0.0) -> torch.Tensor:
+        """Block-table decode for one layer; ``q`` is ``(B, H, 1, D)``, output the same."""
+        if not self._seqlen_ready:
+            raise RuntimeError("PagedKV.attend() before build_mask(): seqlen is stale")
+        if not self._step_written:
+            raise RuntimeError("PagedKV.attend() before write(): this step has no token yet")
+        if dropout_p:
+            raise ValueError("paged decode is inference-only; dropout_p must be 0")
+        expected = (self.batch, self.n_head, 1, self.head_dim)
+        if tuple(q.shape) != expected:
+            raise ValueError(f"attend needs q {expected}, got {tuple(q.shape)}")
+        from model.triton_decode import paged_decode_plan
+
+        q3 = q[:, :, 0, :].contiguous()
+        if self._decode_plan is None:
+            self._decode_plan = paged_decode_plan(
+                q3, self.pool.keys, self.pool.values, self._block_table_tensor, self._seqlen,
+                scale=1.0 / (self.head_dim ** 0.5),
+            )
+        return self._decode_plan.run(layer, q3).unsqueeze(2)
+
+    def advance(self) -> None:
+        """Move every active row's cursor one token (device in place, then host mirrors)."""
+        self.pos.add_(self.active)
+        self.valid.copy_(torch.maximum(self.valid, self.pos))
+        for row in range(self.batch):
+            if self._host_active[row]:
+                self._host_pos[row] += 1
+                self._host_valid[row] = max(self._host_valid[row], self._host_pos[row])
+        self._step_written = False
+        self._seqlen_ready = False
+        if self.check_bounds and max(self._host_pos) > self.max_len:
+            raise IndexError(f"PagedKV overflow: max_len={self.max_len}; a request decoded past its budget")
+        self._refresh_slots()
+
+    # ---------------------------------------------------------------- helpers
+    def past_len(self) -> int:
+        return max(self._host_valid) if self._host_valid else 0
+
+    def bytes(self) -> int:
+        return self.pool.bytes()
+
+    def mb(self) -> float:
+        return self.bytes() / 2**20

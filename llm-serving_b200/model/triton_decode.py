@@ -1,0 +1,326 @@
+"""Block-table decode on B200: the drop-in for the reference's ``model/triton_decode.py``.
+
+The module keeps the reference's public surface so ``PagedKV.attend``, the engines and the
+tests call it unchanged (reference: ``model/triton_decode.py:250-538``):
+
+* ``paged_decode(q, k_cache, v_cache, block_table, seqlen, *, scale=None)`` -- validating
+  one-shot entry point;
+* ``paged_decode_plan(...)`` / ``PagedDecodePlan.run(layer, q)`` -- validate a container's
+  pools once, then one launch per layer;
+* ``TRITON_AVAILABLE`` -- kept under the reference's name for its callers; here it means
+  "the sm_100a paged-decode library is loaded".
+
+Contract (identical to the reference): ``q`` is ``(B, H, D)`` (copied if non-contiguous);
+``k_cache``/``v_cache`` are ``(n_blocks, block_size, H_kv, D)`` with the q dtype (fp16, bf16
+or fp32); ``block_table`` is int32 ``(B, max_blocks)`` on the same CUDA device and only its
+first ``ceil(seqlen[b] / block_size)`` entries of row ``b`` are read; ``seqlen`` is ``(B,)``
+int32 (int64 is cast) with values in ``[0, max_blocks * block_size]``; the output is
+``(B, H, D)`` in ``q.dtype``; ``scale=None`` means ``1 / sqrt(D)``. There is no CPU path and
+no fallback: without the library or CUDA every entry point raises ``RuntimeError``.
+
+What runs underneath is the C ABI of ``include/paged_decode.h`` (``pd_decode`` and
+``pd_plan_*``): a TMA-fed, warp-pipelined sm_100a kernel that balances KV pages over every SM
+and merges split rows in the same launch. Differences from the reference that a caller can
+observe: ``head_dim`` must be in 8..256 (a power of two, as before); pool strides must be
+16-byte multiples with a unit ``head_dim`` stride -- ``paged_decode`` copies a pool that is
+not, ``paged_decode_plan`` refuses it; and a table entry outside the pool reads zeros
+instead of faulting.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from model import _native
+
+TRITON_AVAILABLE: bool = _native.AVAILABLE
+
+__all__ = ["TRITON_AVAILABLE", "paged_decode", "paged_decode_plan", "PagedDecodePlan"]
+
+_LOG2E = 1.4426950408889634
+_MIN_HEAD_DIM = 8
+_MAX_HEAD_DIM = 256
+
+#: Last successful seqlen range check: ``(seqlen, version, capacity)``. Holding the tensor
+#: keeps its storage alive, so the identity test cannot alias a freed tensor. The check is
+#: the one host synchronisation of the wrapper; a persistent seqlen pays it once per version.
+_SEQ_CHECK: tuple[torch.Tensor, int, int] | None = None
+
+#: Per (device, stream) decode workspace for ``paged_decode``: zero-initialised once, left
+#: zero by every launch, never shared by two streams.
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _require_backend() -> None:
+    """No library or no CUDA is an environment problem: RuntimeError, never a fallback."""
+    if not TRITON_AVAILABLE:
+        raise RuntimeError(
+            "paged_decode requires the sm_100a CUDA library that replaces the Triton kernel, "
+            f"but it could not be loaded ({_native.LOAD_ERROR}); the paged decode arm has no "
+            "eager fallback. The dense oracle lives in oracle/ and tests/."
+        )
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            "paged_decode requires CUDA, but torch.cuda is unavailable; the paged decode arm "
+            "has no CPU fallback. The dense oracle lives in oracle/ and tests/."
+        )
+
+
+def _require_cuda_tensors(tensors) -> None:
+    for name, tensor in tensors:
+        if not tensor.is_cuda:
+            raise RuntimeError(
+                f"paged_decode requires CUDA tensors, got {name} on device {tensor.device}; "
+                "there is no silent fallback to a dense implementation."
+            )
+
+
+def _validate(q, k_cache, v_cache, block_table, seqlen) -> None:
+    """The reference's layout contract: structural errors are ValueError."""
+    if q.dim() != 3:
+        raise ValueError(f"q must be (B, H, D), got shape {tuple(q.shape)}")
+    if k_cache.dim() != 4 or v_cache.dim() != 4:
+        raise ValueError(
+            "k_cache/v_cache must be (n_blocks, block_size, H_kv, D), got "
+            f"{tuple(k_cache.shape)} / {tuple(v_cache.shape)}"
+        )
+    if tuple(k_cache.shape) != tuple(v_cache.shape):
+        raise ValueError(
+            f"k_cache/v_cache shapes differ: {tuple(k_cache.shape)} vs {tuple(v_cache.shape)}"
+        )
+    if q.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise ValueError(f"q dtype must be fp16, bf16 or fp32, got {q.dtype}")
+    if not (k_cache.dtype == v_cache.dtype == q.dtype):
+        raise ValueError(
+            f"q/k_cache/v_cache must share one dtype, got {q.dtype}, {k_cache.dtype}, {v_cache.dtype}"
+        )
+    B, H, D = q.shape
+    _, block_size, H_kv, cache_d = k_cache.shape
+    if D < 1:
+        raise ValueError(f"head_dim must be positive, got {D}")
+    if D != cache_d:
+        raise ValueError(f"q head_dim {D} != cache head_dim {cache_d}")
+    if H_kv < 1 or H % H_kv != 0:
+        raise ValueError(f"n_head ({H}) must be a multiple of n_kv_head ({H_kv})")
+    if block_size < 1:
+        raise ValueError(f"block_size must be positive, got {block_size}")
+    if block_size & (block_size - 1):
+        raise ValueError(
+            f"block_size must be a power of two (16 and 32 are the supported sizes), got {block_size}"
+        )
+    if D & (D - 1):
+        raise ValueError(f"head_dim must be a power of two for the kernel, got {D}")
+    if not _MIN_HEAD_DIM <= D <= _MAX_HEAD_DIM:
+        raise ValueError(
+            f"head_dim {D} is outside the sm_100a kernel's range {_MIN_HEAD_DIM}..{_MAX_HEAD_DIM}"
+        )
+    if block_table.dim() != 2:
+        raise ValueError(f"block_table must be (B, max_blocks), got shape {tuple(block_table.shape)}")
+    B_bt, max_blocks = block_table.shape
+    if B_bt != B:
+        raise ValueError(f"block_table batch {B_bt} does not match q batch {B}")
+    if block_table.dtype != torch.int32:
+        raise ValueError(
+            "paged_decode requires an int32 block_table (the kernel's indexing contract); "
+            f"got {block_table.dtype}. Cast at the allocator boundary, not per step."
+        )
+    if seqlen.dim() != 1:
+        raise ValueError(f"seqlen must be (B,), got shape {tuple(seqlen.shape)}")
+    if seqlen.shape[0] != B:
+        raise ValueError(f"seqlen has {seqlen.shape[0]} entries for a batch of {B}")
+    if seqlen.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"seqlen must be int32 or int64, got {seqlen.dtype}")
+    device = q.device
+    for name, tensor in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
+                         ("block_table", block_table), ("seqlen", seqlen)):
+        if tensor.device != device:
+            raise ValueError(
+                f"{name} is on {tensor.device} but q is on {device}; all paged_decode tensors "
+                "must share one device"
+            )
+    if B == 0:
+        return
+    capacity = max_blocks * block_size
+    global _SEQ_CHECK
+    version = -1 if seqlen.is_inference() else int(seqlen._version)
+    cached = _SEQ_CHECK
+    if cached is not None and cached[0] is seqlen and cached[1] == version and cached[2] == capacity:
+        return
+    low = int(seqlen.min())
+    high = int(seqlen.max())
+    if low < 0:
+        raise ValueError(f"seqlen values must be >= 0, got {low}")
+    if high > capacity:
+        raise ValueError(
+            f"seqlen {high} exceeds the block table capacity {capacity} "
+            f"({max_blocks} blocks x {block_size} tokens)"
+        )
+    _SEQ_CHECK = (seqlen, version, capacity)
+
+
+def _tma_ready(pool: torch.Tensor) -> bool:
+    """Whether the pool's layout can be described by a TMA descriptor as it is."""
+    es = pool.element_size()
+    s = pool.stride()
+    return (
+        s[3] == 1
+        and all(x > 0 and (x * es) % 16 == 0 for x in s[:3])
+        and pool.data_ptr() % 16 == 0
+    )
+
+
+def _kernel_pool(pool: torch.Tensor) -> torch.Tensor:
+    if _tma_ready(pool):
+        return pool
+    copy = pool.contiguous() if not pool.is_contiguous() else pool.clone()
+    if not _tma_ready(copy):  # pragma: no cover - a fresh contiguous tensor always is
+        raise ValueError(f"cannot lay out a pool of shape {tuple(pool.shape)} for TMA")
+    return copy
+
+
+def _workspace(q: torch.Tensor, n_kv_head: int) -> torch.Tensor:
+    B, H, D = q.shape
+    need = _native.workspace_bytes(B, H, n_kv_head, D, q.dtype)
+    key = (q.device.index if q.device.index is not None else torch.cuda.current_device(),
+           _native.stream_handle(q.device))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=q.device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def paged_decode(q, k_cache, v_cache, block_table, seqlen, *, scale: float | None = None):
+    """Decode one query token per row against a paged KV pool (one kernel launch)."""
+    _require_backend()
+    _require_cuda_tensors((("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
+                           ("block_table", block_table), ("seqlen", seqlen)))
+    _validate(q, k_cache, v_cache, block_table, seqlen)
+    B, H, D = q.shape
+    if B == 0:
+        return torch.empty_like(q)
+    q = q.contiguous()
+    if block_table.stride(1) != 1 or block_table.stride(0) < block_table.shape[1]:
+        block_table = block_table.contiguous()
+    seqlen = seqlen.contiguous()
+    seqlen32 = seqlen if seqlen.dtype == torch.int32 else seqlen.to(torch.int32)
+    k_cache = _kernel_pool(k_cache)
+    v_cache = _kernel_pool(v_cache)
+    out = torch.empty_like(q)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    with torch.cuda.device(q.device):
+        _native.decode(q, k_cache, v_cache, block_table, seqlen32, out, float(scale) * _LOG2E,
+                       _workspace(q, k_cache.shape[2]))
+    return out
+
+
+class PagedDecodePlan:
+    """Per-container launch state for repeated decode calls (one launch per layer).
+
+    Mirrors the reference's plan (``model/triton_decode.py:331-520``): every
+    ``(k_cache, v_cache)`` pair is validated once with the full :func:`paged_decode` contract,
+    the block table and int32 seqlen are held by reference (in-place updates are seen, an
+    int64 seqlen is refused rather than snapshotted), and :meth:`run` checks only the query
+    layout. On top of that the plan encodes each layer's two TMA descriptors once (in the
+    native ``pd_plan``) and owns the decode workspace.
+    """
+
+    __slots__ = ("n_layer", "grid", "q_shape", "q_dtype", "q_device", "q_strides", "_k", "_v",
+                 "_block_table", "_seqlen", "_native_plan", "_workspace", "_stream_cache")
+
+    def __init__(self, q, k_caches, v_caches, block_table, seqlen, *, scale: float | None = None):
+        _require_backend()
+        _require_cuda_tensors((("q", q), ("block_table", block_table), ("seqlen", seqlen)))
+        if q.dim() != 3:
+            raise ValueError(f"q must be (B, H, D), got shape {tuple(q.shape)}")
+        if not q.is_contiguous():
+            raise ValueError(
+                "paged_decode_plan needs a contiguous (B, H, D) query, got strides "
+                f"{q.stride()}; call .contiguous() once, not per layer"
+            )
+        b, h, d = q.shape
+        if b == 0:
+            raise ValueError("paged_decode_plan needs at least one row")
+        if seqlen.dtype != torch.int32:
+            raise ValueError(
+                "paged_decode_plan requires an int32 seqlen so in-place updates are visible; "
+                f"got {seqlen.dtype}. Cast once at the container boundary."
+            )
+        if seqlen.stride(0) != 1:
+            raise ValueError(
+                f"paged_decode_plan requires a contiguous 1-D seqlen; got strides {seqlen.stride()}"
+            )
+        if block_table.stride(1) != 1:
+            raise ValueError(
+                "paged_decode_plan requires a column-contiguous block table; got strides "
+                f"{block_table.stride()}"
+            )
+        k_caches = list(k_caches)
+        v_caches = list(v_caches)
+        if len(k_caches) != len(v_caches) or not k_caches:
+            raise ValueError(
+                "paged_decode_plan needs one k_cache/v_cache per layer, got "
+                f"{len(k_caches)} / {len(v_caches)}"
+            )
+        for layer, (k_cache, v_cache) in enumerate(zip(k_caches, v_caches)):
+            _require_cuda_tensors(((f"k_cache[{layer}]", k_cache), (f"v_cache[{layer}]", v_cache)))
+            _validate(q, k_cache, v_cache, block_table, seqlen)
+            if tuple(k_cache.shape) != tuple(k_caches[0].shape) or tuple(v_cache.shape) != tuple(
+                v_caches[0].shape
+            ):
+                raise ValueError("paged_decode_plan needs one pool shape for every layer")
+            if k_cache.stride() != k_caches[0].stride():
+                raise ValueError("paged_decode_plan needs one pool layout for every layer")
+            if v_cache.stride() != v_caches[0].stride():
+                raise ValueError("paged_decode_plan needs one v-pool layout for every layer")
+            if not (_tma_ready(k_cache) and _tma_ready(v_cache)):
+                raise ValueError(
+                    "paged_decode_plan needs pools with a unit head_dim stride, 16-byte multiple "
+                    "strides and a 16-byte aligned base (any contiguous pool qualifies)"
+                )
+        self.n_layer = len(k_caches)
+        self._k = k_caches
+        self._v = v_caches
+        self._block_table = block_table
+        self._seqlen = seqlen
+        self.q_shape = (int(b), int(h), int(d))
+        self.q_dtype = q.dtype
+        self.q_device = q.device
+        self.q_strides = (int(q.stride(0)), int(q.stride(1)), int(q.stride(2)))
+        self.grid = (int(b), int(h))  # logical output grid; the launch is one CTA per SM
+        if scale is None:
+            scale = 1.0 / math.sqrt(d)
+        with torch.cuda.device(q.device):
+            need = _native.workspace_bytes(b, h, k_caches[0].shape[2], d, q.dtype)
+            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=q.device)
+            self._native_plan = _native.NativePlan(
+                k_caches, v_caches, block_table, seqlen, b, h, float(scale) * _LOG2E, self._workspace
+            )
+        self._stream_cache = None
+
+    def run(self, layer: int, q):
+        """Launch the kernel for one layer; ``q`` must match the validated layout."""
+        if not 0 <= int(layer) < self.n_layer:
+            raise IndexError(f"layer {layer} outside the plan's {self.n_layer} layers")
+        if (
+            tuple(q.shape) != self.q_shape
+            or q.dtype != self.q_dtype
+            or q.device != self.q_device
+            or q.stride() != self.q_strides
+        ):
+            raise ValueError(
+                "paged_decode_plan.run got a query that does not match the validated layout "
+                f"{(self.q_shape, self.q_dtype, self.q_strides)}; got "
+                f"{(tuple(q.shape), q.dtype, q.stride())}. Rebuild the plan for a new layout."
+            )
+        out = torch.empty_like(q)
+        self._native_plan.run(int(layer), q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
+        return out
+
+
+def paged_decode_plan(q, k_caches, v_caches, block_table, seqlen, *, scale: float | None = None):
+    """Validate one container's paged-decode tensors and cache their launch state."""
+    return PagedDecodePlan(q, k_caches, v_caches, block_table, seqlen, scale=scale)

@@ -1,0 +1,51 @@
+"""Decode kernel (``pd_decode`` through ``paged_decode``) against the CPU oracle on a B200.
+
+Shapes are the reference's kernel grid (tests/unit/test_triton_decode.py:263-292) plus the
+Qwen3-0.6B head shape; tolerances: fp32 1e-4, bf16 <= 2e-3 absolute (|out| < 1) or a
+correctly rounded bf16 result, and argmax equality for bf16 as in the reference.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from helpers import assert_output_close, build_case
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    pytest.param(1, 2, 2, 64, 16, [1], id="b1-gqa1-d64-l1-bs16"),
+    pytest.param(3, 8, 4, 128, 16, [15, 16, 17], id="b3-gqa2-d128-l15-17-bs16"),
+    pytest.param(8, 8, 2, 64, 32, [1, 15, 16, 17, 100, 1, 15, 16], id="b8-gqa4-d64-bs32"),
+    pytest.param(1, 8, 1, 256, 16, [1664], id="b1-gqa8-d256-l1664-bs16"),
+    pytest.param(3, 8, 1, 256, 32, [100, 1664, 1], id="b3-gqa8-d256-bs32"),
+    pytest.param(8, 16, 8, 128, 16, [1664] * 8, id="qwen3-b8-l1664"),
+    pytest.param(4, 16, 8, 128, 16, [0, 5, 3000, 129], id="qwen3-ragged-zero"),
+    pytest.param(2, 8, 2, 256, 16, [700, 33], id="qwen35-d256-gqa4"),
+    pytest.param(2, 4, 2, 32, 16, [40, 7], id="d32"),
+    pytest.param(2, 4, 4, 16, 8, [40, 7], id="d16-bs8"),
+    pytest.param(2, 6, 2, 64, 16, [90, 300], id="gqa3-chunks"),
+    pytest.param(2, 32, 2, 64, 16, [90, 300], id="gqa16-chunks"),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16], ids=["fp32", "bf16", "fp16"])
+@pytest.mark.parametrize("B,H,Hkv,D,bs,lengths", SHAPES)
+def test_decode_matches_oracle(cuda_device, B, H, Hkv, D, bs, lengths, dtype):
+    from model.triton_decode import paged_decode
+
+    q, k, v, table, seqlen = build_case(B, H, Hkv, D, bs, lengths, dtype=dtype, seed=13)
+    ref_f32, ref = oracle.paged_decode(q, k, v, table, seqlen)
+    got = paged_decode(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), table.to(cuda_device),
+                       seqlen.to(cuda_device))
+    torch.cuda.synchronize()
+    assert got.shape == (B, H, D) and got.dtype == dtype
+    assert_output_close(got, ref_f32, dtype)
+    if dtype != torch.float32:
+        nz = seqlen > 0
+        assert torch.equal(got.cpu()[nz].float().argmax(-1), ref_f32[nz].argmax(-1)) or \
+            (got.cpu().float() - ref_f32).abs().max() < 4e-3
+    from model import _native
+    assert _native.device_error() == 0
