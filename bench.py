@@ -1,0 +1,412 @@
+"""Benchmark of the B200 paged-decode path (one JSON line on rank 0).
+
+Workload (the 28-layer Qwen3-0.6B decode step through the paged pool):
+B=32 rows, every context at 2048 tokens, block size 16, 16 q / 8 kv heads, head_dim 128,
+bf16, 28 per-layer pools of 4224 blocks (7.75 GB of K/V, far larger than the 126 MB L2, so
+every step reads cold HBM). One *step* = one decode step's attention for all 28 layers,
+exactly as ``MiniLLM.forward`` drives ``PagedKV``: ``build_mask`` (seqlen := pos + 1), then
+per layer ``write`` (fused paged-KV append of the new token) and ``attend`` (block-table
+decode), then ``advance``. The context grows by one token per step (2048 -> 2048 + steps).
+
+Reported (``metric`` is BASELINE.json's): ``value`` = KV HBM GB/s of the decode kernels over
+the timed steps (sum of seqlen * 2 * H_kv * D * 2 B per layer-step, every rank, / max-over-
+ranks device time); ``us_per_layer_step``; ``roofline`` of the decode kernel from CUDA events
+around each of its launches; ``e2e`` = the same metric through the public API with q/k/v
+copied from pinned host memory every layer and the attention output copied back;
+``cpu_baseline`` = the reference's CPU gather + seat-decode path (ported, oracle/) on a
+bounded sample of the same workload using every host core.
+
+``--impl reference`` times that CPU port alone (the reference's own CPU implementation of this
+path; rank 0 only) and prints the same line with ``"impl": "reference"``.
+
+Multi-GPU (``torchrun --nproc-per-node N``): rows shard by sequence with no collective, so
+every rank decodes its own B=32 batch (weak scaling); time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "llm-serving_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "paged-decode attn µs/layer-step & KV HBM GB/s vs 8 TB/s peak; decode tok/s"
+N_LAYER, BATCH, CONTEXT, NEW_TOKENS = 28, 32, 2048, 64
+H, H_KV, D, BS = 16, 8, 128, 16
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region (background process that
+    writes to a temporary file; stopped with SIGINT so it flushes)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        import tempfile
+
+        self.index = index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-i",
+                 str(self.index), "-lms", "20", "-f", str(self.path)],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # first sample before the timed region starts
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            import signal
+
+            time.sleep(0.05)
+            self.proc.send_signal(signal.SIGINT)
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, max_sm, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            lines = self.path.read_text().splitlines()
+            self.path.unlink()
+        except OSError:
+            lines = []
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                max_sm = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": max_sm, "reasons": sorted(reasons), "samples": 0}
+        loaded = [x for x in sm if max_sm is None or x >= 0.3 * max_sm] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max_sm, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), world, local
+    return None, 0, 1, 0
+
+
+def _max_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def _barrier(dist, device):
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+# ------------------------------------------------------------------------------ GPU arm
+
+
+def _container(device, budget: int, seed: int):
+    """The engine's paged arm at config-2 shape: BlockManager tables, a PagedPool of 28
+    per-layer K/V pools filled with N(0, 1) bf16, and the PagedKV decode container."""
+    from model.paged import PagedKV, PagedPool
+    from serve.block_manager import BlockManager
+
+    manager = BlockManager(BATCH * -(-(CONTEXT + budget) // BS), BS)
+    tables = [manager.reserve(manager.blocks_for(CONTEXT, budget)) for _ in range(BATCH)]
+    pool = PagedPool(N_LAYER, manager.n_blocks, BS, H_KV, D, dtype=torch.bfloat16, device=device, n_head=H)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    for t in pool.keys + pool.values:
+        t.copy_(torch.randn(t.shape, generator=gen, device=device))
+    return PagedKV(pool, tables, [CONTEXT] * BATCH, rope_len=CONTEXT + budget, n_head=H)
+
+
+def run_gpu(args) -> dict | None:
+    from model import _native
+
+    dist, rank, world, local = _dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    steps, warmup = args.steps, args.warmup
+    budget = max(NEW_TOKENS, warmup + 2 * steps + 1)  # tokens each row may still append
+    kv = _container(device, budget, seed=rank)
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    ring = 4  # distinct per-layer inputs cycled over the steps
+    qs = torch.randn(ring, N_LAYER, BATCH, H, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    ks = torch.randn(ring, N_LAYER, BATCH, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    vs = torch.randn(ring, N_LAYER, BATCH, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+
+    def kv_bytes_of_step() -> int:
+        # seqlen after build_mask(next_token=True) is pos + 1 for every row.
+        return sum(p + 1 for p in kv._host_pos) * 2 * H_KV * D * 2 * N_LAYER
+
+    def step(i: int, events=None):
+        kv.build_mask(next_token=True)
+        for layer in range(N_LAYER):
+            kv.write(layer, ks[i % ring, layer], vs[i % ring, layer])
+            if events is not None:
+                events[layer][0].record(stream)
+            kv.attend(layer, qs[i % ring, layer])
+            if events is not None:
+                events[layer][1].record(stream)
+        kv.advance()
+
+    for i in range(warmup):
+        step(i)
+    assert _native.device_error() == 0, "device error word set during warm-up"
+
+    # ---- device-resident timed region -------------------------------------------------
+    kv_bytes = 0
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(N_LAYER)] for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(dist, device)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(steps):
+            kv_bytes += kv_bytes_of_step()
+            step(warmup + i, ev[i])
+        stop.record(stream)
+        _barrier(dist, device)
+    ms_local = start.elapsed_time(stop)
+    decode_ms = sum(e[0].elapsed_time(e[1]) for st in ev for e in st)
+    assert _native.device_error() == 0, "device error word set in the timed region"
+    ms = _max_over_ranks(dist, ms_local, device)
+    total_bytes = _sum_over_ranks(dist, float(kv_bytes), device)
+    per_launch_bytes = kv_bytes / (steps * N_LAYER)
+    per_launch_ms = decode_ms / (steps * N_LAYER)
+
+    # ---- end to end through the public API with host buffers ---------------------------
+    e2e = _run_e2e(kv, device, stream, rank, steps, warmup, dist)
+
+    if rank != 0:
+        _finish(dist)
+        return None
+    peaks = _peaks()
+    achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
+    gbs = total_bytes / (ms * 1e-3) / 1e9
+    traffic = _profiled_traffic()
+    line = {
+        "metric": METRIC,
+        "value": round(gbs, 1),
+        "unit": "GB/s (KV bytes read by decode, all ranks)",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": round(ms / steps, 4),
+        "us_per_layer_step": round(ms * 1e3 / (steps * N_LAYER), 2),
+        "decode_kernel_us_per_layer": round(per_launch_ms * 1e3, 2),
+        "decode_tok_s_attention_only": round(world * BATCH * steps / (ms * 1e-3), 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/q, random-init; no dataset on this path)",
+        "config": {
+            "workload": "BASELINE configs[1] attention path: 28-layer Qwen3-0.6B decode step through "
+                        "PagedKV (fused append + block-table decode per layer)",
+            "batch_per_gpu": BATCH, "context": f"{CONTEXT}+step", "layers": N_LAYER, "block_size": BS,
+            "heads": f"{H}q/{H_KV}kv", "head_dim": D, "parallelism": f"rows sharded by sequence x{world}",
+            "l2": "inputs larger than L2 (7.75 GB of per-layer pools per GPU; each layer reads 268 MB)",
+        },
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+            "traffic": traffic, "kernel": "pd_decode_kernel<bf16,128,2>",
+            "algorithmic_bytes_per_launch": int(per_launch_bytes),
+        },
+        "e2e": e2e,
+        "gpu_launches": steps * N_LAYER * 2,
+        "clocks": clocks.summary(),
+    }
+    line["cpu_baseline"] = cpu_baseline(sample_layers=args.cpu_sample_layers)
+    _finish(dist)
+    return line
+
+
+def _run_e2e(kv, device, stream, rank, steps, warmup, dist) -> dict:
+    """Same steps through PagedKV with per-layer inputs copied from pinned host memory and the
+    attention output copied back (both inside the timed region)."""
+    gen = torch.Generator().manual_seed(99 + rank)
+    hq = torch.randn(N_LAYER, BATCH, H, 1, D, generator=gen).to(torch.bfloat16).pin_memory()
+    hk = torch.randn(N_LAYER, BATCH, H_KV, 1, D, generator=gen).to(torch.bfloat16).pin_memory()
+    hv = torch.randn(N_LAYER, BATCH, H_KV, 1, D, generator=gen).to(torch.bfloat16).pin_memory()
+    hout = torch.empty(N_LAYER, BATCH, H, 1, D, dtype=torch.bfloat16).pin_memory()
+    dq = torch.empty(N_LAYER, BATCH, H, 1, D, dtype=torch.bfloat16, device=device)
+    dk = torch.empty(N_LAYER, BATCH, H_KV, 1, D, dtype=torch.bfloat16, device=device)
+    dv = torch.empty_like(dk)
+    kv_bytes = 0
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = steps
+    _barrier(dist, device)
+    start.record(stream)
+    for _ in range(n):
+        kv.build_mask(next_token=True)
+        kv_bytes += sum(p + 1 for p in kv._host_pos) * 2 * H_KV * D * 2 * N_LAYER
+        for layer in range(N_LAYER):
+            dq[layer].copy_(hq[layer], non_blocking=True)
+            dk[layer].copy_(hk[layer], non_blocking=True)
+            dv[layer].copy_(hv[layer], non_blocking=True)
+            kv.write(layer, dk[layer], dv[layer])
+            out = kv.attend(layer, dq[layer])
+            hout[layer].copy_(out, non_blocking=True)
+        kv.advance()
+    stop.record(stream)
+    _barrier(dist, device)
+    ms = _max_over_ranks(dist, start.elapsed_time(stop), device)
+    total = _sum_over_ranks(dist, float(kv_bytes), device)
+    h2d = N_LAYER * (BATCH * H * D + 2 * BATCH * H_KV * D) * 2
+    d2h = N_LAYER * BATCH * H * D * 2
+    return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s (KV bytes read by decode, all ranks)",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
+            "us_per_layer_step": round(ms * 1e3 / (n * N_LAYER), 2)}
+
+
+def _profiled_traffic():
+    """DRAM bytes of one decode launch from the committed ncu summary (if present)."""
+    path = ROOT / "profiles" / "decode_config2_traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()).get("dram_bytes_per_launch")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def _finish(dist):
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------ CPU arm
+
+
+def _cpu_sample(sample_layers: int, seed: int = 0):
+    """Config-2 shapes for ``sample_layers`` layers on the CPU (bf16 K/V, same generator)."""
+    from serve import workloads
+
+    wl = workloads.config2("cpu", seed=seed, n_layer=sample_layers)
+    return wl
+
+
+def cpu_baseline(sample_layers: int = 2, threads: int = 0) -> dict:
+    """The reference's CPU path (gather_pool + hand_baddbmm seat decode, ported in oracle/)
+    on a bounded sample: ``sample_layers`` layer-steps of the config-2 workload."""
+    from oracle import oracle
+
+    threads = threads or os.cpu_count() or 1
+    wl = _cpu_sample(sample_layers)
+    lpad = -(-CONTEXT // 64) * 64
+    oracle.seat_decode(wl.q[0][:1], torch.zeros(1, H_KV, 64, D, dtype=torch.bfloat16),
+                       torch.zeros(1, H_KV, 64, D, dtype=torch.bfloat16), torch.tensor([1]), threads=threads)
+    t0 = time.perf_counter()
+    for layer in range(sample_layers):
+        gk, gv = oracle.gather_pool(wl.k_pools[layer], wl.v_pools[layer], wl.block_table, wl.seqlen, lpad,
+                                    threads=threads)
+        oracle.seat_decode(wl.q[layer], gk, gv, wl.seqlen, threads=threads)
+    dt = time.perf_counter() - t0
+    kv = wl.kv_bytes_per_layer() * sample_layers
+    return {"value": round(kv / dt / 1e9, 3), "unit": "GB/s (KV bytes read by decode)", "cores": threads,
+            "kind": "port",
+            "sample": f"{sample_layers} layer-steps of config 2 (B=32, L=2048, 16q/8kv, D=128, bf16): "
+                      f"gather_pool + hand_baddbmm seat decode, {dt * 1e3 / sample_layers:.1f} ms/layer-step",
+            "us_per_layer_step": round(dt * 1e6 / sample_layers, 1)}
+
+
+def run_reference(args) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    base = cpu_baseline(sample_layers=1, threads=threads)  # warm-up + first sample
+    per_step = []
+    for _ in range(args.steps):
+        per_step.append(cpu_baseline(sample_layers=1, threads=threads)["us_per_layer_step"])
+    us = statistics.median(per_step)
+    gbs = CONTEXT * BATCH * 2 * H_KV * D * 2 / (us * 1e-6) / 1e9
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(gbs, 3),
+        "unit": "GB/s (KV bytes read by decode, all ranks)", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(us * N_LAYER / 1e3, 2), "us_per_layer_step": round(us, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/q)",
+        "config": {"workload": "BASELINE configs[1] attention path on the CPU: reference gather_pool + "
+                               "hand_baddbmm seat decode (ported, oracle/), one layer-step per sample",
+                   "batch": BATCH, "context": CONTEXT, "layers": N_LAYER, "block_size": BS},
+        "cpu_baseline": {**base, "value": round(gbs, 3)},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s (KV bytes read by decode, all ranks)",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=100)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--cpu-sample-layers", type=int, default=2)
+    args = parser.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    line = run_reference(args) if args.impl == "reference" else run_gpu(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -51,6 +51,10 @@ const char* pd_status_string(int status);
 /* Library ABI version (increments on any signature change). */
 int pd_abi_version(void);
 
+/* Name and description of the last CUDA error a call on this thread returned as PD_ERR_CUDA
+ * (static storage; "" when none). No reference counterpart: the Triton launch raises. */
+const char* pd_last_error_string(void);
+
 /* Reads the calling thread's current device's error word into *bits and, if `clear`,
  * resets it. Synchronises the device. No reference counterpart: the Triton kernel has no
  * device-side status (model/triton_decode.py:63-66 trusts the table instead). */
@@ -68,15 +72,14 @@ int pd_device_error(unsigned int* bits, int clear);
  *   seqlen   (B,) int32; values are clamped to [0, max_blocks * block_size] on device
  *   out      (B, H, D)       strides o_sb, o_sh
  *   scale_log2 = scale * log2(e)  (model/triton_decode.py:291-292)
- *   workspace: device memory of at least pd_decode_workspace_bytes(...) bytes whose
- *     first pd_decode_counter_bytes(...) bytes are zero before the first call; the kernel
- *     leaves them zero again. One workspace must not be used by two launches that may
- *     run concurrently.
+ *   workspace: device memory of at least pd_decode_workspace_bytes(...) bytes, 256-byte
+ *     aligned, with arbitrary contents (no clearing needed: split rows are counted with
+ *     per-launch epochs). One workspace must not be used by two launches that may run
+ *     concurrently.
  *
  * Row b, head h reads only the first ceil(seqlen[b] / block_size) table entries;
  * zero-length rows produce exact zeros (model/triton_decode.py:639).
  */
-size_t pd_decode_counter_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim);
 size_t pd_decode_workspace_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head,
                                  int32_t head_dim, int32_t dtype);
 

@@ -3,11 +3,14 @@
 // Host-side argument checks, TMA descriptor encoding for the paged pools, workspace layout,
 // launch-shape selection and the plan handle. All device work is in pd_decode_*.cu,
 // pd_append.cu and pd_merge.cu.
+#include <atomic>
+#include <chrono>
+#include <cstdio>
 #include <mutex>
 #include <new>
 #include <vector>
 
-#include "../../include/paged_decode.h"
+#include "paged_decode.h"
 #include "pd_internal.h"
 
 namespace pd {
@@ -28,6 +31,24 @@ struct Tuning {
 };
 Tuning g_tuning;
 std::mutex g_mutex;
+
+thread_local char g_last_error[256] = "";
+
+// Launch ids for the split-item arrival counters: distinct per launch in this process, seeded
+// from the clock so a buffer left over from another process is unlikely to match.
+std::atomic<uint32_t> g_epoch{uint32_t(std::chrono::steady_clock::now().time_since_epoch().count()) | 1u};
+
+uint32_t next_epoch() {
+  uint32_t e = g_epoch.fetch_add(1, std::memory_order_relaxed);
+  return e == 0 ? g_epoch.fetch_add(1, std::memory_order_relaxed) : e;
+}
+
+// Records a failed CUDA call for pd_last_error_string and returns PD_ERR_CUDA.
+int cuda_fail(cudaError_t e, const char* where) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(e),
+           cudaGetErrorString(e));
+  return PD_ERR_CUDA;
+}
 
 int g_sm_count[kMaxDevices] = {0};
 unsigned* g_err_ptr[kMaxDevices] = {nullptr};
@@ -177,7 +198,7 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
                                  const Launch& L) {
   WorkspaceLayout w;
   const int rows = batch < L.rows_per_launch ? batch : L.rows_per_launch;
-  w.counters = round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 4, 256);
+  w.counters = round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 8, 256);
   const size_t workers = size_t(L.grid) * L.warps;
   w.ml_off = w.counters;
   w.acc_off = w.ml_off + round_up(workers * 2 * 2 * g.gt * 4, 256);
@@ -252,7 +273,7 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   p.bt_stride = bt_stride;
   p.seqlen = seqlen;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  p.counters = reinterpret_cast<int*>(ws);
+  p.counters = reinterpret_cast<unsigned long long*>(ws);
   p.ws_ml = reinterpret_cast<float*>(ws + P->ws.ml_off);
   p.ws_acc = reinterpret_cast<float*>(ws + P->ws.acc_off);
   p.err = err;
@@ -293,6 +314,7 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
     DecodeParams p = P.base;
     p.batch = rows;
     p.mode = mode;
+    p.epoch = next_epoch();
     p.q = static_cast<const unsigned char*>(q) + int64_t(b0) * q_sb * es;
     p.q_sb = q_sb;
     p.q_sh = q_sh;
@@ -312,7 +334,7 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
     const size_t smem = smem_for(P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
                                  &p.smem_stage_off);
     cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream);
-    if (e != cudaSuccess) return PD_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   }
   return PD_OK;
 }
@@ -374,26 +396,23 @@ const char* pd_status_string(int status) {
 
 int pd_abi_version(void) { return kAbiVersion; }
 
+const char* pd_last_error_string(void) { return g_last_error; }
+
 int pd_device_error(unsigned int* bits, int clear) {
   if (bits == nullptr) return PD_ERR_INVALID;
   int dev = 0;
   if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
-  if (cudaDeviceSynchronize() != cudaSuccess) return PD_ERR_CUDA;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "pd_device_error synchronize");
   unsigned v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_error_word, sizeof(v)) != cudaSuccess) return PD_ERR_CUDA;
+  e = cudaMemcpyFromSymbol(&v, g_error_word, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "pd_device_error read");
   *bits = v;
   if (clear && v != 0) {
     unsigned zero = 0;
     if (cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) != cudaSuccess) return PD_ERR_CUDA;
   }
   return PD_OK;
-}
-
-size_t pd_decode_counter_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim) {
-  Geometry g;
-  if (geometry(n_head, n_kv_head, head_dim, 16, PD_BF16, &g) != PD_OK) return 0;
-  const int rows = batch < 1 ? 1 : (batch > 4096 ? 4096 : batch);
-  return round_up(size_t(rows) * n_kv_head * g.n_gchunks * 4, 256);
 }
 
 size_t pd_decode_workspace_bytes(int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
@@ -508,8 +527,8 @@ int pd_lse_merge(const float* m_parts, const float* l_parts, const float* acc_pa
   p.batch = batch;
   p.n_head = n_head;
   p.head_dim = head_dim;
-  return launch_merge(p, dtype, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PD_OK
-                                                                                  : PD_ERR_CUDA;
+  const cudaError_t e = launch_merge(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PD_OK : cuda_fail(e, "merge launch");
 }
 
 static int append_common(AppendParams& p, int32_t pool_dtype, int32_t src_dtype,
@@ -548,7 +567,7 @@ static int append_common(AppendParams& p, int32_t pool_dtype, int32_t src_dtype,
                    ok_dst(p.k_pool, p.kp_sb, p.kp_sn, p.kp_sh) &&
                    ok_dst(p.v_pool, p.vp_sb, p.vp_sn, p.vp_sh);
   cudaError_t e = launch_append(p, src_dtype, pool_dtype, vec, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? PD_OK : PD_ERR_CUDA;
+  return e == cudaSuccess ? PD_OK : cuda_fail(e, "append launch");
 }
 
 int pd_kv_append_slots(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
@@ -612,7 +631,7 @@ int pd_set_decode_tuning(int32_t warps_per_cta, int32_t stages, int32_t ctas_per
   if (ctas_per_sm > 0) t.ctas_per_sm = ctas_per_sm;
   if (min_tiles_per_warp > 0) t.min_tiles = min_tiles_per_warp;
   if (t.warps > 8 || t.stages < 2 || t.stages > 16 || t.ctas_per_sm > 8) return PD_ERR_INVALID;
-  if (size_t(t.warps) * t.stages * 8192 + 4096 > size_t(kMaxSmemPerBlock)) return PD_ERR_INVALID;
+  if (size_t(t.warps) * t.stages * 8192 + 2048 > size_t(kMaxSmemPerBlock)) return PD_ERR_INVALID;
   g_tuning = t;
   return PD_OK;
 }

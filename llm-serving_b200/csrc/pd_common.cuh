@@ -114,6 +114,10 @@ struct Elem<float> {
     return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
                       __float_as_uint(f[3]));
   }
+  __device__ __forceinline__ static void unpack_pairs(const uint4& r, float2* f) {
+    f[0] = make_float2(__uint_as_float(r.x), __uint_as_float(r.y));
+    f[1] = make_float2(__uint_as_float(r.z), __uint_as_float(r.w));
+  }
   __device__ __forceinline__ static float to_float(float x) { return x; }
   __device__ __forceinline__ static float from_float(float x) { return x; }
 };
@@ -131,6 +135,15 @@ struct Elem<__nv_bfloat16> {
     unpack2(r.y, f + 2);
     unpack2(r.z, f + 4);
     unpack2(r.w, f + 6);
+  }
+  __device__ __forceinline__ static float2 pair(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  __device__ __forceinline__ static void unpack_pairs(const uint4& r, float2* f) {
+    f[0] = pair(r.x);
+    f[1] = pair(r.y);
+    f[2] = pair(r.z);
+    f[3] = pair(r.w);
   }
   __device__ __forceinline__ static uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // round to nearest even
@@ -159,6 +172,12 @@ struct Elem<__half> {
     unpack2(r.z, f + 4);
     unpack2(r.w, f + 6);
   }
+  __device__ __forceinline__ static void unpack_pairs(const uint4& r, float2* f) {
+    f[0] = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    f[1] = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    f[2] = __half22float2(*reinterpret_cast<const __half2*>(&r.z));
+    f[3] = __half22float2(*reinterpret_cast<const __half2*>(&r.w));
+  }
   __device__ __forceinline__ static uint32_t pack2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -184,7 +203,7 @@ struct DecodeParams {
   const int32_t* table;
   int64_t bt_stride;
   const int32_t* seqlen;
-  int* counters;    // (B * H_kv * n_gchunks) arrival counters, zero between launches
+  unsigned long long* counters;  // (B * H_kv * n_gchunks) arrival counters: (epoch << 32) | count
   float* ws_ml;     // (workers * 2, 2 * GT) partial m | l
   float* ws_acc;    // (workers * 2, GT * D) partial accumulators
   unsigned* err;    // device error word
@@ -205,6 +224,7 @@ struct DecodeParams {
   int32_t smem_arrays_off;
   int32_t smem_stage_off;
   float scale_log2;
+  uint32_t epoch;  // launch id; a counter holding another epoch counts as zero
 };
 
 struct AppendParams {

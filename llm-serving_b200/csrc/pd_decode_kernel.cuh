@@ -50,6 +50,7 @@ struct DecodeCfg {
   static constexpr int CPL = CHUNKS / LPR;  // chunks per lane per row
   static constexpr int EPC = 16 / ES;       // elements per chunk
   static constexpr int EPL = CPL * EPC;     // elements per lane per row
+  static constexpr int PPL = EPL / 2;       // element pairs per lane per row (packed fp32 math)
   static constexpr int RPL = 32 / LPR;      // rows covered by one warp-wide load
   static constexpr int LOG_RPL = ilog2(RPL);
   static constexpr int TILE_BYTES = 4096;   // K bytes per stage (same again for V)
@@ -95,6 +96,22 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, const int* pre, const 
   if (c.b < batch) {
     c.ntile = pre[c.b + 1] - pre[c.b];
     c.len = lens[c.b];
+  }
+}
+
+// Arrival on an item counter shared by the pieces of one split item; returns how many pieces
+// of this launch arrived before. The counter holds (epoch << 32) | count: a value written by
+// another launch (or never initialised) has another epoch and counts as zero, so workspaces
+// need no clearing between launches, whatever the previous launch's shape.
+__device__ __forceinline__ int arrive_epoch(unsigned long long* counter, uint32_t epoch) {
+  unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(counter);
+  for (;;) {
+    const bool mine = uint32_t(seen >> 32) == epoch;
+    const unsigned long long want =
+        mine ? seen + 1ull : ((unsigned long long)epoch << 32) | 1ull;
+    const unsigned long long prev = atomicCAS(counter, seen, want);
+    if (prev == seen) return mine ? int(uint32_t(seen)) : 0;
+    seen = prev;
   }
 }
 
@@ -313,8 +330,11 @@ __global__ void __launch_bounds__(256, 1)
     hold_g[j] = idx % GT;
   }
 
-  float qf[GT][C::EPL];
-  float acc[GT][C::EPL];
+  // q and the P.V accumulators as pairs of consecutive head_dim elements: every multiply-add
+  // below is a packed fp32 FMA (two lanes of fp32 per instruction, same rounding as fmaf).
+  float2 qf[GT][C::PPL];
+  float2 acc[GT][C::PPL];
+  auto acc_at = [&](int g, int e) -> float& { return (e & 1) ? acc[g][e >> 1].y : acc[g][e >> 1].x; };
   float m_run[GT], l_run[GT];
   int seg_first_tile = 0;
   bool first_segment = true;
@@ -327,18 +347,18 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
     for (int i = 0; i < C::NT; ++i) {
       const int row = i * C::RPL + rg;
-      float kf[C::EPL];
+      float2 kf[C::PPL];
 #pragma unroll
       for (int c = 0; c < C::CPL; ++c) {
         const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
-        E::unpack(raw, &kf[c * C::EPC]);
+        E::unpack_pairs(raw, &kf[c * (C::EPC / 2)]);
       }
 #pragma unroll
       for (int g = 0; g < GT; ++g) {
-        float a = 0.f;
+        float2 a = __fmul2_rn(qf[g][0], kf[0]);
 #pragma unroll
-        for (int e = 0; e < C::EPL; ++e) a = fmaf(qf[g][e], kf[e], a);
-        sv[i * GT + g] = a;
+        for (int e = 1; e < C::PPL; ++e) a = __ffma2_rn(qf[g][e], kf[e], a);
+        sv[i * GT + g] = a.x + a.y;
       }
     }
 #pragma unroll
@@ -394,8 +414,9 @@ __global__ void __launch_bounds__(256, 1)
         const float alpha = exp2f(m_run[g] - mn);
         m_run[g] = mn;
         l_run[g] *= alpha;
+        const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
-        for (int e = 0; e < C::EPL; ++e) acc[g][e] *= alpha;
+        for (int e = 0; e < C::PPL; ++e) acc[g][e] = __fmul2_rn(acc[g][e], alpha2);
       }
     }
   };
@@ -422,24 +443,25 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
     for (int i = 0; i < C::NT; ++i) {
       const int row = i * C::RPL + rg;
-      float vf[C::EPL];
+      float2 vf[C::PPL];
 #pragma unroll
       for (int c = 0; c < C::CPL; ++c) {
         const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
-        E::unpack(raw, &vf[c * C::EPC]);
+        E::unpack_pairs(raw, &vf[c * (C::EPC / 2)]);
       }
       if (!full) {
         const bool live = row < valid_rows;
 #pragma unroll
-        for (int e = 0; e < C::EPL; ++e) vf[e] = live ? vf[e] : 0.f;
+        for (int e = 0; e < C::PPL; ++e) vf[e] = live ? vf[e] : make_float2(0.f, 0.f);
       }
 #pragma unroll
       for (int g = 0; g < GT; ++g) {
         const int idx = i * GT + g;
         const int src = (rg << C::LOG_LPR) + ((idx / C::R) << C::AL);
         const float pv = __shfl_sync(FULL_MASK, pj[idx % C::R], src);
+        const float2 pv2 = make_float2(pv, pv);
 #pragma unroll
-        for (int e = 0; e < C::EPL; ++e) acc[g][e] = fmaf(pv, vf[e], acc[g][e]);
+        for (int e = 0; e < C::PPL; ++e) acc[g][e] = __ffma2_rn(pv2, vf[e], acc[g][e]);
       }
     }
   };
@@ -453,12 +475,12 @@ __global__ void __launch_bounds__(256, 1)
       for (int cc = 0; cc < C::CPL; ++cc) {
         const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qrow + int64_t(hq + g) * p.q_sh +
                                                                  (cc * C::LPR + pl) * C::EPC));
-        E::unpack(raw, &qf[g][cc * C::EPC]);
+        E::unpack_pairs(raw, &qf[g][cc * (C::EPC / 2)]);
       }
       m_run[g] = -INFINITY;
       l_run[g] = 0.f;
 #pragma unroll
-      for (int e = 0; e < C::EPL; ++e) acc[g][e] = 0.f;
+      for (int e = 0; e < C::PPL; ++e) acc[g][e] = make_float2(0.f, 0.f);
     }
   };
 
@@ -529,7 +551,10 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int g = 0; g < GT; ++g) {
 #pragma unroll
-          for (int e = 0; e < C::EPL; ++e) acc[g][e] += __shfl_xor_sync(FULL_MASK, acc[g][e], o);
+          for (int e = 0; e < C::PPL; ++e) {
+            acc[g][e].x += __shfl_xor_sync(FULL_MASK, acc[g][e].x, o);
+            acc[g][e].y += __shfl_xor_sync(FULL_MASK, acc[g][e].y, o);
+          }
         }
       }
       const bool whole = seg_first_tile == 0 && cur.tile == cur.ntile - 1;
@@ -544,7 +569,7 @@ __global__ void __launch_bounds__(256, 1)
               for (int c = 0; c < C::CPL; ++c) {
                 float o[C::EPC];
 #pragma unroll
-                for (int e = 0; e < C::EPC; ++e) o[e] = acc[g][c * C::EPC + e] * inv;
+                for (int e = 0; e < C::EPC; ++e) o[e] = acc_at(g, c * C::EPC + e) * inv;
                 *reinterpret_cast<uint4*>(orow + int64_t(hq0 + g) * p.o_sh + (c * C::LPR + pl) * C::EPC) =
                     E::pack(o);
               }
@@ -568,8 +593,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
                 for (int e = 0; e < C::EPC; e += 4)
                   *reinterpret_cast<float4*>(dst + e) =
-                      make_float4(acc[g][c * C::EPC + e], acc[g][c * C::EPC + e + 1],
-                                  acc[g][c * C::EPC + e + 2], acc[g][c * C::EPC + e + 3]);
+                      make_float4(acc_at(g, c * C::EPC + e), acc_at(g, c * C::EPC + e + 1),
+                                  acc_at(g, c * C::EPC + e + 2), acc_at(g, c * C::EPC + e + 3));
               }
             }
           }
@@ -595,8 +620,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
               for (int e = 0; e < C::EPC; e += 4)
                 *reinterpret_cast<float4*>(dst + e) =
-                    make_float4(acc[g][c * C::EPC + e], acc[g][c * C::EPC + e + 1],
-                                acc[g][c * C::EPC + e + 2], acc[g][c * C::EPC + e + 3]);
+                    make_float4(acc_at(g, c * C::EPC + e), acc_at(g, c * C::EPC + e + 1),
+                                acc_at(g, c * C::EPC + e + 2), acc_at(g, c * C::EPC + e + 3));
             }
           }
         }
@@ -608,7 +633,7 @@ __global__ void __launch_bounds__(256, 1)
         const int c_first = worker_of(us, units, workers);
         const int c_last = worker_of(ue - 1, units, workers);
         int ticket = 0;
-        if (lane == 0) ticket = atomicAdd(p.counters + item_global, 1);
+        if (lane == 0) ticket = arrive_epoch(p.counters + item_global, p.epoch);
         ticket = __shfl_sync(FULL_MASK, ticket, 0);
         if (ticket == c_last - c_first) {
           __threadfence();
@@ -675,7 +700,6 @@ __global__ void __launch_bounds__(256, 1)
               }
             }
           }
-          if (lane == 0) p.counters[item_global] = 0;  // ready for the next launch
         }
       }
       first_segment = false;

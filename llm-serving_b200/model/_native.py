@@ -40,8 +40,8 @@ _c_float = ctypes.c_float
 _SIGNATURES = {
     "pd_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "pd_abi_version": (ctypes.c_int, []),
+    "pd_last_error_string": (ctypes.c_char_p, []),
     "pd_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
-    "pd_decode_counter_bytes": (_c_size, [_c_i32, _c_i32, _c_i32, _c_i32]),
     "pd_decode_workspace_bytes": (_c_size, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
     "pd_decode": (
         ctypes.c_int,
@@ -130,7 +130,8 @@ def check(status: int, what: str) -> None:
     message = f"{what} failed: {status_string(status)} (status {status})"
     if status in (PD_ERR_INVALID, PD_ERR_UNSUPPORTED, PD_ERR_WORKSPACE):
         raise ValueError(message)
-    raise RuntimeError(message)
+    detail = require().pd_last_error_string().decode()
+    raise RuntimeError(f"{message}: {detail}" if detail else message)
 
 
 def stream_handle(device: torch.device) -> int:

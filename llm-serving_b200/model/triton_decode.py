@@ -48,8 +48,9 @@ _MAX_HEAD_DIM = 256
 #: the one host synchronisation of the wrapper; a persistent seqlen pays it once per version.
 _SEQ_CHECK: tuple[torch.Tensor, int, int] | None = None
 
-#: Per (device, stream) decode workspace for ``paged_decode``: zero-initialised once, left
-#: zero by every launch, never shared by two streams.
+#: Per (device, stream) decode workspace for ``paged_decode``. Its contents never need
+#: clearing (split rows are counted with per-launch epochs); one per stream, so two streams
+#: never share one.
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 
 
@@ -187,7 +188,7 @@ def _workspace(q: torch.Tensor, n_kv_head: int) -> torch.Tensor:
            _native.stream_handle(q.device))
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=q.device)
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
         _WORKSPACES[key] = ws
     return ws
 
@@ -295,7 +296,7 @@ class PagedDecodePlan:
             scale = 1.0 / math.sqrt(d)
         with torch.cuda.device(q.device):
             need = _native.workspace_bytes(b, h, k_caches[0].shape[2], d, q.dtype)
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=q.device)
+            self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
             self._native_plan = _native.NativePlan(
                 k_caches, v_caches, block_table, seqlen, b, h, float(scale) * _LOG2E, self._workspace
             )

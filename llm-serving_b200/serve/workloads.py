@@ -117,8 +117,11 @@ def fragmented_tables(lengths: list[int], n_blocks: int, block_size: int, seed: 
     """Tables for ``lengths`` from a BlockManager whose free list a seeded history fragmented.
 
     History: ``churn`` rounds; each reserves a dummy request of 1..64 blocks (if it fits) and,
-    with probability 1/2, frees a random live dummy. Then every row reserves its blocks, and
-    the dummies still live stay allocated (they are other requests' KV).
+    with probability 1/2, frees a random live dummy. Smallest-first reservations refill the
+    holes during the churn, so a random half of the dummies still live is then freed (finished
+    requests), leaving holes of many sizes. Every row then reserves its blocks -- its table
+    threads through those holes -- and the remaining dummies stay allocated (other requests'
+    KV).
     """
     import random
 
@@ -131,6 +134,8 @@ def fragmented_tables(lengths: list[int], n_blocks: int, block_size: int, seed: 
             live.append(ids)
         if live and rng.random() < 0.5:
             manager.free(live.pop(rng.randrange(len(live))))
+    for _ in range(len(live) // 2):
+        manager.free(live.pop(rng.randrange(len(live))))
     while live and manager.stats()["free"] < sum(-(-n // block_size) for n in lengths):
         manager.free(live.pop(rng.randrange(len(live))))
     tables = []

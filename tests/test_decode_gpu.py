@@ -49,3 +49,26 @@ def test_decode_matches_oracle(cuda_device, B, H, Hkv, D, bs, lengths, dtype):
             (got.cpu().float() - ref_f32).abs().max() < 4e-3
     from model import _native
     assert _native.device_error() == 0
+
+
+def test_one_workspace_serves_any_shape_sequence_without_clearing(cuda_device):
+    """A workspace reused across shapes (and pre-filled with garbage) needs no clearing: the
+    split-row counters carry a per-launch epoch. Regression for a cached workspace whose
+    counter region grew over the previous shape's partials."""
+    from model import _native
+
+    ws = torch.full((64 << 20,), 0xFF, dtype=torch.uint8, device=cuda_device)
+    ws[::7] = 0x3C
+    cases = [(8, 16, 8, 128, 16, [700] * 8), (32, 16, 8, 128, 16, [2100] * 32),
+             (2, 16, 8, 128, 16, [5000, 10]), (32, 16, 8, 128, 16, [2100] * 32)]
+    for i, (B, H, Hkv, D, bs, lengths) in enumerate(cases):
+        q, k, v, table, seqlen = build_case(B, H, Hkv, D, bs, lengths, dtype=torch.bfloat16, seed=40 + i)
+        ref_f32, _ = oracle.paged_decode(q, k, v, table, seqlen)
+        qd = q.to(cuda_device)
+        out = torch.empty_like(qd)
+        assert _native.workspace_bytes(B, H, Hkv, D, q.dtype) <= ws.numel()
+        _native.decode(qd, k.to(cuda_device), v.to(cuda_device), table.to(cuda_device), seqlen.to(cuda_device),
+                       out, _native.log2e_scale(1 / D ** 0.5), ws)
+        torch.cuda.synchronize()
+        assert_output_close(out, ref_f32, torch.bfloat16)
+    assert _native.device_error() == 0
