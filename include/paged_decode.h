@@ -92,6 +92,40 @@ int pd_decode(const void* q, int64_t q_sb, int64_t q_sh,
               int32_t dtype, float scale_log2, void* workspace, size_t workspace_bytes,
               void* stream);
 
+/* pd_decode_noalloc -- the same decode as pd_decode for callers that cannot allocate device
+ * memory. No counterpart in the reference (it always runs inside PyTorch, which allocates).
+ *
+ * Who needs it: hosts that bind this C ABI without owning a device allocator -- for example
+ * a Go, Java or Node serving process calling through cgo/JNI/N-API with only raw tensor
+ * pointers handed to it -- and callers whose device memory is already fully reserved by
+ * another allocator (PyTorch's caching allocator, an inference runtime's arena), where an
+ * extra cudaMalloc can fail and cudaMalloc/cudaFree would synchronise the device.
+ *
+ * What differs from pd_decode: there is no workspace argument. The split-row scratch lives in
+ * one fixed array of PD_NOALLOC_SCRATCH_BYTES (8 MiB) compiled into the library; every GPU
+ * that loads the library holds that much device memory until the process exits. The call
+ * itself performs no allocation of any kind. Its first call on a device, with that device
+ * current, looks the array's device address up (cudaGetSymbolAddress) and caches it; make
+ * that first call before capturing a stream. Shapes whose scratch need exceeds the array
+ * (pd_decode_workspace_bytes(...) > PD_NOALLOC_SCRATCH_BYTES, e.g. head_dim 256 with 8 q
+ * heads per kv head) are rejected with PD_ERR_WORKSPACE and a message in
+ * pd_last_error_string(); use pd_decode with a workspace for those.
+ *
+ * The array keeps whatever the previous call left; nothing in it has to start at zero (split
+ * rows are counted with per-launch epochs). All calls on one device share the array, so two
+ * calls whose kernels can overlap on the GPU (different streams without ordering between
+ * them) race and may return wrong results: issue them on one stream or order them.
+ */
+#define PD_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
+                      const void* k_cache, const void* v_cache, int64_t n_blocks,
+                      int32_t block_size, const int64_t* k_strides, const int64_t* v_strides,
+                      const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+                      const int32_t* seqlen, void* out, int64_t o_sb, int64_t o_sh,
+                      int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
+                      int32_t dtype, float scale_log2, void* stream);
+
 /* ---------------------------------------------------------------- decode plan
  *
  * pd_plan_* replaces `PagedDecodePlan` / `paged_decode_plan` (model/triton_decode.py:

@@ -646,4 +646,57 @@ int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_
   return PD_OK;
 }
 
+// ---------------------------------------------------------------- decode without allocation
+// Scratch for pd_decode_noalloc: a fixed array in this library's device image, so the call
+// never allocates. Host code must not use `g_noalloc_scratch` as an address -- on the host the
+// name stands for a shadow symbol, not device memory -- and instead passes the device address
+// that cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PD_NOALLOC_SCRATCH_BYTES];
+
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array on the current device, looked up on first use.
+static int noalloc_scratch(void** ptr) {
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "pd_decode_noalloc scratch lookup");
+    g_noalloc_ptr[dev] = p;
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return PD_OK;
+}
+
+int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache,
+                      const void* v_cache, int64_t n_blocks, int32_t block_size,
+                      const int64_t* k_strides, const int64_t* v_strides, const int32_t* block_table,
+                      int64_t bt_stride, int32_t max_blocks, const int32_t* seqlen, void* out,
+                      int64_t o_sb, int64_t o_sh, int32_t batch, int32_t n_head, int32_t n_kv_head,
+                      int32_t head_dim, int32_t dtype, float scale_log2, void* stream) {
+  const size_t need = pd_decode_workspace_bytes(batch, n_head, n_kv_head, head_dim, dtype);
+  if (need == 0) {
+    Geometry g;
+    const int st = geometry(n_head, n_kv_head, head_dim, block_size, dtype, &g);
+    return st != PD_OK ? st : PD_ERR_CUDA;
+  }
+  if (need > size_t(PD_NOALLOC_SCRATCH_BYTES)) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "pd_decode_noalloc: this shape needs %zu bytes of scratch but the built-in array "
+             "holds %u; call pd_decode with a workspace instead",
+             need, unsigned(PD_NOALLOC_SCRATCH_BYTES));
+    return PD_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != PD_OK) return st;
+  return decode_common(q, q_sb, q_sh, k_cache, v_cache, n_blocks, block_size, k_strides, v_strides,
+                       block_table, bt_stride, max_blocks, seqlen, out, o_sb, o_sh, nullptr, nullptr,
+                       nullptr, 0, batch, n_head, n_kv_head, head_dim, dtype, scale_log2, scratch,
+                       size_t(PD_NOALLOC_SCRATCH_BYTES), stream);
+}
+
 }  // extern "C"

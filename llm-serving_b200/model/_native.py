@@ -49,6 +49,12 @@ _SIGNATURES = {
          _c_i32, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_float,
          _c_ptr, _c_size, _c_ptr],
     ),
+    "pd_decode_noalloc": (
+        ctypes.c_int,
+        [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_ptr, _c_i64,
+         _c_i32, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_float,
+         _c_ptr],
+    ),
     "pd_decode_partials": (
         ctypes.c_int,
         [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_ptr, _c_i64,
@@ -183,6 +189,25 @@ def decode(q, k_cache, v_cache, block_table, seqlen, out, scale_log2, workspace)
         workspace.data_ptr(), workspace.numel(), stream_handle(q.device),
     )
     check(status, "pd_decode")
+
+
+def decode_noalloc(q, k_cache, v_cache, block_table, seqlen, out, scale_log2) -> None:
+    """pd_decode without a workspace: the library's built-in scratch array is used, and the
+    call allocates nothing (for hosts that cannot allocate device memory). Calls on one device
+    share that array, so keep them ordered on one stream."""
+    B, H, D = q.shape
+    _, bs, hkv, _ = k_cache.shape
+    status = require().pd_decode_noalloc(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0], bs,
+        strides3(k_cache), strides3(v_cache),
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        seqlen.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1),
+        B, H, hkv, D, dtype_code(q.dtype), float(scale_log2), stream_handle(q.device),
+    )
+    if status == PD_ERR_WORKSPACE:
+        raise ValueError(f"pd_decode_noalloc failed: {require().pd_last_error_string().decode()}")
+    check(status, "pd_decode_noalloc")
 
 
 def decode_partials(q, k_cache, v_cache, block_table, seqlen, m_out, l_out, acc_out, scale_log2,
