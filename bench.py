@@ -236,7 +236,7 @@ def run_gpu(args) -> dict | None:
     peaks = _peaks()
     achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
     gbs = total_bytes / (ms * 1e-3) / 1e9
-    traffic = _profiled_traffic()
+    traffic = _profiled_traffic(per_launch_bytes)
     line = {
         "metric": METRIC,
         "value": round(gbs, 1),
@@ -313,15 +313,16 @@ def _run_e2e(kv, device, stream, rank, steps, warmup, dist) -> dict:
             "us_per_layer_step": round(ms * 1e3 / (n * N_LAYER), 2)}
 
 
-def _profiled_traffic():
-    """DRAM bytes of one decode launch from the committed ncu summary (if present)."""
-    path = ROOT / "profiles" / "decode_config2_traffic.json"
-    if path.exists():
-        try:
-            return json.loads(path.read_text()).get("dram_bytes_per_launch")
-        except (ValueError, OSError):
-            return None
-    return None
+def _profiled_traffic(algorithmic_bytes: float):
+    """DRAM bytes of one decode launch: the ncu-measured ratio of DRAM bytes (read + write) to
+    algorithmic KV bytes on the config-2 profile case (profiles/decode_traffic.json), scaled
+    to this launch's algorithmic bytes (traffic grows with the KV bytes read)."""
+    path = ROOT / "profiles" / "decode_traffic.json"
+    try:
+        ratio = json.loads(path.read_text())["dram_over_algorithmic"]
+    except (OSError, ValueError, KeyError):
+        return None
+    return int(ratio * algorithmic_bytes)
 
 
 def _finish(dist):
@@ -392,14 +393,43 @@ def run_reference(args) -> dict | None:
     }
 
 
+def profile_case(name: str, launches: int = 4) -> None:
+    """A short, deterministic run for profilers: one layer of a benchmark config and
+    ``launches`` decode launches (plus one fused append), nothing else on the GPU afterwards."""
+    from model import _native
+    from model.triton_decode import paged_decode_plan
+    from serve import workloads
+
+    device = torch.device("cuda", 0)
+    wl = getattr(workloads, name)(device, n_layer=1)
+    plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
+    B = wl.q[0].shape[0]
+    hkv, d = wl.k_pools[0].shape[2], wl.k_pools[0].shape[3]
+    gen = torch.Generator(device=device).manual_seed(5)
+    k_new = torch.randn(B, hkv, d, generator=gen, device=device).to(wl.k_pools[0].dtype)
+    pos = (wl.seqlen.to(torch.int64) - 1).clamp_min(0)
+    _native.append_table(wl.k_pools[0], wl.v_pools[0], wl.block_table, pos, k_new, k_new)
+    for _ in range(launches):
+        plan.run(0, wl.q[0])
+    torch.cuda.synchronize()
+    if _native.device_error() != 0:
+        raise SystemExit("device error word set")
+    print(json.dumps({"profile_case": name, "launches": launches, "kv_bytes": wl.kv_bytes_per_layer()}))
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--profile-case", default=None,
+                        help="run a short profiler case (config1..config5) instead of the benchmark")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=100)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--cpu-sample-layers", type=int, default=2)
     args = parser.parse_args(argv)
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return 0
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     line = run_reference(args) if args.impl == "reference" else run_gpu(args)

@@ -99,19 +99,26 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, const int* pre, const 
   }
 }
 
-// Arrival on an item counter shared by the pieces of one split item; returns how many pieces
-// of this launch arrived before. The counter holds (epoch << 32) | count: a value written by
-// another launch (or never initialised) has another epoch and counts as zero, so workspaces
-// need no clearing between launches, whatever the previous launch's shape.
-__device__ __forceinline__ int arrive_epoch(unsigned long long* counter, uint32_t epoch) {
-  unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(counter);
+// Arrival on the counter shared by the pieces of one split item; returns how many pieces of
+// this launch arrived before. Counters live in workspace memory that is never cleared and hold
+// (epoch << 32) | count. Every launch re-tags its item counters with its own epoch in the
+// prologue (each CTA a share of them), so an arrival is one atomicAdd with no contention
+// beyond the hardware's. An arrival that beats its counter's re-tag sees another epoch; its
+// add lands on a value the re-tag overwrites, so it waits for the re-tag and adds again
+// (bounded: on expiry it records DEVERR_WAIT_TIMEOUT and returns -1, i.e. "not last").
+__device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t epoch, unsigned* err) {
+  unsigned long long t0 = 0;
   for (;;) {
-    const bool mine = uint32_t(seen >> 32) == epoch;
-    const unsigned long long want =
-        mine ? seen + 1ull : ((unsigned long long)epoch << 32) | 1ull;
-    const unsigned long long prev = atomicCAS(counter, seen, want);
-    if (prev == seen) return mine ? int(uint32_t(seen)) : 0;
-    seen = prev;
+    const unsigned long long old = atomicAdd(counter, 1ull);
+    if (uint32_t(old >> 32) == epoch) return int(uint32_t(old));
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > WAIT_LIMIT_NS) {
+      atomicOr(err, DEVERR_WAIT_TIMEOUT);
+      return -1;
+    }
+    __nanosleep(128);
   }
 }
 
@@ -149,6 +156,13 @@ __global__ void __launch_bounds__(256, 1)
   if (tid == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
+  }
+  // Re-tag this launch's item counters with its epoch (this CTA's share of them).
+  {
+    const int64_t n_items = int64_t(B) * p.n_kv_head * p.n_gchunks;
+    const unsigned long long tag = (unsigned long long)p.epoch << 32;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < n_items; i += int64_t(gridDim.x) * blockDim.x)
+      atomicExch(p.counters + i, tag);
   }
 
   // ---- prologue: clamp lengths, tiles per row, block-wide exclusive scan -------------
@@ -633,31 +647,52 @@ __global__ void __launch_bounds__(256, 1)
         const int c_first = worker_of(us, units, workers);
         const int c_last = worker_of(ue - 1, units, workers);
         int ticket = 0;
-        if (lane == 0) ticket = arrive_epoch(p.counters + item_global, p.epoch);
+        if (lane == 0) ticket = take_ticket(p.counters + item_global, p.epoch, p.err);
         ticket = __shfl_sync(FULL_MASK, ticket, 0);
         if (ticket == c_last - c_first) {
           __threadfence();
-          // Merge the (c_last - c_first + 1) pieces of this item.
+          // Merge the (c_last - c_first + 1) pieces of this item in one pass: lane i holds
+          // piece i's (m, l); the max, the weights 2^(m_i - M) and the normaliser come from
+          // shuffles, and the accumulators of all pieces are loaded back to back.
           const int64_t first_start = int64_t(c_first) * units / workers;
           const int64_t first_slot = int64_t(c_first) * 2 + (first_start == us ? 0 : 1);
           auto slot_of = [&](int c) -> int64_t { return c == c_first ? first_slot : int64_t(c) * 2; };
-          float M[GT];
+          const int npieces = c_last - c_first + 1;
+          float M[GT], Lsum[GT], wv[GT];
 #pragma unroll
-          for (int g = 0; g < GT; ++g) M[g] = -INFINITY;
-          for (int c = c_first + lane; c <= c_last; c += 32) {
+          for (int g = 0; g < GT; ++g) {
+            M[g] = -INFINITY;
+            Lsum[g] = 0.f;
+            wv[g] = 0.f;
+          }
+          float mv[GT], lv[GT];
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            mv[g] = -INFINITY;
+            lv[g] = 0.f;
+          }
+          if (lane < npieces) {
+            const float* sm = p.ws_ml + slot_of(c_first + lane) * (2 * GT);
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+              mv[g] = __ldcg(sm + g);
+              lv[g] = __ldcg(sm + GT + g);
+            }
+          }
+          for (int c = c_first + 32 + lane; c <= c_last; c += 32) {  // more than 32 pieces: rare
             const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
 #pragma unroll
             for (int g = 0; g < GT; ++g) M[g] = fmaxf(M[g], __ldcg(sm + g));
           }
 #pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) {
+          for (int g = 0; g < GT; ++g) {
+            M[g] = fmaxf(M[g], mv[g]);
 #pragma unroll
-            for (int g = 0; g < GT; ++g) M[g] = fmaxf(M[g], __shfl_xor_sync(FULL_MASK, M[g], o));
+            for (int o = 16; o >= 1; o >>= 1) M[g] = fmaxf(M[g], __shfl_xor_sync(FULL_MASK, M[g], o));
+            wv[g] = lane < npieces ? exp2f(mv[g] - M[g]) : 0.f;
+            Lsum[g] = lv[g] * wv[g];
           }
-          float Lsum[GT];
-#pragma unroll
-          for (int g = 0; g < GT; ++g) Lsum[g] = 0.f;
-          for (int c = c_first + lane; c <= c_last; c += 32) {
+          for (int c = c_first + 32 + lane; c <= c_last; c += 32) {
             const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
 #pragma unroll
             for (int g = 0; g < GT; ++g) Lsum[g] += __ldcg(sm + GT + g) * exp2f(__ldcg(sm + g) - M[g]);
@@ -668,23 +703,53 @@ __global__ void __launch_bounds__(256, 1)
             for (int g = 0; g < GT; ++g) Lsum[g] += __shfl_xor_sync(FULL_MASK, Lsum[g], o);
           }
           const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
-          for (int q4 = lane; q4 < GT * (D / 4); q4 += 32) {
+          // Every lane runs every iteration (the shuffles below are warp-wide); only lanes
+          // with a real output element store.
+          for (int base = 0; base < GT * (D / 4); base += 32) {
+            const bool active = base + lane < GT * (D / 4);
+            const int q4 = active ? base + lane : 0;
             const int g = q4 / (D / 4);
             const int d = (q4 - g * (D / 4)) * 4;
             float Mg = M[0], Lg = Lsum[0];
 #pragma unroll
             for (int gg = 1; gg < GT; ++gg)
               if (g == gg) { Mg = M[gg]; Lg = Lsum[gg]; }
+            // Pieces in batches of MB (8, or 4 for wide head groups to stay within the register
+            // budget): all loads of a batch are issued before any of them is used, so a merge
+            // costs ~npieces / MB L2 round trips instead of npieces.
+            constexpr int MB = (GT * C::EPL > 16) ? 4 : 8;
+            auto weight = [&](int i) -> float {  // 2^(m_i - M) of piece i for this lane's head
+              if (i < 32) {
+                float f = __shfl_sync(FULL_MASK, wv[0], i);
+#pragma unroll
+                for (int gg = 1; gg < GT; ++gg) {
+                  const float fg = __shfl_sync(FULL_MASK, wv[gg], i);
+                  if (g == gg) f = fg;
+                }
+                return f;
+              }
+              return exp2f(__ldcg(p.ws_ml + slot_of(c_first + i) * (2 * GT) + g) - Mg);
+            };
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c = c_first; c <= c_last; ++c) {
-              const int64_t sl = slot_of(c);
-              const float f = exp2f(__ldcg(p.ws_ml + sl * (2 * GT) + g) - Mg);
-              const float4 x = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D) + g * D + d));
-              a.x = fmaf(f, x.x, a.x);
-              a.y = fmaf(f, x.y, a.y);
-              a.z = fmaf(f, x.z, a.z);
-              a.w = fmaf(f, x.w, a.w);
+            for (int i0 = 0; i0 < npieces; i0 += MB) {
+              float4 x[MB];
+              float f[MB];
+#pragma unroll
+              for (int j = 0; j < MB; ++j) {
+                const int i = i0 + j < npieces ? i0 + j : npieces - 1;
+                x[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + slot_of(c_first + i) * (GT * D) + g * D + d));
+              }
+#pragma unroll
+              for (int j = 0; j < MB; ++j) f[j] = i0 + j < npieces ? weight(i0 + j) : 0.f;
+#pragma unroll
+              for (int j = 0; j < MB; ++j) {
+                a.x = fmaf(f[j], x[j].x, a.x);
+                a.y = fmaf(f[j], x[j].y, a.y);
+                a.z = fmaf(f[j], x[j].z, a.z);
+                a.w = fmaf(f[j], x[j].w, a.w);
+              }
             }
+            if (!active) continue;
             if (p.mode == 0) {
               const float inv = 1.f / fmaxf(Lg, 1.f);
               T* o = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb + int64_t(hq0 + g) * p.o_sh + d;
