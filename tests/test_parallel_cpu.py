@@ -5,7 +5,9 @@ runs, with the CPU oracle standing in for the two kernels (test-only injection).
   (acc | m | l) buffers are all-gathered, the LSE merge of all parts equals the oracle on the
   whole rows;
 * row sharding: the shards tile the batch and each rank's rows decode like the same rows
-  of the full batch.
+  of the full batch;
+* failure: a rank that leaves between steps (before the exchange) makes the surviving rank's
+  next exchange end with an error inside the process-group timeout instead of waiting forever.
 """
 
 from __future__ import annotations
@@ -91,6 +93,54 @@ def test_context_parallel_and_row_sharding_on_two_cpu_ranks():
         assert row_err == 0.0
         ranges.append(rows)
     assert ranges[0][0] == 0 and ranges[-1][1] == 6 and ranges[0][1] == ranges[1][0]
+
+
+def _leaving_worker(rank: int, world: int, port: int, results):
+    for path in (ROOT / "llm-serving_b200", ROOT, ROOT / "tests"):
+        sys.path.insert(0, str(path))
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from model.parallel_decode import ContextParallelDecode
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    dist.barrier()
+    if rank == 1:
+        os._exit(3)  # leaves between steps: nothing of it is in flight
+
+    def partials(q_, k_, v_, table_, seqlen_, m, l, acc, scale):
+        m.zero_(), l.zero_(), acc.zero_()
+
+    cp = ContextParallelDecode(partials=partials, merge=lambda *a: None)
+    q = torch.zeros(2, 4, 8)
+    try:
+        cp(q, None, None, None, None)
+        results[rank] = "no error"
+    except Exception as exc:  # noqa: BLE001 - the test inspects the type name
+        results[rank] = type(exc).__name__
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_ends_the_next_exchange_with_an_error():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert codes == [0, 3], codes
+    assert results[0] != "no error", "the exchange with a departed rank returned normally"
 
 
 def test_shard_helpers_tile_their_ranges():
