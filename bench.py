@@ -5,8 +5,10 @@ B=32 rows, every context at 2048 tokens, block size 16, 16 q / 8 kv heads, head_
 bf16, 28 per-layer pools of 4224 blocks (7.75 GB of K/V, far larger than the 126 MB L2, so
 every step reads cold HBM). One *step* = one decode step's attention for all 28 layers,
 exactly as ``MiniLLM.forward`` drives ``PagedKV``: ``build_mask`` (seqlen := pos + 1), then
-per layer ``write`` (fused paged-KV append of the new token) and ``attend`` (block-table
-decode), then ``advance``. The context grows by one token per step (2048 -> 2048 + steps).
+per layer ``write`` (records the new token) and ``attend`` (ONE launch that appends the
+token to the paged pool and runs the block-table decode over it), then ``advance``. The
+context grows by one token per step (2048 -> 2048 + steps). ``gpu_launches`` is the
+library's own launch counter over the timed region.
 
 Reported (``metric`` is BASELINE.json's): ``value`` = KV HBM GB/s of the decode kernels over
 the timed steps (sum of seqlen * 2 * H_kv * D * 2 B per layer-step, every rank, / max-over-
@@ -212,6 +214,7 @@ def run_gpu(args) -> dict | None:
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(N_LAYER)] for _ in range(steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(dist, device)
+    launches_before = _native.launch_count()
     with ClockSampler(local) as clocks:
         start.record(stream)
         for i in range(steps):
@@ -219,6 +222,7 @@ def run_gpu(args) -> dict | None:
             step(warmup + i, ev[i])
         stop.record(stream)
         _barrier(dist, device)
+    launches = _native.launch_count() - launches_before
     ms_local = start.elapsed_time(stop)
     decode_ms = sum(e[0].elapsed_time(e[1]) for st in ev for e in st)
     assert _native.device_error() == 0, "device error word set in the timed region"
@@ -255,7 +259,7 @@ def run_gpu(args) -> dict | None:
         "data": "synthetic (seeded N(0,1) K/V/q, random-init; no dataset on this path)",
         "config": {
             "workload": "BASELINE configs[1] attention path: 28-layer Qwen3-0.6B decode step through "
-                        "PagedKV (fused append + block-table decode per layer)",
+                        "PagedKV (append + block-table decode fused into one launch per layer)",
             "batch_per_gpu": BATCH, "context": f"{CONTEXT}+step", "layers": N_LAYER, "block_size": BS,
             "heads": f"{H}q/{H_KV}kv", "head_dim": D, "parallelism": f"rows sharded by sequence x{world}",
             "l2": "inputs larger than L2 (7.75 GB of per-layer pools per GPU; each layer reads 268 MB)",
@@ -267,7 +271,7 @@ def run_gpu(args) -> dict | None:
             "algorithmic_bytes_per_launch": int(per_launch_bytes),
         },
         "e2e": e2e,
-        "gpu_launches": steps * N_LAYER * 2,
+        "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
     line["cpu_baseline"] = cpu_baseline(sample_layers=args.cpu_sample_layers)
@@ -394,8 +398,9 @@ def run_reference(args) -> dict | None:
 
 
 def profile_case(name: str, launches: int = 4) -> None:
-    """A short, deterministic run for profilers: one layer of a benchmark config and
-    ``launches`` decode launches (plus one fused append), nothing else on the GPU afterwards."""
+    """A short, deterministic run for profilers: one layer of a benchmark config, one
+    stand-alone append and ``launches`` fused append + decode launches (the bench step's
+    kernel; each appends the same token again), nothing else on the GPU afterwards."""
     from model import _native
     from model.triton_decode import paged_decode_plan
     from serve import workloads
@@ -410,7 +415,7 @@ def profile_case(name: str, launches: int = 4) -> None:
     pos = (wl.seqlen.to(torch.int64) - 1).clamp_min(0)
     _native.append_table(wl.k_pools[0], wl.v_pools[0], wl.block_table, pos, k_new, k_new)
     for _ in range(launches):
-        plan.run(0, wl.q[0])
+        plan.run_append(0, wl.q[0], k_new, k_new, pos)
     torch.cuda.synchronize()
     if _native.device_error() != 0:
         raise SystemExit("device error word set")

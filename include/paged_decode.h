@@ -51,6 +51,10 @@ const char* pd_status_string(int status);
 /* Library ABI version (increments on any signature change). */
 int pd_abi_version(void);
 
+/* Number of kernels this library has launched in this process, over all devices and
+ * threads (a benchmark reports how many of its launches were this library's). */
+uint64_t pd_launch_count(void);
+
 /* Name and description of the last CUDA error a call on this thread returned as PD_ERR_CUDA
  * (static storage; "" when none). No reference counterpart: the Triton launch raises. */
 const char* pd_last_error_string(void);
@@ -146,6 +150,21 @@ int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
                    int32_t head_dim, int32_t dtype, float scale_log2, void* workspace,
                    size_t workspace_bytes);
 int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, void* stream);
+
+/* pd_plan_run_append -- `PagedKV.write(layer, k, v)` followed by `PagedKV.attend(layer, q)`
+ * (model/paged.py:503-557) in ONE launch. Row b's new K and V rows, k_new / v_new
+ * (B, H_kv, D) with element strides (k_sb, k_sh) / (v_sb, v_sh) in the plan's dtype and
+ * 16-byte aligned rows, are stored at logical position pos[b] (int64) of the row -- pool
+ * block block_table[b, pos / block_size], slot pos % block_size, exactly the slot
+ * pd_kv_append_table writes -- and the decode of the same launch attends over them.
+ * The result (out and the pools) equals pd_kv_append_table followed by pd_plan_run on the
+ * same stream, provided no row reads a slot another row appends in this call (blocks are
+ * not shared between rows for writing). A position outside the row's table or a block
+ * outside the pool is skipped and recorded as PD_DEVERR_APPEND_RANGE, as in the append.
+ */
+int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                       const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                       int64_t v_sb, int64_t v_sh, const int64_t* pos, void* stream);
 void pd_plan_destroy(pd_plan* plan);
 
 /* ---------------------------------------------------------------- split-KV partials

@@ -34,6 +34,9 @@ std::mutex g_mutex;
 
 thread_local char g_last_error[256] = "";
 
+// Kernels launched by this library in this process (pd_launch_count).
+std::atomic<unsigned long long> g_launches{0};
+
 // Launch ids for the split-item arrival counters: distinct per launch in this process, seeded
 // from the clock so a buffer left over from another process is unlikely to match.
 std::atomic<uint32_t> g_epoch{uint32_t(std::chrono::steady_clock::now().time_since_epoch().count()) | 1u};
@@ -159,7 +162,7 @@ struct Launch {
 
 size_t smem_for(int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
   const size_t bars = round_up(size_t(warps) * stages * 8, 16);
-  const size_t arrays = round_up(size_t(32 + 2 * rows + 1) * 4, 16);
+  const size_t arrays = round_up(size_t(32 + 3 * rows + 1) * 4, 16);
   *arrays_off = int(bars);
   *stage_off = int(bars + arrays);
   return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(warps) * stages * stage_bytes;
@@ -303,10 +306,25 @@ int check_rows(const void* ptr, int64_t sb, int64_t sh, int dtype) {
   return PD_OK;
 }
 
+// The new token of every row for a fused append + decode launch (pd_plan_run_append).
+struct AppendArgs {
+  const void* k;
+  int64_t k_sb, k_sh;
+  const void* v;
+  int64_t v_sb, v_sh;
+  const int64_t* pos;
+  void* pool_k;
+  void* pool_v;
+  const int64_t* k_strides;  // pool element strides: block, token, head
+  const int64_t* v_strides;
+  int64_t n_blocks;
+};
+
 // Launches the decode kernel over the batch in chunks of rows_per_launch rows.
 int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& vmap, const void* q,
                  int64_t q_sb, int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float* pm,
-                 float* pl, float* pacc, int mode, int dtype, cudaStream_t stream) {
+                 float* pl, float* pacc, int mode, int dtype, cudaStream_t stream,
+                 const AppendArgs* app = nullptr) {
   const int batch = P.base.batch;
   const int es = elem_size(dtype);
   for (int b0 = 0; b0 < batch; b0 += P.L.rows_per_launch) {
@@ -331,10 +349,30 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
     }
     if (P.base.table) p.table = P.base.table + int64_t(b0) * P.base.bt_stride;
     p.seqlen = P.base.seqlen + b0;
+    if (app != nullptr) {
+      p.append = 1;
+      p.app_k = static_cast<const unsigned char*>(app->k) + int64_t(b0) * app->k_sb * es;
+      p.app_v = static_cast<const unsigned char*>(app->v) + int64_t(b0) * app->v_sb * es;
+      p.app_k_sb = app->k_sb;
+      p.app_k_sh = app->k_sh;
+      p.app_v_sb = app->v_sb;
+      p.app_v_sh = app->v_sh;
+      p.app_pos = app->pos + b0;
+      p.pool_k = app->pool_k;
+      p.pool_v = app->pool_v;
+      p.pk_sb = app->k_strides[0];
+      p.pk_sn = app->k_strides[1];
+      p.pk_sh = app->k_strides[2];
+      p.pv_sb = app->v_strides[0];
+      p.pv_sn = app->v_strides[1];
+      p.pv_sh = app->v_strides[2];
+      p.n_blocks = app->n_blocks;
+    }
     const size_t smem = smem_for(P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
                                  &p.smem_stage_off);
     cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream);
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   return PD_OK;
 }
@@ -377,8 +415,12 @@ struct pd_plan {
   int32_t n_layer;
   int32_t dtype;
   int64_t q_sb, q_sh;
+  int64_t n_blocks;
+  int64_t k_strides[3], v_strides[3];
   std::vector<CUtensorMap> kmaps;
   std::vector<CUtensorMap> vmaps;
+  std::vector<void*> k_pools;  // for the fused append's stores
+  std::vector<void*> v_pools;
 };
 
 extern "C" {
@@ -395,6 +437,8 @@ const char* pd_status_string(int status) {
 }
 
 int pd_abi_version(void) { return kAbiVersion; }
+
+uint64_t pd_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* pd_last_error_string(void) { return g_last_error; }
 
@@ -474,9 +518,18 @@ int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
   h->dtype = dtype;
   h->q_sh = head_dim;
   h->q_sb = int64_t(n_head) * head_dim;
+  h->n_blocks = n_blocks;
+  for (int i = 0; i < 3; ++i) {
+    h->k_strides[i] = k_strides[i];
+    h->v_strides[i] = v_strides[i];
+  }
   h->kmaps.resize(n_layer);
   h->vmaps.resize(n_layer);
+  h->k_pools.resize(n_layer);
+  h->v_pools.resize(n_layer);
   for (int layer = 0; layer < n_layer; ++layer) {
+    h->k_pools[layer] = const_cast<void*>(k_caches[layer]);
+    h->v_pools[layer] = const_cast<void*>(v_caches[layer]);
     st = encode_pool(&h->kmaps[layer], k_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
                      k_strides, dtype, h->P.g.box_tokens);
     if (st == PD_OK)
@@ -498,6 +551,33 @@ int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, vo
   return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
                       plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
                       static_cast<cudaStream_t>(stream));
+}
+
+int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                       const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                       int64_t v_sb, int64_t v_sh, const int64_t* pos, void* stream) {
+  if (plan == nullptr || layer < 0 || layer >= plan->n_layer) return PD_ERR_INVALID;
+  if (check_rows(q, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  if (check_rows(out, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  if (check_rows(k_new, k_sb, k_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  if (check_rows(v_new, v_sb, v_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
+  if (pos == nullptr || (reinterpret_cast<uintptr_t>(pos) & 7u) != 0) return PD_ERR_INVALID;
+  AppendArgs app;
+  app.k = k_new;
+  app.k_sb = k_sb;
+  app.k_sh = k_sh;
+  app.v = v_new;
+  app.v_sb = v_sb;
+  app.v_sh = v_sh;
+  app.pos = pos;
+  app.pool_k = plan->k_pools[layer];
+  app.pool_v = plan->v_pools[layer];
+  app.k_strides = plan->k_strides;
+  app.v_strides = plan->v_strides;
+  app.n_blocks = plan->n_blocks;
+  return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
+                      plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
+                      static_cast<cudaStream_t>(stream), &app);
 }
 
 void pd_plan_destroy(pd_plan* plan) { delete plan; }
@@ -528,7 +608,9 @@ int pd_lse_merge(const float* m_parts, const float* l_parts, const float* acc_pa
   p.n_head = n_head;
   p.head_dim = head_dim;
   const cudaError_t e = launch_merge(p, dtype, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? PD_OK : cuda_fail(e, "merge launch");
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return PD_OK;
 }
 
 static int append_common(AppendParams& p, int32_t pool_dtype, int32_t src_dtype,
@@ -567,7 +649,9 @@ static int append_common(AppendParams& p, int32_t pool_dtype, int32_t src_dtype,
                    ok_dst(p.k_pool, p.kp_sb, p.kp_sn, p.kp_sh) &&
                    ok_dst(p.v_pool, p.vp_sb, p.vp_sn, p.vp_sh);
   cudaError_t e = launch_append(p, src_dtype, pool_dtype, vec, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? PD_OK : cuda_fail(e, "append launch");
+  if (e != cudaSuccess) return cuda_fail(e, "append launch");
+  if (p.n_tokens > 0) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return PD_OK;
 }
 
 int pd_kv_append_slots(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,

@@ -91,6 +91,12 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA)
+// accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -225,6 +231,21 @@ struct DecodeParams {
   int32_t smem_stage_off;
   float scale_log2;
   uint32_t epoch;  // launch id; a counter holding another epoch counts as zero
+  // Fused append (append != 0): before the decode reads them, row b's new K and V rows
+  // (app_k/app_v, same dtype as the pool, 16-byte aligned) are stored at logical position
+  // app_pos[b] of the row, i.e. pool block table[b, pos / bs], slot pos % bs, and the tile
+  // that covers that position takes the two rows from the source instead of from its TMA
+  // copy. Precondition: no other row of the launch reads an appended slot.
+  int32_t append;
+  const void* app_k;
+  const void* app_v;
+  int64_t app_k_sb, app_k_sh, app_v_sb, app_v_sh;
+  const int64_t* app_pos;
+  void* pool_k;
+  void* pool_v;
+  int64_t pk_sb, pk_sn, pk_sh;  // pool element strides: block, token, head
+  int64_t pv_sb, pv_sn, pv_sh;
+  int64_t n_blocks;
 };
 
 struct AppendParams {

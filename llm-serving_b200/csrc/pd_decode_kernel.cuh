@@ -143,12 +143,14 @@ __global__ void __launch_bounds__(256, 1)
   const int S = p.stages;
   const int B = p.batch;
 
-  // Dynamic shared memory: [mbarriers | warp_sums[32] | lens[B] | pre[B+1] | pad | stages].
+  // Dynamic shared memory:
+  // [mbarriers | warp_sums[32] | lens[B] | pre[B+1] | apos[B] | pad | stages].
   // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off);
   int* lens = warp_sums + 32;
   int* pre = lens + B;  // B + 1 entries: exclusive prefix of tiles per row
+  int* apos = pre + B + 1;  // fused append: position to take from the source, or -1
   const uint32_t smem_base = smem_addr(smem);
   unsigned char* stage_base =
       smem + (((smem_base + uint32_t(p.smem_stage_off) + 1023u) & ~1023u) - smem_base);
@@ -165,6 +167,41 @@ __global__ void __launch_bounds__(256, 1)
       atomicExch(p.counters + i, tag);
   }
 
+  // ---- fused append: store every row's new K/V rows in the pools (16 B per thread) -----
+  // Tiles read below may still see the old bytes of these slots (their TMA copies are not
+  // ordered after these stores); the consumer overwrites those rows from the source, so
+  // this launch's result never depends on which bytes a copy saw.
+  if (p.append) {
+    constexpr int CH = C::CHUNKS;
+    const int64_t tasks = int64_t(B) * p.n_kv_head * 2 * CH;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < tasks; i += int64_t(gridDim.x) * blockDim.x) {
+      const int c = int(i % CH);
+      int64_t r = i / CH;
+      const int kv = int(r & 1);
+      r >>= 1;
+      const int h = int(r % p.n_kv_head);
+      const int b = int(r / p.n_kv_head);
+      const int64_t pos = __ldg(p.app_pos + b);
+      const int64_t page = pos >= 0 ? (pos >> p.log2_bs) : -1;
+      const bool report = c == 0 && kv == 0 && h == 0;
+      if (page < 0 || page >= p.max_blocks) {
+        if (report) atomicOr(p.err, DEVERR_APPEND_RANGE);
+        continue;
+      }
+      const int64_t blk = __ldg(p.table + int64_t(b) * p.bt_stride + page);
+      if (blk < 0 || blk >= p.n_blocks) {
+        if (report) atomicOr(p.err, DEVERR_APPEND_RANGE);
+        continue;
+      }
+      const int64_t off = pos & (p.block_size - 1);
+      const T* src = kv ? reinterpret_cast<const T*>(p.app_v) + int64_t(b) * p.app_v_sb + int64_t(h) * p.app_v_sh
+                        : reinterpret_cast<const T*>(p.app_k) + int64_t(b) * p.app_k_sb + int64_t(h) * p.app_k_sh;
+      T* dst = kv ? reinterpret_cast<T*>(p.pool_v) + blk * p.pv_sb + off * p.pv_sn + int64_t(h) * p.pv_sh
+                  : reinterpret_cast<T*>(p.pool_k) + blk * p.pk_sb + off * p.pk_sn + int64_t(h) * p.pk_sh;
+      *reinterpret_cast<uint4*>(dst + c * C::EPC) = __ldg(reinterpret_cast<const uint4*>(src + c * C::EPC));
+    }
+  }
+
   // ---- prologue: clamp lengths, tiles per row, block-wide exclusive scan -------------
   {
     const int per = (B + blockDim.x - 1) / blockDim.x;
@@ -175,6 +212,17 @@ __global__ void __launch_bounds__(256, 1)
       int len = __ldg(p.seqlen + b);
       len = len < 0 ? 0 : (len > p.capacity ? p.capacity : len);
       lens[b] = len;
+      if (p.append) {
+        // The appended token is read from the source only if the row reads it at all and
+        // its slot was written above (a position inside the table, a block inside the pool).
+        const int64_t pos = __ldg(p.app_pos + b);
+        int ap = -1;
+        if (pos >= 0 && pos < len) {
+          const int64_t blk = __ldg(p.table + int64_t(b) * p.bt_stride + (pos >> p.log2_bs));
+          if (blk >= 0 && blk < p.n_blocks) ap = int(pos);
+        }
+        apos[b] = ap;
+      }
       local += (len + C::TILE - 1) >> C::LOG_TILE;
     }
     int incl = local;
@@ -498,6 +546,27 @@ __global__ void __launch_bounds__(256, 1)
     }
   };
 
+  // Fused append: after tile c's copies landed in `stage`, overwrite the appended token's
+  // K and V rows with the source rows (16 B per lane), so the tile holds the new token
+  // whatever the copy read from the pool.
+  auto patch = [&](const Cursor& c, int stage) {
+    if (!p.append) return;
+    const int ap = apos[c.b];
+    if (ap < 0 || (ap >> C::LOG_TILE) != c.tile) return;
+    unsigned char* krow = my_stages + size_t(stage) * C::STAGE_BYTES + (ap & (C::TILE - 1)) * C::ROW_BYTES;
+    unsigned char* vrow = krow + C::TILE_BYTES;
+    const T* ksrc = reinterpret_cast<const T*>(p.app_k) + int64_t(c.b) * p.app_k_sb + int64_t(c.h) * p.app_k_sh;
+    const T* vsrc = reinterpret_cast<const T*>(p.app_v) + int64_t(c.b) * p.app_v_sb + int64_t(c.h) * p.app_v_sh;
+    for (int i = lane; i < 2 * C::CHUNKS; i += 32) {
+      const bool isv = i >= C::CHUNKS;
+      const int ci = isv ? i - C::CHUNKS : i;
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>((isv ? vsrc : ksrc) + ci * C::EPC));
+      *reinterpret_cast<uint4*>((isv ? vrow : krow) + ci * 16) = x;
+    }
+    fence_proxy_async_smem();  // the stage is refilled by TMA later
+    __syncwarp();
+  };
+
   auto fail_and_drain = [&](int64_t from) {
     if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
     for (int64_t j = from; j < issued; ++j)
@@ -512,6 +581,7 @@ __global__ void __launch_bounds__(256, 1)
     fail_and_drain(0);
     return;
   }
+  patch(cur, 0);
   start_segment(cur);
   seg_first_tile = cur.tile;
   tile_scores(0, cur.len - (cur.tile << C::LOG_TILE), sc_cur);
@@ -522,9 +592,12 @@ __global__ void __launch_bounds__(256, 1)
     cursor_advance(nxt, pre, lens, B, items_per_row, p.n_gchunks);
     const int s_n = s + 1 == S ? 0 : s + 1;
     const uint32_t parity_n = s + 1 == S ? parity ^ 1u : parity;
-    if (has_next && !warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
-      fail_and_drain(k + 1);
-      return;
+    if (has_next) {
+      if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
+        fail_and_drain(k + 1);
+        return;
+      }
+      patch(nxt, s_n);
     }
     const int tok0 = cur.tile << C::LOG_TILE;
     const int valid_rows = cur.len - tok0;  // rows [0, valid_rows) of tile k are live

@@ -40,6 +40,7 @@ _c_float = ctypes.c_float
 _SIGNATURES = {
     "pd_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "pd_abi_version": (ctypes.c_int, []),
+    "pd_launch_count": (ctypes.c_uint64, []),
     "pd_last_error_string": (ctypes.c_char_p, []),
     "pd_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
     "pd_decode_workspace_bytes": (_c_size, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
@@ -73,6 +74,10 @@ _SIGNATURES = {
          _c_i32, _c_float, _c_ptr, _c_size],
     ),
     "pd_plan_run": (ctypes.c_int, [_c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr]),
+    "pd_plan_run_append": (
+        ctypes.c_int,
+        [_c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr],
+    ),
     "pd_plan_destroy": (None, [_c_ptr]),
     "pd_kv_append_slots": (
         ctypes.c_int,
@@ -148,6 +153,11 @@ def strides3(t: torch.Tensor):
     """The (dim0, dim1, dim2) element strides of a 4-D pool or 3-D row tensor as int64[3]."""
     s = t.stride()
     return (_c_i64 * 3)(*(int(x) for x in s[:3]))
+
+
+def launch_count() -> int:
+    """Kernels this library launched in this process so far."""
+    return int(require().pd_launch_count())
 
 
 def log2e_scale(scale: float) -> float:
@@ -291,6 +301,15 @@ class NativePlan:
         status = self._lib.pd_plan_run(self._handle, layer, q.data_ptr(), out.data_ptr(), stream)
         if status:
             check(status, "pd_plan_run")
+
+    def run_append(self, layer: int, q, out, k_new, v_new, pos, stream: int) -> None:
+        """Append ``k_new``/``v_new`` ``(B, H_kv, D)`` at ``pos`` (int64) and decode, one launch."""
+        status = self._lib.pd_plan_run_append(
+            self._handle, layer, q.data_ptr(), out.data_ptr(), k_new.data_ptr(), k_new.stride(0),
+            k_new.stride(1), v_new.data_ptr(), v_new.stride(0), v_new.stride(1), pos.data_ptr(), stream,
+        )
+        if status:
+            check(status, "pd_plan_run_append")
 
     def __del__(self) -> None:
         handle = getattr(self, "_handle", None)

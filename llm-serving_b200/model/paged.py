@@ -6,10 +6,14 @@ scheduler and model layers call it unchanged. What changed is underneath:
 
 * ``PagedPool.write_slots`` (prefill and decode writes) is one launch of the append kernel
   (``pd_kv_append_slots``) that moves K and V together, instead of two ``index_copy_``.
-* ``PagedKV.write`` is one launch of the fused append (``pd_kv_append_table``): the kernel
-  derives each row's slot ``table[row, pos // bs] * bs + pos % bs`` itself from the int32
-  block table and the int64 ``pos`` vector, so no device slot map is built per step.
-* ``PagedKV.attend`` launches the decode plan of :mod:`model.triton_decode`.
+* ``PagedKV.write`` + ``PagedKV.attend`` of one layer are ONE launch
+  (``pd_plan_run_append``): ``write`` validates and records the step's K/V, and the decode
+  launch of ``attend`` first stores them at ``table[row, pos // bs] * bs + pos % bs`` and then
+  attends over them. Anything else that touches the pool before that ``attend`` -- reading
+  ``PagedPool.keys`` / ``values``, another write, ``build_mask``, ``advance``, ``flush`` --
+  first performs the recorded append as its own launch (``pd_kv_append_table``), so every
+  observer sees the same pool as with an immediate write. ``PagedKV(..., fuse_append=False)``
+  always writes immediately.
 
 Layout (unchanged): one ``(n_blocks, block_size, n_kv_head, head_dim)`` K and V tensor per
 layer, allocated once and never replaced; token ``t`` of a request lives at block
@@ -71,14 +75,40 @@ class PagedPool:
         self.dtype = dtype
         self.device = torch.device(device)
         shape = (self.n_blocks, self.block_size, self.n_kv_head, self.head_dim)
-        self.keys = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
-        self.values = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
+        self._keys = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
+        self._values = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(self.n_layer)]
         # Flat (n_blocks * block_size, n_kv_head, head_dim) views: a slot id is a row of these.
-        self._keys_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self.keys]
-        self._values_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self.values]
+        self._keys_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self._keys]
+        self._values_flat = [t.view(-1, self.n_kv_head, self.head_dim) for t in self._values]
+        # A decode-step append recorded by PagedKV.write and not yet launched (see flush).
+        self._pending = None
         # One-entry cache of the prefill slot map keyed by (table, start, length).
         self._prefill_key: tuple | None = None
         self._prefill_slots: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------ pool tensors
+    @property
+    def keys(self) -> list[torch.Tensor]:
+        """Per-layer K pools. Reading them first performs a recorded append (:meth:`flush`)."""
+        self.flush()
+        return self._keys
+
+    @property
+    def values(self) -> list[torch.Tensor]:
+        """Per-layer V pools. Reading them first performs a recorded append (:meth:`flush`)."""
+        self.flush()
+        return self._values
+
+    def flush(self) -> None:
+        """Launch the decode-step append that ``PagedKV.write`` recorded, if any, on the
+        stream it was recorded on. Afterwards the pools hold every written token."""
+        pending, self._pending = self._pending, None
+        if pending is not None:
+            pending.launch()
+
+    def _record(self, pending) -> None:
+        self.flush()
+        self._pending = pending
 
     # ------------------------------------------------------------------ checks
     def _check_layer(self, layer: int) -> int:
@@ -164,8 +194,9 @@ class PagedPool:
                 raise ValueError(f"{name} dtype must be fp32, fp16 or bf16, got {t.dtype}")
         if k.shape[0] == 0:
             return
-        with torch.cuda.device(self.keys[layer].device):
-            _native.append_slots(self.keys[layer], self.values[layer], slot_ids.contiguous(),
+        self.flush()
+        with torch.cuda.device(self._keys[layer].device):
+            _native.append_slots(self._keys[layer], self._values[layer], slot_ids.contiguous(),
                                  _unit_last_stride(k), _unit_last_stride(v.to(k.dtype)))
 
     def write_prefill_slots(self, layer: int, slot_ids: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -194,6 +225,27 @@ class PagedPool:
         return self.bytes() / 2**20
 
 
+class _PendingAppend:
+    """One decode-step append recorded by :meth:`PagedKV.write`: consumed by the fused launch
+    of the same layer's ``attend``, or launched alone by :meth:`PagedPool.flush`."""
+
+    __slots__ = ("owner", "layer", "k", "v", "stream")
+
+    def __init__(self, owner: "PagedKV", layer: int, k: torch.Tensor, v: torch.Tensor, stream) -> None:
+        self.owner, self.layer, self.k, self.v, self.stream = owner, layer, k, v, stream
+
+    def launch(self) -> None:
+        with torch.cuda.stream(self.stream):
+            self.owner._append_now(self.layer, self.k, self.v)
+
+
+def _fusable_rows(t: torch.Tensor, dtype: torch.dtype) -> bool:
+    """(B, H_kv, D) rows the fused append reads directly: pool dtype, 16-byte aligned rows."""
+    es = t.element_size()
+    return (t.dtype == dtype and t.stride(2) == 1 and (t.stride(0) * es) % 16 == 0
+            and (t.stride(1) * es) % 16 == 0 and t.data_ptr() % 16 == 0)
+
+
 class PagedKV:
     """Decode-time container over a :class:`PagedPool` (the ``KvSlab`` step protocol).
 
@@ -208,7 +260,7 @@ class PagedKV:
     block_table_decode = True
 
     def __init__(self, pool: PagedPool, block_tables, lengths, *, rope_len: int, seats=None,
-                 n_head: int | None = None, check_bounds: bool = True) -> None:
+                 n_head: int | None = None, check_bounds: bool = True, fuse_append: bool = True) -> None:
         if not isinstance(pool, PagedPool):
             raise TypeError(f"PagedKV needs a PagedPool, got {type(pool).__name__}")
         if pool.device.type != "cuda":
@@ -284,10 +336,15 @@ class PagedKV:
         self._decode_plan = None
         self._step_written = False
         self._seqlen_ready = False
+        # The fused append + decode launch needs rows that never share a block (a row must not
+        # read a slot another row appends); tables from BlockManager never do.
+        owned = [b for table in self.block_tables for b in table]
+        self.fuse_append = bool(fuse_append) and len(owned) == len(set(owned))
 
     # ---------------------------------------------------------------- step hooks
     def build_mask(self, *, next_token: bool = False) -> None:
         """Step boundary: ``seqlen := pos + next_token`` as int32, in place (no mask/bias)."""
+        self.pool.flush()
         longest = max(n + int(next_token) for n in self._host_valid)
         if self.check_bounds and longest > self.max_len:
             raise IndexError(f"PagedKV overflow: needs {longest} positions, run position bound is {self.max_len}")
@@ -340,11 +397,23 @@ class PagedKV:
                 raise ValueError(f"{name} dtype must be fp32, fp16 or bf16, got {t.dtype}")
             if not _same_device(t.device, self.device):
                 raise ValueError(f"{name} on {t.device} but the pool is on {self.device}")
-        with torch.cuda.device(self.pool.keys[layer].device):
-            _native.append_table(self.pool.keys[layer], self.pool.values[layer], self._block_table_tensor,
-                                 self.pos, _unit_last_stride(k[:, :, 0, :]),
-                                 _unit_last_stride(v[:, :, 0, :].to(k.dtype)))
+        k3, v3 = k[:, :, 0, :], v[:, :, 0, :]
+        if self.fuse_append and _fusable_rows(k3, self.dtype) and _fusable_rows(v3, self.dtype):
+            self.pool._record(_PendingAppend(self, layer, k3, v3, torch.cuda.current_stream(self.device)))
+        else:
+            self.pool.flush()
+            self._append_now(layer, k3, v3)
         self._step_written = True
+
+    def _append_now(self, layer: int, k3: torch.Tensor, v3: torch.Tensor) -> None:
+        """The append alone: one ``pd_kv_append_table`` launch on the current stream."""
+        with torch.cuda.device(self.pool._keys[layer].device):
+            _native.append_table(self.pool._keys[layer], self.pool._values[layer], self._block_table_tensor,
+                                 self.pos, _unit_last_stride(k3), _unit_last_stride(v3.to(k3.dtype)))
+
+    def flush(self) -> None:
+        """Perform a recorded append now (see :meth:`PagedPool.flush`)."""
+        self.pool.flush()
 
     def attend(self, layer: int, q: torch.Tensor, *, dropout_p: float = 0.0) -> torch.Tensor:
         """Block-table decode for one layer; ``q`` is ``(B, H, 1, D)``, output the same."""
@@ -362,13 +431,21 @@ class PagedKV:
         q3 = q[:, :, 0, :].contiguous()
         if self._decode_plan is None:
             self._decode_plan = paged_decode_plan(
-                q3, self.pool.keys, self.pool.values, self._block_table_tensor, self._seqlen,
+                q3, self.pool._keys, self.pool._values, self._block_table_tensor, self._seqlen,
                 scale=1.0 / (self.head_dim ** 0.5),
             )
+        pending = self.pool._pending
+        if (pending is not None and pending.owner is self and pending.layer == int(layer)
+                and pending.stream == torch.cuda.current_stream(self.device)
+                and self._decode_plan.can_fuse_append(pending.k, pending.v, self.pos)):
+            self.pool._pending = None
+            return self._decode_plan.run_append(layer, q3, pending.k, pending.v, self.pos).unsqueeze(2)
+        self.pool.flush()
         return self._decode_plan.run(layer, q3).unsqueeze(2)
 
     def advance(self) -> None:
         """Move every active row's cursor one token (device in place, then host mirrors)."""
+        self.pool.flush()
         self.pos.add_(self.active)
         self.valid.copy_(torch.maximum(self.valid, self.pos))
         for row in range(self.batch):

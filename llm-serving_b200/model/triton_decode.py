@@ -302,8 +302,7 @@ class PagedDecodePlan:
             )
         self._stream_cache = None
 
-    def run(self, layer: int, q):
-        """Launch the kernel for one layer; ``q`` must match the validated layout."""
+    def _check_query(self, layer: int, q) -> int:
         if not 0 <= int(layer) < self.n_layer:
             raise IndexError(f"layer {layer} outside the plan's {self.n_layer} layers")
         if (
@@ -317,8 +316,47 @@ class PagedDecodePlan:
                 f"{(self.q_shape, self.q_dtype, self.q_strides)}; got "
                 f"{(tuple(q.shape), q.dtype, q.stride())}. Rebuild the plan for a new layout."
             )
+        return int(layer)
+
+    def run(self, layer: int, q):
+        """Launch the kernel for one layer; ``q`` must match the validated layout."""
+        layer = self._check_query(layer, q)
         out = torch.empty_like(q)
-        self._native_plan.run(int(layer), q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
+        self._native_plan.run(layer, q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
+        return out
+
+    def can_fuse_append(self, k_new, v_new, pos) -> bool:
+        """Whether :meth:`run_append` takes these tensors: ``(B, H_kv, D)`` rows in the plan's
+        dtype on its device with a unit last stride and 16-byte aligned rows, and an int64
+        ``(B,)`` contiguous ``pos``."""
+        b, _, d = self.q_shape
+        shape = (b, self._k[0].shape[2], d)
+        es = self._k[0].element_size()
+        for t in (k_new, v_new):
+            if tuple(t.shape) != shape or t.dtype != self.q_dtype or t.device != self.q_device:
+                return False
+            if t.stride(2) != 1 or (t.stride(0) * es) % 16 or (t.stride(1) * es) % 16 or t.data_ptr() % 16:
+                return False
+        return (pos.dtype == torch.int64 and tuple(pos.shape) == (b,) and pos.device == self.q_device
+                and pos.stride(0) == 1)
+
+    def run_append(self, layer: int, q, k_new, v_new, pos):
+        """Store row ``b``'s new K/V ``(B, H_kv, D)`` at logical position ``pos[b]`` of layer
+        ``layer``'s pools and decode that layer, in one launch.
+
+        Same result as ``PagedKV.write`` followed by :meth:`run` -- the pools and the output
+        are bit-identical -- provided no row reads a slot another row appends (rows do not
+        share blocks they write). Tensors must pass :meth:`can_fuse_append`.
+        """
+        layer = self._check_query(layer, q)
+        if not self.can_fuse_append(k_new, v_new, pos):
+            raise ValueError(
+                "paged_decode_plan.run_append needs (B, H_kv, D) k/v rows in the plan's dtype with "
+                "16-byte aligned rows and an int64 (B,) pos on the plan's device"
+            )
+        out = torch.empty_like(q)
+        self._native_plan.run_append(layer, q, out, k_new, v_new, pos,
+                                     torch.cuda.current_stream(self.q_device).cuda_stream)
         return out
 
 
