@@ -78,8 +78,9 @@ int pd_device_error(unsigned int* bits, int clear);
  *   scale_log2 = scale * log2(e)  (model/triton_decode.py:291-292)
  *   workspace: device memory of at least pd_decode_workspace_bytes(...) bytes, 256-byte
  *     aligned, with arbitrary contents (no clearing needed: split rows are counted with
- *     per-launch epochs). One workspace must not be used by two launches that may run
- *     concurrently.
+ *     per-launch epochs that the kernel keeps in the workspace and advances itself, so
+ *     launches replayed from a captured CUDA graph stay correct). One workspace must not be
+ *     used by two launches that may run concurrently.
  *
  * Row b, head h reads only the first ceil(seqlen[b] / block_size) table entries;
  * zero-length rows produce exact zeros (model/triton_decode.py:639).

@@ -4,7 +4,6 @@
 // launch-shape selection and the plan handle. All device work is in pd_decode_*.cu,
 // pd_append.cu and pd_merge.cu.
 #include <atomic>
-#include <chrono>
 #include <cstdio>
 #include <mutex>
 #include <new>
@@ -36,15 +35,6 @@ thread_local char g_last_error[256] = "";
 
 // Kernels launched by this library in this process (pd_launch_count).
 std::atomic<unsigned long long> g_launches{0};
-
-// Launch ids for the split-item arrival counters: distinct per launch in this process, seeded
-// from the clock so a buffer left over from another process is unlikely to match.
-std::atomic<uint32_t> g_epoch{uint32_t(std::chrono::steady_clock::now().time_since_epoch().count()) | 1u};
-
-uint32_t next_epoch() {
-  uint32_t e = g_epoch.fetch_add(1, std::memory_order_relaxed);
-  return e == 0 ? g_epoch.fetch_add(1, std::memory_order_relaxed) : e;
-}
 
 // Records a failed CUDA call for pd_last_error_string and returns PD_ERR_CUDA.
 int cuda_fail(cudaError_t e, const char* where) {
@@ -162,7 +152,7 @@ struct Launch {
 
 size_t smem_for(int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
   const size_t bars = round_up(size_t(warps) * stages * 8, 16);
-  const size_t arrays = round_up(size_t(32 + 3 * rows + 1) * 4, 16);
+  const size_t arrays = round_up(size_t(1 + 32 + 3 * rows + 1) * 4, 16);
   *arrays_off = int(bars);
   *stage_off = int(bars + arrays);
   return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(warps) * stages * stage_bytes;
@@ -192,8 +182,11 @@ int launch_shape(int dev, int batch, const Geometry& g, Launch* L) {
   return PD_OK;
 }
 
+// Workspace: [header 256 B: epoch word (u32) at 0, exit counter (u64) at 8 | item arrival
+// counters (u64) | partial (m, l) slots | partial accumulator slots]. The header is the
+// kernel's own launch bookkeeping; nothing in the workspace needs to start at zero.
 struct WorkspaceLayout {
-  size_t counters;  // bytes
+  size_t counters_off;
   size_t ml_off, acc_off, total;
 };
 
@@ -201,9 +194,9 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
                                  const Launch& L) {
   WorkspaceLayout w;
   const int rows = batch < L.rows_per_launch ? batch : L.rows_per_launch;
-  w.counters = round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 8, 256);
+  w.counters_off = 256;
   const size_t workers = size_t(L.grid) * L.warps;
-  w.ml_off = w.counters;
+  w.ml_off = w.counters_off + round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 8, 256);
   w.acc_off = w.ml_off + round_up(workers * 2 * 2 * g.gt * 4, 256);
   w.total = w.acc_off + round_up(workers * 2 * size_t(g.gt) * head_dim * 4, 256);
   return w;
@@ -276,7 +269,9 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   p.bt_stride = bt_stride;
   p.seqlen = seqlen;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  p.counters = reinterpret_cast<unsigned long long*>(ws);
+  p.epoch_word = reinterpret_cast<unsigned*>(ws);
+  p.exit_counter = reinterpret_cast<unsigned long long*>(ws + 8);
+  p.counters = reinterpret_cast<unsigned long long*>(ws + P->ws.counters_off);
   p.ws_ml = reinterpret_cast<float*>(ws + P->ws.ml_off);
   p.ws_acc = reinterpret_cast<float*>(ws + P->ws.acc_off);
   p.err = err;
@@ -332,7 +327,6 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
     DecodeParams p = P.base;
     p.batch = rows;
     p.mode = mode;
-    p.epoch = next_epoch();
     p.q = static_cast<const unsigned char*>(q) + int64_t(b0) * q_sb * es;
     p.q_sb = q_sb;
     p.q_sh = q_sh;

@@ -230,7 +230,12 @@ struct DecodeParams {
   int32_t smem_arrays_off;
   int32_t smem_stage_off;
   float scale_log2;
-  uint32_t epoch;  // launch id; a counter holding another epoch counts as zero
+  // Launch id ("epoch") bookkeeping in the workspace header. Each launch reads its epoch
+  // from *epoch_word; the last of its warps to leave (counted on *exit_counter, tagged like
+  // the item counters) stores epoch + 1 there, so consecutive launches on one workspace --
+  // replays of a captured CUDA graph included -- never share an epoch.
+  unsigned* epoch_word;
+  unsigned long long* exit_counter;
   // Fused append (append != 0): before the decode reads them, row b's new K and V rows
   // (app_k/app_v, same dtype as the pool, 16-byte aligned) are stored at logical position
   // app_pos[b] of the row, i.e. pool block table[b, pos / bs], slot pos % bs, and the tile

@@ -25,8 +25,10 @@
 //    heads this is a GEMV at 2 flop/byte and the HBM stream is the roof.
 //  * A worker whose range covers a whole item writes the output directly. A split item
 //    leaves (m, l, acc) in the workspace; the last of its workers to finish (arrival
-//    counter, __threadfence) merges the pieces with the log-sum-exp rule and resets the
-//    counter, so split-KV costs no extra launch.
+//    counter, __threadfence) merges the pieces with the log-sum-exp rule, so split-KV costs
+//    no extra launch. Counters are tagged with the launch's epoch, which the kernel keeps in
+//    the workspace header and advances itself when its last warp leaves: the workspace never
+//    needs clearing, and a launch replayed from a CUDA graph gets a fresh epoch every time.
 //  * Block-table entries are fetched 32 at a time into one register per lane (plus the
 //    next 32 prefetched), so a TMA issue never waits on a dependent global load inside a
 //    row. Table entries past ceil(seqlen / bs) are never read; an entry outside the pool
@@ -122,20 +124,45 @@ __device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t
   }
 }
 
+// Leaving the launch (lane 0 of every warp, on every path): one arrival on the exit counter.
+// The last of the launch's `total_warps` arrivals advances the workspace epoch for the next
+// launch. An arrival that beats CTA 0's re-tag of the counter sees another epoch; like
+// take_ticket it waits (bounded) for the re-tag and arrives again.
+__device__ __forceinline__ void leave_launch(unsigned long long* exit_counter, unsigned* epoch_word,
+                                             uint32_t epoch, unsigned total_warps, unsigned* err) {
+  unsigned long long t0 = 0;
+  for (;;) {
+    const unsigned long long old = atomicAdd(exit_counter, 1ull);
+    if (uint32_t(old >> 32) == epoch) {
+      if (uint32_t(old) == total_warps - 1u) atomicExch(epoch_word, epoch + 1u);
+      return;
+    }
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > WAIT_LIMIT_NS) {
+      atomicOr(err, DEVERR_WAIT_TIMEOUT);
+      return;
+    }
+    __nanosleep(128);
+  }
+}
+
 // Worker that owns unit u when `units` units are cut into `workers` ranges
 // [w*units/workers, (w+1)*units/workers).
 __device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) {
   return int(((u + 1) * int64_t(workers) - 1) / units);
 }
 
+// One launch's work for this thread's warp. It returns on several paths (no work, a failed
+// wait, the end of the warp's range); pd_decode_kernel then lets the warp leave the launch.
+// The launch's epoch sits in the first word of the shared arrays (written by thread 0 before
+// the body starts, read after the prologue's first block barrier).
 template <typename T, int D, int GT>
-__global__ void __launch_bounds__(256, 1)
-    pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
-                     const __grid_constant__ CUtensorMap vmap) {
+__device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtensorMap& kmap,
+                                            const CUtensorMap& vmap, unsigned char* smem) {
   using C = DecodeCfg<T, D, GT>;
   using E = Elem<T>;
-  extern __shared__ __align__(1024) unsigned char smem[];
-
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -144,10 +171,11 @@ __global__ void __launch_bounds__(256, 1)
   const int B = p.batch;
 
   // Dynamic shared memory:
-  // [mbarriers | warp_sums[32] | lens[B] | pre[B+1] | apos[B] | pad | stages].
+  // [mbarriers | epoch | warp_sums[32] | lens[B] | pre[B+1] | apos[B] | pad | stages].
   // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off);
+  const uint32_t* s_epoch = reinterpret_cast<const uint32_t*>(smem + p.smem_arrays_off);
+  int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off) + 1;
   int* lens = warp_sums + 32;
   int* pre = lens + B;  // B + 1 entries: exclusive prefix of tiles per row
   int* apos = pre + B + 1;  // fused append: position to take from the source, or -1
@@ -159,19 +187,16 @@ __global__ void __launch_bounds__(256, 1)
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
-  // Re-tag this launch's item counters with its epoch (this CTA's share of them).
-  {
-    const int64_t n_items = int64_t(B) * p.n_kv_head * p.n_gchunks;
-    const unsigned long long tag = (unsigned long long)p.epoch << 32;
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < n_items; i += int64_t(gridDim.x) * blockDim.x)
-      atomicExch(p.counters + i, tag);
-  }
 
   // ---- fused append: store every row's new K/V rows in the pools (16 B per thread) -----
-  // Tiles read below may still see the old bytes of these slots (their TMA copies are not
-  // ordered after these stores); the consumer overwrites those rows from the source, so
-  // this launch's result never depends on which bytes a copy saw.
-  if (p.append) {
+  // Every thread runs this exactly once, on whichever path it takes: a worker warp right
+  // after issuing its first TMA copies (the stores and their dependent loads then overlap
+  // the first DRAM round trip), any other warp before it leaves. Tiles may see the old
+  // bytes of these slots (their copies are not ordered after the stores); the consumer
+  // overwrites those rows from the source, so the result never depends on which bytes a
+  // copy saw.
+  auto store_appended = [&]() {
+    if (!p.append) return;
     constexpr int CH = C::CHUNKS;
     const int64_t tasks = int64_t(B) * p.n_kv_head * 2 * CH;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < tasks; i += int64_t(gridDim.x) * blockDim.x) {
@@ -200,7 +225,7 @@ __global__ void __launch_bounds__(256, 1)
                   : reinterpret_cast<T*>(p.pool_k) + blk * p.pk_sb + off * p.pk_sn + int64_t(h) * p.pk_sh;
       *reinterpret_cast<uint4*>(dst + c * C::EPC) = __ldg(reinterpret_cast<const uint4*>(src + c * C::EPC));
     }
-  }
+  };
 
   // ---- prologue: clamp lengths, tiles per row, block-wide exclusive scan -------------
   {
@@ -210,19 +235,12 @@ __global__ void __launch_bounds__(256, 1)
     int local = 0;
     for (int b = b0; b < b1; ++b) {
       int len = __ldg(p.seqlen + b);
+      const int64_t pos = p.append ? __ldg(p.app_pos + b) : -1;
       len = len < 0 ? 0 : (len > p.capacity ? p.capacity : len);
       lens[b] = len;
-      if (p.append) {
-        // The appended token is read from the source only if the row reads it at all and
-        // its slot was written above (a position inside the table, a block inside the pool).
-        const int64_t pos = __ldg(p.app_pos + b);
-        int ap = -1;
-        if (pos >= 0 && pos < len) {
-          const int64_t blk = __ldg(p.table + int64_t(b) * p.bt_stride + (pos >> p.log2_bs));
-          if (blk >= 0 && blk < p.n_blocks) ap = int(pos);
-        }
-        apos[b] = ap;
-      }
+      // Fused append: the tile holding the appended token takes it from the source when the
+      // row reads that position (a position inside [0, len) is inside the table).
+      if (p.append) apos[b] = pos >= 0 && pos < len ? int(pos) : -1;
       local += (len + C::TILE - 1) >> C::LOG_TILE;
     }
     int incl = local;
@@ -252,6 +270,17 @@ __global__ void __launch_bounds__(256, 1)
     }
     __syncthreads();
   }
+  const uint32_t epoch = *s_epoch;
+
+  // Re-tag this launch's item counters (this CTA's share) and, in CTA 0, the exit counter
+  // with the launch's epoch. Arrivals come at least one tile later.
+  {
+    const int64_t n_items = int64_t(B) * p.n_kv_head * p.n_gchunks;
+    const unsigned long long tag = (unsigned long long)epoch << 32;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < n_items; i += int64_t(gridDim.x) * blockDim.x)
+      atomicExch(p.counters + i, tag);
+    if (blockIdx.x == 0 && tid == 0) atomicExch(p.exit_counter, tag);
+  }
 
   const int items_per_row = p.n_kv_head * p.n_gchunks;
   const int64_t units = int64_t(items_per_row) * pre[B];
@@ -273,7 +302,10 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   }
-  if (units == 0) return;
+  if (units == 0) {
+    store_appended();
+    return;
+  }
 
   // ---- this warp's unit range ----------------------------------------------------------
   // Never more workers than units: every worker range must be non-empty, because a split
@@ -285,10 +317,12 @@ __global__ void __launch_bounds__(256, 1)
     if (want < workers) workers = int(want < 1 ? 1 : want);
   }
   const int w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
-  if (w >= workers) return;
   const int64_t u0 = int64_t(w) * units / workers;
   const int64_t u1 = int64_t(w + 1) * units / workers;
-  if (u0 >= u1) return;
+  if (w >= workers || u0 >= u1) {
+    store_appended();
+    return;
+  }
   const int64_t nunits = u1 - u0;
 
   uint64_t* my_bars = bars + warp * S;
@@ -376,6 +410,7 @@ __global__ void __launch_bounds__(256, 1)
       cursor_advance(pc, pre, lens, B, items_per_row, p.n_gchunks);
     }
   }
+  store_appended();
 
   // ---- consumer state -----------------------------------------------------------------
   const int rg = lane >> C::LOG_LPR;        // row group of this lane
@@ -720,7 +755,7 @@ __global__ void __launch_bounds__(256, 1)
         const int c_first = worker_of(us, units, workers);
         const int c_last = worker_of(ue - 1, units, workers);
         int ticket = 0;
-        if (lane == 0) ticket = take_ticket(p.counters + item_global, p.epoch, p.err);
+        if (lane == 0) ticket = take_ticket(p.counters + item_global, epoch, p.err);
         ticket = __shfl_sync(FULL_MASK, ticket, 0);
         if (ticket == c_last - c_first) {
           __threadfence();
@@ -854,6 +889,19 @@ __global__ void __launch_bounds__(256, 1)
     s = s_n;
     parity = parity_n;
   }
+}
+
+template <typename T, int D, int GT>
+__global__ void __launch_bounds__(256, 1)
+    pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint32_t* s_epoch = reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off);
+  if (threadIdx.x == 0) *s_epoch = *reinterpret_cast<volatile unsigned*>(p.epoch_word);
+  decode_body<T, D, GT>(p, kmap, vmap, smem);
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0)
+    leave_launch(p.exit_counter, p.epoch_word, *s_epoch, gridDim.x * (blockDim.x >> 5), p.err);
 }
 
 template <typename T, int D, int GT>

@@ -415,8 +415,20 @@ class PagedKV:
         """Perform a recorded append now (see :meth:`PagedPool.flush`)."""
         self.pool.flush()
 
-    def attend(self, layer: int, q: torch.Tensor, *, dropout_p: float = 0.0) -> torch.Tensor:
-        """Block-table decode for one layer; ``q`` is ``(B, H, 1, D)``, output the same."""
+    def _plan_for(self, q3: torch.Tensor):
+        from model.triton_decode import paged_decode_plan
+
+        if self._decode_plan is None:
+            self._decode_plan = paged_decode_plan(
+                q3, self.pool._keys, self.pool._values, self._block_table_tensor, self._seqlen,
+                scale=1.0 / (self.head_dim ** 0.5),
+            )
+        return self._decode_plan
+
+    def attend(self, layer: int, q: torch.Tensor, *, dropout_p: float = 0.0,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """Block-table decode for one layer; ``q`` is ``(B, H, 1, D)``, output the same.
+        ``out`` (optional) is a preallocated contiguous ``(B, H, 1, D)`` result buffer."""
         if not self._seqlen_ready:
             raise RuntimeError("PagedKV.attend() before build_mask(): seqlen is stale")
         if not self._step_written:
@@ -426,22 +438,17 @@ class PagedKV:
         expected = (self.batch, self.n_head, 1, self.head_dim)
         if tuple(q.shape) != expected:
             raise ValueError(f"attend needs q {expected}, got {tuple(q.shape)}")
-        from model.triton_decode import paged_decode_plan
-
         q3 = q[:, :, 0, :].contiguous()
-        if self._decode_plan is None:
-            self._decode_plan = paged_decode_plan(
-                q3, self.pool._keys, self.pool._values, self._block_table_tensor, self._seqlen,
-                scale=1.0 / (self.head_dim ** 0.5),
-            )
+        plan = self._plan_for(q3)
+        out3 = None if out is None else out[:, :, 0, :]
         pending = self.pool._pending
         if (pending is not None and pending.owner is self and pending.layer == int(layer)
                 and pending.stream == torch.cuda.current_stream(self.device)
-                and self._decode_plan.can_fuse_append(pending.k, pending.v, self.pos)):
+                and plan.can_fuse_append(pending.k, pending.v, self.pos)):
             self.pool._pending = None
-            return self._decode_plan.run_append(layer, q3, pending.k, pending.v, self.pos).unsqueeze(2)
+            return plan.run_append(layer, q3, pending.k, pending.v, self.pos, out=out3).unsqueeze(2)
         self.pool.flush()
-        return self._decode_plan.run(layer, q3).unsqueeze(2)
+        return plan.run(layer, q3, out=out3).unsqueeze(2)
 
     def advance(self) -> None:
         """Move every active row's cursor one token (device in place, then host mirrors)."""
@@ -456,6 +463,49 @@ class PagedKV:
         self._seqlen_ready = False
         if self.check_bounds and max(self._host_pos) > self.max_len:
             raise IndexError(f"PagedKV overflow: max_len={self.max_len}; a request decoded past its budget")
+        self._refresh_slots()
+
+    # ---------------------------------------------------------------- CUDA-graph support
+    def prepare(self, q: torch.Tensor) -> None:
+        """Build the decode plan for queries shaped like ``q`` ``(B, H, 1, D)`` and load its
+        kernel (one decode into a scratch output), touching neither the pool nor the step
+        state -- what a captured step needs to exist before capture."""
+        expected = (self.batch, self.n_head, 1, self.head_dim)
+        if tuple(q.shape) != expected:
+            raise ValueError(f"prepare needs q {expected}, got {tuple(q.shape)}")
+        q3 = q[:, :, 0, :].contiguous()
+        self._plan_for(q3).run(0, q3)
+
+    def _host_snapshot(self):
+        return (list(self._host_pos), list(self._host_valid), self._slot_error, self._step_written,
+                self._seqlen_ready)
+
+    def _host_restore(self, snap) -> None:
+        (self._host_pos, self._host_valid, self._slot_error, self._step_written, self._seqlen_ready) = (
+            list(snap[0]), list(snap[1]), snap[2], snap[3], snap[4])
+        self._slot_cache = None
+
+    def _replayed_step(self, next_token: bool) -> None:
+        """Host side of one step whose device work was replayed from a graph: the checks that
+        build_mask and write make, then the position mirrors advance makes."""
+        longest = max(n + int(next_token) for n in self._host_valid)
+        if self.check_bounds and longest > self.max_len:
+            raise IndexError(f"PagedKV overflow: needs {longest} positions, run position bound is {self.max_len}")
+        if self.check_bounds and max(self._host_pos) >= self.max_len:
+            raise IndexError(f"PagedKV overflow: write position {max(self._host_pos)} >= max_len {self.max_len}")
+        if self._slot_error is not None:
+            row, position, block_index, have = self._slot_error
+            raise IndexError(
+                f"row {row}: position {position} needs block {block_index}, but its block table has {have} blocks"
+            )
+
+    def _replayed_advance(self) -> None:
+        for row in range(self.batch):
+            if self._host_active[row]:
+                self._host_pos[row] += 1
+                self._host_valid[row] = max(self._host_valid[row], self._host_pos[row])
+        self._step_written = False
+        self._seqlen_ready = False
         self._refresh_slots()
 
     # ---------------------------------------------------------------- helpers

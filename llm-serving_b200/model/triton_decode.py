@@ -318,10 +318,19 @@ class PagedDecodePlan:
             )
         return int(layer)
 
-    def run(self, layer: int, q):
-        """Launch the kernel for one layer; ``q`` must match the validated layout."""
+    def _output(self, out):
+        if out is None:
+            return torch.empty(self.q_shape, dtype=self.q_dtype, device=self.q_device)
+        if (tuple(out.shape) != self.q_shape or out.dtype != self.q_dtype or out.device != self.q_device
+                or out.stride() != self.q_strides):
+            raise ValueError(f"out must be a contiguous {self.q_shape} {self.q_dtype} tensor on {self.q_device}")
+        return out
+
+    def run(self, layer: int, q, *, out=None):
+        """Launch the kernel for one layer; ``q`` must match the validated layout. ``out``
+        (optional) is a preallocated contiguous ``(B, H, D)`` result buffer."""
         layer = self._check_query(layer, q)
-        out = torch.empty_like(q)
+        out = self._output(out)
         self._native_plan.run(layer, q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
         return out
 
@@ -340,7 +349,7 @@ class PagedDecodePlan:
         return (pos.dtype == torch.int64 and tuple(pos.shape) == (b,) and pos.device == self.q_device
                 and pos.stride(0) == 1)
 
-    def run_append(self, layer: int, q, k_new, v_new, pos):
+    def run_append(self, layer: int, q, k_new, v_new, pos, *, out=None):
         """Store row ``b``'s new K/V ``(B, H_kv, D)`` at logical position ``pos[b]`` of layer
         ``layer``'s pools and decode that layer, in one launch.
 
@@ -354,7 +363,7 @@ class PagedDecodePlan:
                 "paged_decode_plan.run_append needs (B, H_kv, D) k/v rows in the plan's dtype with "
                 "16-byte aligned rows and an int64 (B,) pos on the plan's device"
             )
-        out = torch.empty_like(q)
+        out = self._output(out)
         self._native_plan.run_append(layer, q, out, k_new, v_new, pos,
                                      torch.cuda.current_stream(self.q_device).cuda_stream)
         return out
