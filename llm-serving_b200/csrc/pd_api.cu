@@ -30,6 +30,14 @@ struct Tuning {
 };
 Tuning g_tuning;
 std::mutex g_mutex;
+// Decode kernel choice: 1 = shared-stage (CTA) kernel wherever a row has exactly one item per
+// consumer warp, 0 = per-warp kernel everywhere (the default: on B200 it streams config-2
+// shapes as fast as the shared-stage kernel with less synchronisation). cta_stages 0 = sized
+// from shared memory.
+int g_decode_mode = 0;
+int g_cta_stages = 0;
+int g_row_cost = 3;  // column split: virtual columns charged per row start
+constexpr int kCtaConsumerWarps = 8;
 
 thread_local char g_last_error[256] = "";
 
@@ -108,7 +116,9 @@ struct Geometry {
   int n_gchunks;
   int tile;        // tokens per stage
   int box_tokens;  // tokens per TMA box
-  int stage_bytes;
+  bool cta;        // shared-stage kernel: one consumer warp per item of a row
+  int box_heads;   // kv heads per TMA box: all of them in the shared-stage kernel, else 1
+  int stage_bytes; // K + V bytes of one stage (of one warp, or of the CTA when shared)
 };
 
 int geometry(int n_head, int n_kv_head, int head_dim, int block_size, int dtype, Geometry* g) {
@@ -126,11 +136,21 @@ int geometry(int n_head, int n_kv_head, int head_dim, int block_size, int dtype,
   const int row_bytes = head_dim * elem_size(dtype);
   g->tile = 4096 / row_bytes;
   g->box_tokens = block_size < g->tile ? block_size : g->tile;
-  g->stage_bytes = 2 * 4096;
+  int mode;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    mode = g_decode_mode;
+  }
+  g->cta = mode == 1 && n_kv_head * g->n_gchunks == kCtaConsumerWarps && gt <= 4 &&
+           (dtype == PD_BF16 || dtype == PD_F16) && head_dim >= 64;
+  g->box_heads = g->cta ? n_kv_head : 1;
+  g->stage_bytes = 2 * 4096 * g->box_heads;
   return PD_OK;
 }
 
 DecodeLaunchFn launcher_for(int dtype, const Geometry& g) {
+  if (g.cta) return dtype == PD_BF16 ? decode_launcher_cta_bf16(g.d_index, g.gt_index)
+                                     : decode_launcher_cta_f16(g.d_index, g.gt_index);
   switch (dtype) {
     case PD_F32: return decode_launcher_f32(g.d_index, g.gt_index);
     case PD_F16: return decode_launcher_f16(g.d_index, g.gt_index);
@@ -150,12 +170,14 @@ struct Launch {
   size_t smem;
 };
 
-size_t smem_for(int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
-  const size_t bars = round_up(size_t(warps) * stages * 8, 16);
+// Per-warp kernel: `stages` stages and barriers per warp. Shared-stage kernel: `stages` shared
+// stages with a full and an empty barrier each.
+size_t smem_for(bool cta, int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
+  const size_t bars = round_up(size_t(cta ? 2 : warps) * stages * 8, 16);
   const size_t arrays = round_up(size_t(1 + 32 + 3 * rows + 1) * 4, 16);
   *arrays_off = int(bars);
   *stage_off = int(bars + arrays);
-  return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(warps) * stages * stage_bytes;
+  return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(cta ? 1 : warps) * stages * stage_bytes;
 }
 
 int launch_shape(int dev, int batch, const Geometry& g, Launch* L) {
@@ -166,15 +188,22 @@ int launch_shape(int dev, int batch, const Geometry& g, Launch* L) {
   }
   const int sms = sm_count(dev);
   if (sms <= 0) return PD_ERR_CUDA;
-  L->warps = t.warps;
-  L->stages = t.stages;
+  int cta_stages;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    cta_stages = g_cta_stages;
+  }
+  L->warps = g.cta ? kCtaConsumerWarps + 1 : t.warps;  // shared stages: consumers + a producer
+  L->stages = g.cta ? (cta_stages > 0 ? cta_stages : std::min(8, std::max(2, 196608 / g.stage_bytes)))
+                    : t.stages;
   L->min_tiles = t.min_tiles;
-  L->grid = sms * t.ctas_per_sm;
+  const int ctas_per_sm = g.cta ? 1 : t.ctas_per_sm;
+  L->grid = sms * ctas_per_sm;
   int rows = batch < 1 ? 1 : batch;
   if (rows > 4096) rows = 4096;
   for (;;) {
-    L->smem = smem_for(L->warps, L->stages, rows, g.stage_bytes, &L->arrays_off, &L->stage_off);
-    if (L->smem * size_t(t.ctas_per_sm) <= size_t(kMaxSmemPerBlock)) break;
+    L->smem = smem_for(g.cta, L->warps, L->stages, rows, g.stage_bytes, &L->arrays_off, &L->stage_off);
+    if (L->smem * size_t(ctas_per_sm) <= size_t(kMaxSmemPerBlock)) break;
     if (rows <= 256) return PD_ERR_INVALID;  // tuning asks for more shared memory than exists
     rows /= 2;
   }
@@ -203,7 +232,7 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
 }
 
 int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_size, int n_kv_head,
-                int head_dim, const int64_t* strides, int dtype, int box_tokens) {
+                int head_dim, const int64_t* strides, int dtype, int box_tokens, int box_heads) {
   if (load_encoder() != PD_OK) return PD_ERR_CUDA;
   const int es = elem_size(dtype);
   if (!aligned16(base)) return PD_ERR_INVALID;
@@ -219,7 +248,7 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
   // Byte strides of dims 1..3: head, token-in-block, block.
   const cuuint64_t gstr[3] = {cuuint64_t(strides[2] * es), cuuint64_t(strides[1] * es),
                               cuuint64_t(strides[0] * es)};
-  const cuuint32_t box[4] = {cuuint32_t(head_dim), 1u, cuuint32_t(box_tokens), 1u};
+  const cuuint32_t box[4] = {cuuint32_t(head_dim), cuuint32_t(box_heads), cuuint32_t(box_tokens), 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUresult r = g_encode(map, t, 4, const_cast<void*>(base), dims, gstr, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -288,6 +317,10 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   p.log2_box = ilog2_host(P->g.box_tokens);
   p.stages = P->L.stages;
   p.min_tiles = P->L.min_tiles;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    p.row_cost = g_row_cost;
+  }
   p.smem_arrays_off = P->L.arrays_off;
   p.smem_stage_off = P->L.stage_off;
   p.scale_log2 = scale_log2;
@@ -362,7 +395,7 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
       p.pv_sh = app->v_strides[2];
       p.n_blocks = app->n_blocks;
     }
-    const size_t smem = smem_for(P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
+    const size_t smem = smem_for(P.g.cta, P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
                                  &p.smem_stage_off);
     cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream);
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
@@ -390,10 +423,10 @@ int decode_common(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache
     return PD_ERR_INVALID;
   CUtensorMap kmap, vmap;
   st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype,
-                   P.g.box_tokens);
+                   P.g.box_tokens, P.g.box_heads);
   if (st != PD_OK) return st;
   st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype,
-                   P.g.box_tokens);
+                   P.g.box_tokens, P.g.box_heads);
   if (st != PD_OK) return st;
   return run_prepared(P, kmap, vmap, q, q_sb, q_sh, out, o_sb, o_sh, pm, pl, pacc, mode, dtype,
                       static_cast<cudaStream_t>(stream));
@@ -525,10 +558,10 @@ int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
     h->k_pools[layer] = const_cast<void*>(k_caches[layer]);
     h->v_pools[layer] = const_cast<void*>(v_caches[layer]);
     st = encode_pool(&h->kmaps[layer], k_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
-                     k_strides, dtype, h->P.g.box_tokens);
+                     k_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads);
     if (st == PD_OK)
       st = encode_pool(&h->vmaps[layer], v_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
-                       v_strides, dtype, h->P.g.box_tokens);
+                       v_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads);
     if (st != PD_OK) {
       delete h;
       return st;
@@ -711,6 +744,24 @@ int pd_set_decode_tuning(int32_t warps_per_cta, int32_t stages, int32_t ctas_per
   if (t.warps > 8 || t.stages < 2 || t.stages > 16 || t.ctas_per_sm > 8) return PD_ERR_INVALID;
   if (size_t(t.warps) * t.stages * 8192 + 2048 > size_t(kMaxSmemPerBlock)) return PD_ERR_INVALID;
   g_tuning = t;
+  return PD_OK;
+}
+
+int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost) {
+  if (mode < 0 || mode > 1 || shared_stages < 0 || shared_stages > 8 || row_cost < -1 || row_cost > 64)
+    return PD_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  g_decode_mode = mode;
+  g_cta_stages = shared_stages;
+  if (row_cost >= 0) g_row_cost = row_cost;
+  return PD_OK;
+}
+
+int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (mode) *mode = g_decode_mode;
+  if (shared_stages) *shared_stages = g_cta_stages;
+  if (row_cost) *row_cost = g_row_cost;
   return PD_OK;
 }
 

@@ -51,6 +51,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -89,6 +93,20 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// Atomic add at GPU scope with release semantics: this thread's earlier writes (and those of
+// threads synchronised with it, e.g. by __syncwarp) are visible before the add is.
+__device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long* p,
+                                                                   unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+
+// Prefetches one 128-byte line into L2.
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA)
@@ -226,7 +244,8 @@ struct DecodeParams {
   int32_t log2_box;
   int32_t mode;        // 0: normalised output, 1: (m, l, acc) partials
   int32_t stages;      // pipeline depth per warp
-  int32_t min_tiles;   // minimum tiles per active warp
+  int32_t min_tiles;   // minimum tiles per active warp (unit split)
+  int32_t row_cost;    // column split: extra virtual columns charged to every row start
   int32_t smem_arrays_off;
   int32_t smem_stage_off;
   float scale_log2;

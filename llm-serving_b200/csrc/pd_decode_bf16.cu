@@ -12,6 +12,18 @@ static const DecodeLaunchFn kTable[6][4] = {PD_ROW(8),  PD_ROW(16),  PD_ROW(32),
                                             PD_ROW(64), PD_ROW(128), PD_ROW(256)};
 #undef PD_ROW
 
+#define PD_CTA_ROW(D) \
+  {launch_decode<__nv_bfloat16, D, 1, true>, launch_decode<__nv_bfloat16, D, 2, true>, launch_decode<__nv_bfloat16, D, 4, true>, \
+   launch_decode<__nv_bfloat16, D, 8, true>}
+
+static const DecodeLaunchFn kCtaTable[3][4] = {PD_CTA_ROW(64), PD_CTA_ROW(128), PD_CTA_ROW(256)};
+#undef PD_CTA_ROW
+
+DecodeLaunchFn decode_launcher_cta_bf16(int d_index, int gt_index) {
+  if (d_index < 3 || d_index >= 6 || gt_index < 0 || gt_index >= 4) return nullptr;
+  return kCtaTable[d_index - 3][gt_index];
+}
+
 DecodeLaunchFn decode_launcher_bf16(int d_index, int gt_index) {
   if (d_index < 0 || d_index >= 6 || gt_index < 0 || gt_index >= 4) return nullptr;
   return kTable[d_index][gt_index];

@@ -101,6 +101,20 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, const int* pre, const 
   }
 }
 
+// Column-mode advance: the item (kv head, q-head chunk) stays fixed, the cursor walks the
+// row's tiles and then the next rows' (rows with no tiles are skipped).
+__device__ __forceinline__ void cursor_advance_col(Cursor& c, const int* pre, const int* lens, int batch) {
+  if (++c.tile < c.ntile) return;
+  c.tile = 0;
+  do {
+    ++c.b;
+  } while (c.b < batch && pre[c.b + 1] == pre[c.b]);
+  if (c.b < batch) {
+    c.ntile = pre[c.b + 1] - pre[c.b];
+    c.len = lens[c.b];
+  }
+}
+
 // Arrival on the counter shared by the pieces of one split item; returns how many pieces of
 // this launch arrived before. Counters live in workspace memory that is never cleared and hold
 // (epoch << 32) | count. Every launch re-tags its item counters with its own epoch in the
@@ -111,7 +125,7 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, const int* pre, const 
 __device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t epoch, unsigned* err) {
   unsigned long long t0 = 0;
   for (;;) {
-    const unsigned long long old = atomicAdd(counter, 1ull);
+    const unsigned long long old = atomicAdd(counter, 1ull);  // callers fence before arriving
     if (uint32_t(old >> 32) == epoch) return int(uint32_t(old));
     const unsigned long long now = global_timer_ns();
     if (t0 == 0) {
@@ -158,7 +172,14 @@ __device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) 
 // wait, the end of the warp's range); pd_decode_kernel then lets the warp leave the launch.
 // The launch's epoch sits in the first word of the shared arrays (written by thread 0 before
 // the body starts, read after the prologue's first block barrier).
-template <typename T, int D, int GT>
+//
+// CTA = false: every warp runs its own TMA pipeline (per-warp stages, unit or column split).
+// CTA = true (used when a row has exactly one item per consumer warp): the CTA shares its
+// stages. The last warp is the producer: per column it loads the whole K and V boxes of all
+// kv heads (one TMA copy each per block part) into a shared stage, and the consumer warps --
+// warp j streams item j -- read their head's rows from it and release the stage on an
+// "empty" barrier. Contiguous block-sized copies keep the DRAM stream dense.
+template <typename T, int D, int GT, bool CTA>
 __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtensorMap& kmap,
                                             const CUtensorMap& vmap, unsigned char* smem) {
   using C = DecodeCfg<T, D, GT>;
@@ -166,12 +187,17 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
+  const int nwarps = (blockDim.x >> 5) - (CTA ? 1 : 0);  // consumer warps
+  const bool producer = CTA && warp == nwarps;
   const int S = p.stages;
   const int B = p.batch;
+  // Shared-stage geometry (CTA mode): a stage holds TILE tokens of every kv head for K, then V.
+  const int kv_stage_bytes = CTA ? p.n_kv_head * C::TILE_BYTES : C::TILE_BYTES;  // K (or V) part
+  const int row_stride = CTA ? p.n_kv_head * C::ROW_BYTES : C::ROW_BYTES;       // token to token
 
   // Dynamic shared memory:
   // [mbarriers | epoch | warp_sums[32] | lens[B] | pre[B+1] | apos[B] | pad | stages].
+  // mbarriers: per-warp mode S per warp; CTA mode full[S] then empty[S].
   // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   const uint32_t* s_epoch = reinterpret_cast<const uint32_t*>(smem + p.smem_arrays_off);
@@ -252,7 +278,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     if (lane == 31) warp_sums[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-      int v = lane < nwarps ? warp_sums[lane] : 0;
+      int v = lane < int(blockDim.x >> 5) ? warp_sums[lane] : 0;  // every warp's share
       int vi = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -307,46 +333,106 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     return;
   }
 
-  // ---- this warp's unit range ----------------------------------------------------------
-  // Never more workers than units: every worker range must be non-empty, because a split
-  // item is merged when all workers overlapping it have arrived.
-  int workers = int(gridDim.x) * nwarps;
-  if (int64_t(workers) > units) workers = int(units);
-  if (p.min_tiles > 1) {
-    const int64_t want = (units + p.min_tiles - 1) / p.min_tiles;
-    if (want < workers) workers = int(want < 1 ? 1 : want);
+  // ---- this warp's share of the work -----------------------------------------------------
+  // Column mode (a row has exactly one item per warp): the (row, tile) columns are cut into
+  // one contiguous range per CTA, and warp j streams item j over the CTA's columns. The
+  // block's kv heads are then requested by the CTA's warps at about the same time, which is
+  // what keeps DRAM pages open. Otherwise (unit mode) the units (row, item, tile) are cut
+  // into one contiguous range per warp.
+  const bool colmode = CTA || items_per_row == nwarps;
+  const int64_t ncols = pre[B];
+  // Column mode cuts *virtual* columns: each row is preceded by row_cost extra ones (what a
+  // row switch costs a warp -- a table window, a q load, a partial store -- in tile times),
+  // so a range that crosses into a new row gets that many fewer real tiles. vpre(b) is the
+  // first virtual column of row b; its real tiles start row_cost later.
+  const int rc = colmode ? p.row_cost : 0;
+  auto vpre = [&](int b) -> int64_t { return int64_t(pre[b]) + int64_t(rc) * b; };
+  const int64_t vcols = colmode ? vpre(B) : 0;
+  // Ranges in use: never more than virtual columns, so that no range is empty.
+  const int col_parts = int(vcols < int64_t(gridDim.x) ? vcols : int64_t(gridDim.x));
+  // Real column at virtual column v (0 <= v <= vcols); a row's extra columns map to its first tile.
+  auto real_col = [&](int64_t v) -> int64_t {
+    if (v >= vcols) return ncols;
+    int lo = 0, hi = B;  // first row i with vpre(i) > v
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (vpre(mid) > v) hi = mid; else lo = mid + 1;
+    }
+    const int64_t t = v - vpre(lo - 1) - rc;
+    return pre[lo - 1] + (t > 0 ? t : 0);
+  };
+  auto range_start = [&](int c) -> int64_t { return real_col(int64_t(c) * vcols / col_parts); };
+  int workers = 0, w = 0;     // unit mode: worker count and this warp's worker id
+  int64_t u0 = 0, u1 = 0;     // unit mode: range of units; column mode: range of real columns
+  if (colmode) {
+    if (int(blockIdx.x) < col_parts) {
+      u0 = range_start(int(blockIdx.x));
+      u1 = range_start(int(blockIdx.x) + 1);
+    }
+  } else {
+    // Never more workers than units: every worker range must be non-empty, because a split
+    // item is merged when all workers overlapping it have arrived.
+    workers = int(gridDim.x) * nwarps;
+    if (int64_t(workers) > units) workers = int(units);
+    if (p.min_tiles > 1) {
+      const int64_t want = (units + p.min_tiles - 1) / p.min_tiles;
+      if (want < workers) workers = int(want < 1 ? 1 : want);
+    }
+    w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
+    u0 = w < workers ? int64_t(w) * units / workers : 0;
+    u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
   }
-  const int w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
-  const int64_t u0 = int64_t(w) * units / workers;
-  const int64_t u1 = int64_t(w + 1) * units / workers;
-  if (w >= workers || u0 >= u1) {
+  if (u0 >= u1) {
     store_appended();
     return;
   }
   const int64_t nunits = u1 - u0;
+  // Partial-result slot pair of this warp (two: its range's first and last segment).
+  const int wslot = colmode ? int(blockIdx.x) * nwarps + warp : w;
+  auto advance = [&](Cursor& c) {
+    if (colmode) cursor_advance_col(c, pre, lens, B);
+    else cursor_advance(c, pre, lens, B, items_per_row, p.n_gchunks);
+  };
 
-  uint64_t* my_bars = bars + warp * S;
-  unsigned char* my_stages = stage_base + size_t(warp) * S * C::STAGE_BYTES;
-  if (lane == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(smem_addr(my_bars + s), 1);
-    fence_barrier_init();
+  // Stage s of this warp: K at stage_k(s), V at stage_k(s) + kv_stage_bytes. Its "full"
+  // barrier completes when the stage's copies land; in CTA mode the consumers' arrivals on
+  // its "empty" barrier hand it back to the producer.
+  uint64_t* my_bars = CTA ? bars : bars + warp * S;
+  uint64_t* empty_bars = bars + S;  // CTA mode only
+  unsigned char* my_stages = CTA ? stage_base : stage_base + size_t(warp) * S * C::STAGE_BYTES;
+  const size_t stage_stride = CTA ? size_t(2) * kv_stage_bytes : size_t(C::STAGE_BYTES);
+  if (CTA) {
+    if (tid == 0) {
+      for (int s = 0; s < S; ++s) {
+        mbar_init(smem_addr(my_bars + s), 1);
+        mbar_init(smem_addr(empty_bars + s), nwarps);
+      }
+      fence_barrier_init();
+    }
+    __syncthreads();  // the CTA's warps share one range: all of them are here
+  } else {
+    if (lane == 0) {
+      for (int s = 0; s < S; ++s) mbar_init(smem_addr(my_bars + s), 1);
+      fence_barrier_init();
+    }
+    __syncwarp();
   }
-  __syncwarp();
 
-  // Locate u0: the last row whose first unit is <= u0 (rows with no tiles are skipped).
+  // Locate u0: the last row whose first unit (column) is <= u0 (rows with no tiles are skipped).
   Cursor cur;
   {
-    int lo = 0, hi = B;  // find first i with items_per_row * pre[i] > u0
+    const int per_row = colmode ? 1 : items_per_row;
+    int lo = 0, hi = B;  // find first i with per_row * pre[i] > u0
     while (lo < hi) {
       const int mid = (lo + hi) >> 1;
-      if (int64_t(items_per_row) * pre[mid] > u0) hi = mid; else lo = mid + 1;
+      if (int64_t(per_row) * pre[mid] > u0) hi = mid; else lo = mid + 1;
     }
     cur.b = lo - 1;
     cur.ntile = pre[cur.b + 1] - pre[cur.b];
     cur.len = lens[cur.b];
-    const int64_t r = u0 - int64_t(items_per_row) * pre[cur.b];
-    cur.item = int(r / cur.ntile);
-    cur.tile = int(r - int64_t(cur.item) * cur.ntile);
+    const int64_t r = u0 - int64_t(per_row) * pre[cur.b];
+    cur.item = colmode ? (producer ? 0 : warp) : int(r / cur.ntile);
+    cur.tile = int(r - int64_t(colmode ? 0 : cur.item) * cur.ntile);
     cur.h = cur.item / p.n_gchunks;
     cur.gc = cur.item - cur.h * p.n_gchunks;
   }
@@ -356,7 +442,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   const int box_tokens = p.box_tokens;
   const int log2_box = p.log2_box;
   const int nbox = C::TILE >> log2_box;
-  const uint32_t box_bytes = uint32_t(box_tokens) * C::ROW_BYTES;
+  const uint32_t box_bytes = uint32_t(box_tokens) * uint32_t(row_stride);  // one copy
   int win_row = -1, win_base = 0, win_cur = 0, win_nxt = 0;
 
   auto table_entry = [&](int row, int page, int npages) -> int {
@@ -386,8 +472,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     const int nvalid = min(nbox, (remain + box_tokens - 1) >> log2_box);
     const int npages = (c.len + bs - 1) >> p.log2_bs;
     const uint32_t bar = smem_addr(my_bars + s);
-    const uint32_t kdst = smem_addr(my_stages + size_t(s) * C::STAGE_BYTES);
-    const uint32_t vdst = kdst + C::TILE_BYTES;
+    const uint32_t kdst = smem_addr(my_stages + size_t(s) * stage_stride);
+    const uint32_t vdst = kdst + uint32_t(kv_stage_bytes);
     if (lane == 0) mbar_arrive_expect_tx(bar, 2u * uint32_t(nvalid) * box_bytes);
     for (int j = 0; j < nvalid; ++j) {
       const int tok = tok0 + j * box_tokens;
@@ -395,22 +481,59 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       const int off = tok & (bs - 1);
       const int blk = block_of(c.b, page, npages);
       if (lane == 0) {
-        tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, h, off, blk);
-        tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, h, off, blk);
+        tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, CTA ? 0 : h, off, blk);
+        tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, CTA ? 0 : h, off, blk);
       }
+    }
+  };
+
+  // Pulls the q rows of the item that cursor c opens into L2, so that start_segment, a few
+  // tiles later, does not wait on DRAM.
+  auto prefetch_q = [&](const Cursor& c) {
+    constexpr int LINES = (C::ROW_BYTES + 127) / 128;  // 128-byte lines per q row
+    if (lane < GT * LINES) {
+      const int hq = c.h * p.group + c.gc * GT + lane / LINES;
+      prefetch_l2(reinterpret_cast<const unsigned char*>(p.q) +
+                  (int64_t(c.b) * p.q_sb + int64_t(hq) * p.q_sh) * C::ES + (lane % LINES) * 128);
     }
   };
 
   Cursor pc = cur;
   int64_t issued = 0;
-  {
+  if (producer) {
+    // CTA mode: the producer streams the CTA's columns into the shared stages. Stage s is
+    // reused once all consumer warps released its previous column (empty barrier).
+    for (; issued < nunits; ++issued) {
+      const int s = int(issued % S);
+      if (issued >= S &&
+          !warp_wait_phase(smem_addr(empty_bars + s), uint32_t(((issued / S) - 1) & 1), WAIT_LIMIT_NS)) {
+        if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
+        break;
+      }
+      issue(pc, s);
+      advance(pc);
+      if (issued + 1 == (nunits < S ? nunits : S)) store_appended();
+    }
+    if (issued < (nunits < S ? nunits : S)) store_appended();
+    // Leave only once the copies issued last have landed (bounded): the CTA must not retire
+    // with a copy in flight, whatever the consumers did.
+    const int64_t from = issued > S ? issued - S : 0;
+    for (int64_t j = from; j < issued; ++j)
+      warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), WAIT_LIMIT_NS);
+    return;
+  }
+  if (!CTA) {
     const int64_t first = nunits < S ? nunits : S;
     for (; issued < first; ++issued) {
       issue(pc, int(issued));
-      cursor_advance(pc, pre, lens, B, items_per_row, p.n_gchunks);
+      advance(pc);
+      if (pc.tile == 0 && issued + 1 < nunits) prefetch_q(pc);
     }
   }
   store_appended();
+  // This warp's rows inside a stage: per-warp stages hold only its head; shared stages hold
+  // every kv head, and the warp's item fixes its head (column mode).
+  const int head_off = CTA ? (warp / p.n_gchunks) * C::ROW_BYTES : 0;
 
   // ---- consumer state -----------------------------------------------------------------
   const int rg = lane >> C::LOG_LPR;        // row group of this lane
@@ -435,11 +558,17 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   float m_run[GT], l_run[GT];
   int seg_first_tile = 0;
   bool first_segment = true;
+  // Split segments of this range whose partials are stored and whose arrival comes after the
+  // loop: a range holds at most two (its first and its last segment).
+  int n_pend = 0;
+  int pend_b0 = 0, pend_item0 = 0, pend_b1 = 0, pend_item1 = 0;
+  bool early = false;                 // the first pending segment already arrived (lane 0's
+  unsigned long long early_old = 0;   // add returned early_old)
 
   // Phase A of a tile: q.K for every (row, q head) of the stage, reduce-scattered so this
   // lane ends with its R held scores, scaled to log2 units and masked past valid_rows.
   auto tile_scores = [&](int stage, int valid_rows, float (&sc)[C::R]) {
-    const unsigned char* ks = my_stages + size_t(stage) * C::STAGE_BYTES;
+    const unsigned char* ks = my_stages + size_t(stage) * stage_stride + head_off;
     float sv[C::NV];
 #pragma unroll
     for (int i = 0; i < C::NT; ++i) {
@@ -447,7 +576,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       float2 kf[C::PPL];
 #pragma unroll
       for (int c = 0; c < C::CPL; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
+        const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * row_stride + (c * C::LPR + pl) * 16);
         E::unpack_pairs(raw, &kf[c * (C::EPC / 2)]);
       }
 #pragma unroll
@@ -536,14 +665,14 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
           if (hold_g[j] == g) l_run[g] += pj[j];
       }
     }
-    const unsigned char* vs = my_stages + size_t(stage) * C::STAGE_BYTES + C::TILE_BYTES;
+    const unsigned char* vs = my_stages + size_t(stage) * stage_stride + kv_stage_bytes + head_off;
 #pragma unroll
     for (int i = 0; i < C::NT; ++i) {
       const int row = i * C::RPL + rg;
       float2 vf[C::PPL];
 #pragma unroll
       for (int c = 0; c < C::CPL; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * C::ROW_BYTES + (c * C::LPR + pl) * 16);
+        const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * row_stride + (c * C::LPR + pl) * 16);
         E::unpack_pairs(raw, &vf[c * (C::EPC / 2)]);
       }
       if (!full) {
@@ -588,8 +717,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     if (!p.append) return;
     const int ap = apos[c.b];
     if (ap < 0 || (ap >> C::LOG_TILE) != c.tile) return;
-    unsigned char* krow = my_stages + size_t(stage) * C::STAGE_BYTES + (ap & (C::TILE - 1)) * C::ROW_BYTES;
-    unsigned char* vrow = krow + C::TILE_BYTES;
+    unsigned char* krow = my_stages + size_t(stage) * stage_stride + (ap & (C::TILE - 1)) * row_stride + head_off;
+    unsigned char* vrow = krow + kv_stage_bytes;
     const T* ksrc = reinterpret_cast<const T*>(p.app_k) + int64_t(c.b) * p.app_k_sb + int64_t(c.h) * p.app_k_sh;
     const T* vsrc = reinterpret_cast<const T*>(p.app_v) + int64_t(c.b) * p.app_v_sb + int64_t(c.h) * p.app_v_sh;
     for (int i = lane; i < 2 * C::CHUNKS; i += 32) {
@@ -604,8 +733,112 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
 
   auto fail_and_drain = [&](int64_t from) {
     if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
-    for (int64_t j = from; j < issued; ++j)
-      warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), DRAIN_LIMIT_NS);
+    if (!CTA) {  // shared stages' copies are the producer's; it waits for them before it leaves
+      for (int64_t j = from; j < issued; ++j)
+        warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), DRAIN_LIMIT_NS);
+    }
+  };
+
+  // Merge of split item (mb, mitem) by the piece that arrived last (ticket == pieces - 1).
+  // Pieces are the item's workers c_first..c_last in order; each lane owns NG consecutive
+  // float4 groups of the GT x D output (all of one q head) and folds the pieces in batches
+  // of MB with a running maximum, every load of a batch in flight together.
+  auto merge_if_last = [&](int mb, int mitem, int ticket) {
+    // The item's pieces: in unit mode the workers whose unit ranges overlap it, in column
+    // mode the CTAs whose column ranges overlap its row (slot pair of that CTA's warp mitem).
+    // (Column mode: the ranges holding the row's real tiles, virtual columns
+    // [vpre(mb) + row_cost, vpre(mb + 1)); a range of only the extra columns is not a piece.)
+    const int mntile = pre[mb + 1] - pre[mb];
+    const int64_t us = colmode ? vpre(mb) + rc : int64_t(items_per_row) * pre[mb] + int64_t(mitem) * mntile;
+    const int64_t total = colmode ? vcols : units;
+    const int nparts = colmode ? col_parts : workers;
+    const int c_first = worker_of(us, total, nparts);
+    const int c_last = worker_of(us + mntile - 1, total, nparts);
+    if (ticket != c_last - c_first) return;
+    __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
+    const int npieces = c_last - c_first + 1;
+    auto pair_of = [&](int c) -> int64_t { return colmode ? int64_t(c) * nwarps + mitem : int64_t(c); };
+    // Its first piece's slot: the range's first segment if the range starts at the item.
+    const bool first_starts_here = colmode ? range_start(c_first) == pre[mb]
+                                           : int64_t(c_first) * units / workers == us;
+    const int64_t first_slot = pair_of(c_first) * 2 + (first_starts_here ? 0 : 1);
+    auto slot_of = [&](int i) -> int64_t { return i == 0 ? first_slot : pair_of(c_first + i) * 2; };
+    const int mh = mitem / p.n_gchunks;
+    const int mhq0 = mh * p.group + (mitem - mh * p.n_gchunks) * GT;
+    constexpr int GROUPS = GT * (D / 4);             // float4 groups of the item's output
+    constexpr int NG = GROUPS >= 32 ? GROUPS / 32 : 1;  // groups per lane
+    constexpr int GB = NG < 8 ? NG : 8;              // groups per pass
+    constexpr int MB = GB == 1 ? 8 : (GB == 2 ? 6 : 8 / GB);  // pieces per batch
+    const bool active = lane * NG < GROUPS;
+    const int g = active ? (lane * NG) / (D / 4) : 0;  // the lane's q head within the item
+    const int64_t hrow = int64_t(mb) * p.n_head + mhq0 + g;
+    for (int g0 = 0; g0 < NG; g0 += GB) {
+      float M = -INFINITY, L = 0.f;
+      float4 a[GB];
+#pragma unroll
+      for (int t = 0; t < GB; ++t) a[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i0 = 0; i0 < npieces; i0 += MB) {
+        float mj[MB], lj[MB];
+        float4 x[MB][GB];
+#pragma unroll
+        for (int j = 0; j < MB; ++j) {
+          const int64_t sl = slot_of(i0 + j < npieces ? i0 + j : npieces - 1);
+          mj[j] = __ldcg(p.ws_ml + sl * (2 * GT) + g);
+          lj[j] = __ldcg(p.ws_ml + sl * (2 * GT) + GT + g);
+#pragma unroll
+          for (int t = 0; t < GB; ++t) {
+            const int col = ((lane * NG + g0 + t) & (D / 4 - 1)) * 4;
+            x[j][t] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D) + g * D + col));
+          }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int j = 0; j < MB; ++j)
+          if (i0 + j < npieces) Mn = fmaxf(Mn, mj[j]);
+        const float rescale = M == Mn ? 1.f : exp2f(M - Mn);
+        L *= rescale;
+#pragma unroll
+        for (int t = 0; t < GB; ++t) {
+          a[t].x *= rescale;
+          a[t].y *= rescale;
+          a[t].z *= rescale;
+          a[t].w *= rescale;
+        }
+#pragma unroll
+        for (int j = 0; j < MB; ++j) {
+          if (i0 + j >= npieces) continue;
+          const float f = mj[j] == -INFINITY ? 0.f : exp2f(mj[j] - Mn);
+          L = fmaf(f, lj[j], L);
+#pragma unroll
+          for (int t = 0; t < GB; ++t) {
+            a[t].x = fmaf(f, x[j][t].x, a[t].x);
+            a[t].y = fmaf(f, x[j][t].y, a[t].y);
+            a[t].z = fmaf(f, x[j][t].z, a[t].z);
+            a[t].w = fmaf(f, x[j][t].w, a[t].w);
+          }
+        }
+        M = Mn;
+      }
+      if (!active) continue;
+#pragma unroll
+      for (int t = 0; t < GB; ++t) {
+        const int col = ((lane * NG + g0 + t) & (D / 4 - 1)) * 4;
+        if (p.mode == 0) {
+          const float inv = 1.f / fmaxf(L, 1.f);
+          T* o = reinterpret_cast<T*>(p.out) + int64_t(mb) * p.o_sb + int64_t(mhq0 + g) * p.o_sh + col;
+          o[0] = E::from_float(a[t].x * inv);
+          o[1] = E::from_float(a[t].y * inv);
+          o[2] = E::from_float(a[t].z * inv);
+          o[3] = E::from_float(a[t].w * inv);
+        } else {
+          *reinterpret_cast<float4*>(p.part_acc + hrow * D + col) = a[t];
+          if (g0 == 0 && t == 0 && col == 0) {  // the lane that owns the head's first column
+            p.part_m[hrow] = M;
+            p.part_l[hrow] = L;
+          }
+        }
+      }
+    }
   };
 
   // ---- pipelined tile loop: scores of tile k+1 overlap softmax + P.V of tile k ---------
@@ -624,10 +857,10 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   for (int64_t k = 0; k < nunits; ++k) {
     const bool has_next = k + 1 < nunits;
     Cursor nxt = cur;
-    cursor_advance(nxt, pre, lens, B, items_per_row, p.n_gchunks);
+    advance(nxt);
     const int s_n = s + 1 == S ? 0 : s + 1;
     const uint32_t parity_n = s + 1 == S ? parity ^ 1u : parity;
-    if (has_next) {
+    if (!CTA && has_next) {
       if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
         fail_and_drain(k + 1);
         return;
@@ -640,9 +873,11 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     const int hq0 = cur.h * p.group + cur.gc * GT;  // first q head of this item
 
     tile_max_update(sc_cur);
-    // Straight-line region: phase A of tile k+1 (when it exists; its stage is not being
-    // written otherwise) and phase B of tile k are independent chains.
-    tile_scores(s_n, nxt.len - (nxt.tile << C::LOG_TILE), sc_nxt);
+    // Per-warp stages: phase A of tile k+1 (when it exists; its stage is not being written
+    // otherwise) and phase B of tile k are independent chains, run side by side. Shared
+    // stages: a warp holds one stage at a time, so that more of them are in flight; the
+    // CTA's other warps cover the latency instead.
+    if (!CTA) tile_scores(s_n, nxt.len - (nxt.tile << C::LOG_TILE), sc_nxt);
     if (__builtin_expect(full_tile, 1)) {
       tile_pv(s, sc_cur, valid_rows, true);
     } else {
@@ -650,11 +885,23 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     }
     __syncwarp();
 
-    // Refill the stage just consumed with the tile `stages` ahead.
-    if (issued < nunits) {
+    if (CTA) {
+      // Hand the stage just consumed back to the producer, then take the next one.
+      if (lane == 0) mbar_arrive(smem_addr(empty_bars + s));
+      if (has_next) {
+        if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
+          fail_and_drain(k + 1);
+          return;
+        }
+        patch(nxt, s_n);
+        tile_scores(s_n, nxt.len - (nxt.tile << C::LOG_TILE), sc_nxt);
+      }
+    } else if (issued < nunits) {
+      // Refill the stage just consumed with the tile `stages` ahead.
       issue(pc, s);
-      cursor_advance(pc, pre, lens, B, items_per_row, p.n_gchunks);
+      advance(pc);
       ++issued;
+      if (pc.tile == 0 && issued < nunits) prefetch_q(pc);
     }
 
     // ---- segment end ---------------------------------------------------------------------
@@ -723,7 +970,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
         }
       } else {
         // Split item: park (m, l, acc) in this worker's slot, then the last arrival merges.
-        const int64_t slot = int64_t(w) * 2 + (first_segment ? 0 : 1);
+        const int64_t slot = int64_t(wslot) * 2 + (first_segment ? 0 : 1);
         float* ml = p.ws_ml + slot * (2 * GT);
         float* wa = p.ws_acc + slot * (GT * D);
         if (lane == 0) {
@@ -747,133 +994,25 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
             }
           }
         }
-        __threadfence();
-        __syncwarp();
-        const int64_t item_global = int64_t(cur.b) * items_per_row + cur.item;
-        const int64_t us = int64_t(items_per_row) * pre[cur.b] + int64_t(cur.item) * cur.ntile;
-        const int64_t ue = us + cur.ntile;
-        const int c_first = worker_of(us, units, workers);
-        const int c_last = worker_of(ue - 1, units, workers);
-        int ticket = 0;
-        if (lane == 0) ticket = take_ticket(p.counters + item_global, epoch, p.err);
-        ticket = __shfl_sync(FULL_MASK, ticket, 0);
-        if (ticket == c_last - c_first) {
-          __threadfence();
-          // Merge the (c_last - c_first + 1) pieces of this item in one pass: lane i holds
-          // piece i's (m, l); the max, the weights 2^(m_i - M) and the normaliser come from
-          // shuffles, and the accumulators of all pieces are loaded back to back.
-          const int64_t first_start = int64_t(c_first) * units / workers;
-          const int64_t first_slot = int64_t(c_first) * 2 + (first_start == us ? 0 : 1);
-          auto slot_of = [&](int c) -> int64_t { return c == c_first ? first_slot : int64_t(c) * 2; };
-          const int npieces = c_last - c_first + 1;
-          float M[GT], Lsum[GT], wv[GT];
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            M[g] = -INFINITY;
-            Lsum[g] = 0.f;
-            wv[g] = 0.f;
-          }
-          float mv[GT], lv[GT];
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            mv[g] = -INFINITY;
-            lv[g] = 0.f;
-          }
-          if (lane < npieces) {
-            const float* sm = p.ws_ml + slot_of(c_first + lane) * (2 * GT);
-#pragma unroll
-            for (int g = 0; g < GT; ++g) {
-              mv[g] = __ldcg(sm + g);
-              lv[g] = __ldcg(sm + GT + g);
-            }
-          }
-          for (int c = c_first + 32 + lane; c <= c_last; c += 32) {  // more than 32 pieces: rare
-            const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
-#pragma unroll
-            for (int g = 0; g < GT; ++g) M[g] = fmaxf(M[g], __ldcg(sm + g));
-          }
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            M[g] = fmaxf(M[g], mv[g]);
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) M[g] = fmaxf(M[g], __shfl_xor_sync(FULL_MASK, M[g], o));
-            wv[g] = lane < npieces ? exp2f(mv[g] - M[g]) : 0.f;
-            Lsum[g] = lv[g] * wv[g];
-          }
-          for (int c = c_first + 32 + lane; c <= c_last; c += 32) {
-            const float* sm = p.ws_ml + slot_of(c) * (2 * GT);
-#pragma unroll
-            for (int g = 0; g < GT; ++g) Lsum[g] += __ldcg(sm + GT + g) * exp2f(__ldcg(sm + g) - M[g]);
-          }
-#pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) {
-#pragma unroll
-            for (int g = 0; g < GT; ++g) Lsum[g] += __shfl_xor_sync(FULL_MASK, Lsum[g], o);
-          }
-          const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
-          // Every lane runs every iteration (the shuffles below are warp-wide); only lanes
-          // with a real output element store.
-          for (int base = 0; base < GT * (D / 4); base += 32) {
-            const bool active = base + lane < GT * (D / 4);
-            const int q4 = active ? base + lane : 0;
-            const int g = q4 / (D / 4);
-            const int d = (q4 - g * (D / 4)) * 4;
-            float Mg = M[0], Lg = Lsum[0];
-#pragma unroll
-            for (int gg = 1; gg < GT; ++gg)
-              if (g == gg) { Mg = M[gg]; Lg = Lsum[gg]; }
-            // Pieces in batches of MB (8, or 4 for wide head groups to stay within the register
-            // budget): all loads of a batch are issued before any of them is used, so a merge
-            // costs ~npieces / MB L2 round trips instead of npieces.
-            constexpr int MB = (GT * C::EPL > 16) ? 4 : 8;
-            auto weight = [&](int i) -> float {  // 2^(m_i - M) of piece i for this lane's head
-              if (i < 32) {
-                float f = __shfl_sync(FULL_MASK, wv[0], i);
-#pragma unroll
-                for (int gg = 1; gg < GT; ++gg) {
-                  const float fg = __shfl_sync(FULL_MASK, wv[gg], i);
-                  if (g == gg) f = fg;
-                }
-                return f;
-              }
-              return exp2f(__ldcg(p.ws_ml + slot_of(c_first + i) * (2 * GT) + g) - Mg);
-            };
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int i0 = 0; i0 < npieces; i0 += MB) {
-              float4 x[MB];
-              float f[MB];
-#pragma unroll
-              for (int j = 0; j < MB; ++j) {
-                const int i = i0 + j < npieces ? i0 + j : npieces - 1;
-                x[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + slot_of(c_first + i) * (GT * D) + g * D + d));
-              }
-#pragma unroll
-              for (int j = 0; j < MB; ++j) f[j] = i0 + j < npieces ? weight(i0 + j) : 0.f;
-#pragma unroll
-              for (int j = 0; j < MB; ++j) {
-                a.x = fmaf(f[j], x[j].x, a.x);
-                a.y = fmaf(f[j], x[j].y, a.y);
-                a.z = fmaf(f[j], x[j].z, a.z);
-                a.w = fmaf(f[j], x[j].w, a.w);
-              }
-            }
-            if (!active) continue;
-            if (p.mode == 0) {
-              const float inv = 1.f / fmaxf(Lg, 1.f);
-              T* o = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb + int64_t(hq0 + g) * p.o_sh + d;
-              o[0] = E::from_float(a.x * inv);
-              o[1] = E::from_float(a.y * inv);
-              o[2] = E::from_float(a.z * inv);
-              o[3] = E::from_float(a.w * inv);
-            } else {
-              *reinterpret_cast<float4*>(p.part_acc + (hrow + g) * D + d) = a;
-              if (d == 0) {
-                p.part_m[hrow + g] = Mg;
-                p.part_l[hrow + g] = Lg;
-              }
-            }
-          }
+        // Arrive on the item's counter. A segment that ends inside the range arrives now, with
+        // a release-ordered add whose answer is read only after the loop (the warp keeps
+        // streaming); the other pieces of its item end later, so one of them usually merges.
+        // The range's last segment arrives after the loop. (Only a range's first and last
+        // segments can be split, so two slots suffice.)
+        if (k != nunits - 1) {
+          __syncwarp();  // every lane's partial stores precede lane 0's release
+          if (lane == 0)
+            early_old = atom_add_release_gpu(p.counters + int64_t(cur.b) * items_per_row + cur.item, 1ull);
+          early = true;
         }
+        if (n_pend == 0) {
+          pend_b0 = cur.b;
+          pend_item0 = cur.item;
+        } else {
+          pend_b1 = cur.b;
+          pend_item1 = cur.item;
+        }
+        ++n_pend;
       }
       first_segment = false;
     }
@@ -889,25 +1028,42 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     s = s_n;
     parity = parity_n;
   }
+
+  // ---- arrivals of this range's split segments; the last piece of an item merges it ----
+  // No copy is in flight any more, so the fence only waits for the partial stores.
+  if (n_pend > 0) {
+    __threadfence();
+    __syncwarp();
+    int t0 = 0, t1 = 0;
+    if (lane == 0) {
+      // An early add that beat the counter's re-tag was overwritten by it: arrive again.
+      t0 = early && uint32_t(early_old >> 32) == epoch
+               ? int(uint32_t(early_old))
+               : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, epoch, p.err);
+      if (n_pend > 1) t1 = take_ticket(p.counters + int64_t(pend_b1) * items_per_row + pend_item1, epoch, p.err);
+    }
+    merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0));
+    if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0));
+  }
 }
 
-template <typename T, int D, int GT>
-__global__ void __launch_bounds__(256, 1)
+template <typename T, int D, int GT, bool CTA>
+__global__ void __launch_bounds__(CTA ? 288 : 256, 1)
     pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) unsigned char smem[];
   uint32_t* s_epoch = reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off);
   if (threadIdx.x == 0) *s_epoch = *reinterpret_cast<volatile unsigned*>(p.epoch_word);
-  decode_body<T, D, GT>(p, kmap, vmap, smem);
+  decode_body<T, D, GT, CTA>(p, kmap, vmap, smem);
   __syncwarp();
   if ((threadIdx.x & 31) == 0)
     leave_launch(p.exit_counter, p.epoch_word, *s_epoch, gridDim.x * (blockDim.x >> 5), p.err);
 }
 
-template <typename T, int D, int GT>
+template <typename T, int D, int GT, bool CTA = false>
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                           dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
-  auto fn = pd_decode_kernel<T, D, GT>;
+  auto fn = pd_decode_kernel<T, D, GT, CTA>;
   static int attr_smem[64] = {0};  // per-device dynamic-smem opt-in already granted
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);

@@ -91,6 +91,8 @@ _SIGNATURES = {
     ),
     "pd_set_decode_tuning": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32]),
     "pd_get_decode_tuning": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 4),
+    "pd_set_decode_mode": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
+    "pd_get_decode_mode": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 3),
 }
 
 #: Names exported by the library (the header's entry points); tests check all resolve.
@@ -182,6 +184,18 @@ def set_decode_tuning(warps: int = 0, stages: int = 0, ctas_per_sm: int = 0, min
 def get_decode_tuning() -> tuple[int, int, int, int]:
     vals = [_c_i32(0) for _ in range(4)]
     check(require().pd_get_decode_tuning(*[ctypes.byref(v) for v in vals]), "pd_get_decode_tuning")
+    return tuple(int(v.value) for v in vals)
+
+
+def set_decode_mode(mode: int, shared_stages: int = 0, row_cost: int = -1) -> None:
+    """0: per-warp kernel everywhere (default), 1: shared-stage kernel where it applies;
+    row_cost: extra columns charged per row start by the column split (-1 keeps it)."""
+    check(require().pd_set_decode_mode(int(mode), int(shared_stages), int(row_cost)), "pd_set_decode_mode")
+
+
+def get_decode_mode() -> tuple[int, int, int]:
+    vals = [_c_i32(0) for _ in range(3)]
+    check(require().pd_get_decode_mode(*[ctypes.byref(v) for v in vals]), "pd_get_decode_mode")
     return tuple(int(v.value) for v in vals)
 
 

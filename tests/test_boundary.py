@@ -98,6 +98,23 @@ def test_tuning_is_validated_and_restorable():
     _native.set_decode_tuning(*before)
 
 
+def test_decode_mode_is_validated_and_restorable():
+    before = _native.get_decode_mode()
+    with pytest.raises(ValueError):
+        _native.set_decode_mode(2)
+    with pytest.raises(ValueError):
+        _native.set_decode_mode(1, 9)
+    assert _native.get_decode_mode() == before
+    with pytest.raises(ValueError):
+        _native.set_decode_mode(0, 0, 65)
+    _native.set_decode_mode(1, 3, 5)
+    assert _native.get_decode_mode() == (1, 3, 5)
+    _native.set_decode_mode(0, 0, -1)
+    assert _native.get_decode_mode() == (0, 0, 5)
+    _native.set_decode_mode(*before)
+    assert _native.get_decode_mode() == before
+
+
 # ------------------------------------------------------------ Python surface (no GPU needed)
 
 
