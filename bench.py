@@ -424,10 +424,53 @@ def profile_case(name: str, launches: int = 4) -> None:
     print(json.dumps({"profile_case": name, "launches": launches, "kv_bytes": wl.kv_bytes_per_layer()}))
 
 
+def config_sweep(reps: int = 5) -> None:
+    """The decode kernel alone on every BASELINE config: each layer's plan launch once, the
+    layers back to back in a CUDA graph (distinct per-layer pools, so every launch reads cold
+    HBM), best and median of ``reps`` replays. One JSON line per config (not the bench line)."""
+    from model import _native
+    from model.triton_decode import paged_decode_plan
+    from serve import workloads
+
+    device = torch.device("cuda", 0)
+    peak = _peaks()["hbm_gbs"]
+    for name, n_layer in (("config1", 28), ("config2", 28), ("config3", 28), ("config4", 4), ("config5", 2)):
+        wl = getattr(workloads, name)(device, n_layer=n_layer)
+        plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
+        for layer in range(n_layer):
+            plan.run(layer, wl.q[layer])
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for layer in range(n_layer):
+                plan.run(layer, wl.q[layer])
+        graph.replay()
+        times = []
+        for _ in range(reps):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            graph.replay()
+            stop.record()
+            torch.cuda.synchronize(device)
+            times.append(start.elapsed_time(stop) * 1e3 / n_layer)
+        if _native.device_error() != 0:
+            raise SystemExit(f"{name}: device error word set")
+        kv = wl.kv_bytes_per_layer()
+        best, med = min(times), statistics.median(times)
+        print(json.dumps({"config": name, "rows": int(wl.q[0].shape[0]), "layers": n_layer,
+                          "kv_bytes_per_launch": kv, "us_per_launch_best": round(best, 2),
+                          "us_per_launch_median": round(med, 2), "kv_gbs_best": round(kv / best / 1e3, 1),
+                          "roofline_frac_best": round(kv / best / 1e3 / peak, 4), "peak_gbs": peak}), flush=True)
+        del graph, plan, wl
+        torch.cuda.empty_cache()
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--profile-case", default=None,
                         help="run a short profiler case (config1..config5) instead of the benchmark")
+    parser.add_argument("--configs", action="store_true",
+                        help="time the decode kernel alone on every BASELINE config instead of the benchmark")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=100)
     parser.add_argument("--warmup", type=int, default=5)
@@ -436,6 +479,9 @@ def main(argv=None) -> int:
     args = parser.parse_args(argv)
     if args.profile_case:
         profile_case(args.profile_case)
+        return 0
+    if args.configs:
+        config_sweep()
         return 0
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
