@@ -18,7 +18,8 @@ ranks device time); ``us_per_layer_step``; ``roofline`` of the decode kernel wit
 duration bounded by the timed region / decode launches (a replay runs the decode launches back
 to back plus six tiny bookkeeping kernels per step);
 ``e2e`` = the same metric through the public API with every step's q/k/v copied from pinned
-host memory into the graph's input buffers and all outputs copied back;
+host memory into a step graph's input buffers and all outputs copied back, the copies on a
+second stream overlapping the neighbouring steps (two step graphs alternate);
 ``cpu_baseline`` = the reference's CPU gather + seat-decode path (ported, oracle/) on a
 bounded sample of the same workload using every host core.
 
@@ -289,34 +290,63 @@ def run_gpu(args) -> dict | None:
 
 
 def _run_e2e(kv, graph, device, stream, rank, steps, dist) -> dict:
-    """The same steps through the public API with host buffers: every step copies its
-    per-layer q/k/v from pinned host memory into the step graph's input buffers, replays the
-    step and copies all layers' attention outputs back (all inside the timed region)."""
+    """The same steps through the public API with host buffers. Every step copies its
+    per-layer q/k/v from pinned host memory into a step graph's input buffers, replays the
+    step and copies all layers' attention outputs back to pinned host memory, all inside the
+    timed region. As a serving loop would, the copies run on a second stream and overlap the
+    neighbouring steps' compute: two captured step graphs alternate, so step i+1's inputs
+    land while step i computes and step i's outputs leave while step i+1 computes (events
+    order every buffer reuse)."""
+    from serve.graph import PagedStepGraph
+
     gen = torch.Generator().manual_seed(99 + rank)
     hq = torch.randn(tuple(graph.q.shape), generator=gen).to(torch.bfloat16).pin_memory()
     hk = torch.randn(tuple(graph.k.shape), generator=gen).to(torch.bfloat16).pin_memory()
     hv = torch.randn(tuple(graph.v.shape), generator=gen).to(torch.bfloat16).pin_memory()
-    hout = torch.empty(tuple(graph.out.shape), dtype=torch.bfloat16).pin_memory()
-    kv_bytes = 0
+    hout = torch.empty((2,) + tuple(graph.out.shape), dtype=torch.bfloat16).pin_memory()
+    graphs = [graph, PagedStepGraph(kv, torch.empty_like(graph.q), torch.empty_like(graph.k),
+                                    torch.empty_like(graph.v))]
+    copy = torch.cuda.Stream(device)
+    ready = [torch.cuda.Event() for _ in range(2)]  # inputs of the buffer set are in place
+    done = [torch.cuda.Event() for _ in range(2)]   # the step that used the buffer set finished
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def upload(g, i):
+        g.q.copy_(hq, non_blocking=True)
+        g.k.copy_(hk, non_blocking=True)
+        g.v.copy_(hv, non_blocking=True)
+        ready[i % 2].record(copy)
+
+    kv_bytes = 0
     _barrier(dist, device)
     start.record(stream)
-    for _ in range(steps):
+    copy.wait_stream(stream)
+    with torch.cuda.stream(copy):
+        upload(graphs[0], 0)
+    for i in range(steps):
+        g = graphs[i % 2]
         kv_bytes += sum(p + 1 for p in kv._host_pos) * 2 * H_KV * D * 2 * N_LAYER
-        graph.q.copy_(hq, non_blocking=True)
-        graph.k.copy_(hk, non_blocking=True)
-        graph.v.copy_(hv, non_blocking=True)
-        out = graph.replay()
-        hout.copy_(out, non_blocking=True)
+        stream.wait_event(ready[i % 2])
+        g.replay()
+        done[i % 2].record(stream)
+        with torch.cuda.stream(copy):
+            if i + 1 < steps:  # the other set was last used by step i - 1
+                if i >= 1:
+                    copy.wait_event(done[(i + 1) % 2])
+                upload(graphs[(i + 1) % 2], i + 1)
+            copy.wait_event(done[i % 2])
+            hout[i % 2].copy_(g.out, non_blocking=True)
+    stream.wait_stream(copy)
     stop.record(stream)
     _barrier(dist, device)
     ms = _max_over_ranks(dist, start.elapsed_time(stop), device)
     total = _sum_over_ranks(dist, float(kv_bytes), device)
     h2d = (hq.numel() + hk.numel() + hv.numel()) * 2
-    d2h = hout.numel() * 2
+    d2h = graph.out.numel() * 2
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s (KV bytes read by decode, all ranks)",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "us_per_layer_step": round(ms * 1e3 / (steps * N_LAYER), 2)}
+            "us_per_layer_step": round(ms * 1e3 / (steps * N_LAYER), 2),
+            "copies": "overlapped with neighbouring steps on a second stream (two step graphs alternate)"}
 
 
 def _profiled_traffic(algorithmic_bytes: float):
@@ -425,7 +455,8 @@ def profile_case(name: str, launches: int = 4) -> None:
 
 
 def config_sweep(reps: int = 5) -> None:
-    """The decode kernel alone on every BASELINE config: each layer's plan launch once, the
+    """The decode kernel alone on every BASELINE config (and the hybrid Qwen3.5 engine's
+    full-attention shape): each layer's plan launched once, the
     layers back to back in a CUDA graph (distinct per-layer pools, so every launch reads cold
     HBM), best and median of ``reps`` replays. One JSON line per config (not the bench line)."""
     from model import _native
@@ -434,7 +465,8 @@ def config_sweep(reps: int = 5) -> None:
 
     device = torch.device("cuda", 0)
     peak = _peaks()["hbm_gbs"]
-    for name, n_layer in (("config1", 28), ("config2", 28), ("config3", 28), ("config4", 4), ("config5", 2)):
+    for name, n_layer in (("config1", 28), ("config2", 28), ("config3", 28), ("config4", 4), ("config5", 2),
+                          ("qwen35", 6)):
         wl = getattr(workloads, name)(device, n_layer=n_layer)
         plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
         for layer in range(n_layer):

@@ -166,6 +166,20 @@ int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, vo
 int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
                        const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
                        int64_t v_sb, int64_t v_sh, const int64_t* pos, void* stream);
+
+/* pd_plan_run_append_rope -- pd_plan_run_append with the new K rows given BEFORE their
+ * rotary embedding: the model's `k = apply_rotary_emb_partial(k, cos, sin, rotary_dim)`
+ * (model/layers.py:59-117, called at layers.py:210-211 and qwen35.py:207-211) happens
+ * inside the same launch. GPT-NeoX pairing (i, i + rotary_dim / 2) over the first
+ * rotary_dim elements, the rest passing through; every product and sum is rounded to the
+ * plan's dtype exactly as torch's elementwise ops round, so the stored rows are bit-identical
+ * to rotating with torch and appending. rope_cos / rope_sin: row b's table at
+ * rope_cos + b * rope_stride (elements), rotary_dim / 2 entries, the plan's dtype. */
+int pd_plan_run_append_rope(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                            const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                            int64_t v_sb, int64_t v_sh, const int64_t* pos, const void* rope_cos,
+                            const void* rope_sin, int64_t rope_stride, int32_t rotary_dim,
+                            void* stream);
 void pd_plan_destroy(pd_plan* plan);
 
 /* ---------------------------------------------------------------- split-KV partials
@@ -231,6 +245,18 @@ int pd_kv_append_table(void* k_pool, void* v_pool, int64_t n_blocks, int32_t blo
                        const int64_t* k_strides, const void* v, const int64_t* v_strides,
                        int32_t src_dtype, int32_t batch, int32_t n_kv_head, int32_t head_dim,
                        void* stream);
+
+/* pd_kv_append_table_rope -- pd_kv_append_table with the K rows rotated first, exactly as
+ * pd_plan_run_append_rope rotates them (source, pool and tables share one dtype; row b's
+ * tables at rope_cos / rope_sin + b * rope_stride). */
+int pd_kv_append_table_rope(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                            const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                            int32_t pool_dtype, const int32_t* block_table, int64_t bt_stride,
+                            int32_t max_blocks, const int64_t* pos, const void* k,
+                            const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            int32_t src_dtype, int32_t batch, int32_t n_kv_head, int32_t head_dim,
+                            const void* rope_cos, const void* rope_sin, int64_t rope_stride,
+                            int32_t rotary_dim, void* stream);
 
 /* ---------------------------------------------------------------- tuning / introspection
  * Launch shape of the decode kernel: warps per CTA, pipeline stages per warp, CTAs per SM

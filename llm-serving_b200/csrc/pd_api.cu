@@ -327,6 +327,14 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   return PD_OK;
 }
 
+// Rotary tables: a positive even width that fits the head, row stride >= width / 2, and
+// one dtype for the K source, the pool and the tables.
+bool rope_args_ok(const void* rope_cos, const void* rope_sin, int64_t rope_stride, int32_t rotary_dim,
+                         int32_t head_dim, int32_t src_dtype, int32_t pool_dtype) {
+  return rope_cos != nullptr && rope_sin != nullptr && rotary_dim >= 2 && rotary_dim % 2 == 0 &&
+         rotary_dim <= head_dim && rope_stride >= rotary_dim / 2 && src_dtype == pool_dtype;
+}
+
 int check_rows(const void* ptr, int64_t sb, int64_t sh, int dtype) {
   const int es = elem_size(dtype);
   if (ptr == nullptr || !aligned16(ptr)) return PD_ERR_INVALID;
@@ -346,6 +354,10 @@ struct AppendArgs {
   const int64_t* k_strides;  // pool element strides: block, token, head
   const int64_t* v_strides;
   int64_t n_blocks;
+  const void* rope_cos;  // rotary tables of the appended K rows, or nullptr
+  const void* rope_sin;
+  int64_t rope_stride;
+  int32_t rope_dim;
 };
 
 // Launches the decode kernel over the batch in chunks of rows_per_launch rows.
@@ -394,6 +406,12 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
       p.pv_sn = app->v_strides[1];
       p.pv_sh = app->v_strides[2];
       p.n_blocks = app->n_blocks;
+      if (app->rope_cos != nullptr) {
+        p.rope_cos = static_cast<const unsigned char*>(app->rope_cos) + int64_t(b0) * app->rope_stride * es;
+        p.rope_sin = static_cast<const unsigned char*>(app->rope_sin) + int64_t(b0) * app->rope_stride * es;
+        p.rope_stride = app->rope_stride;
+        p.rope_dim = app->rope_dim;
+      }
     }
     const size_t smem = smem_for(P.g.cta, P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
                                  &p.smem_stage_off);
@@ -580,9 +598,10 @@ int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, vo
                       static_cast<cudaStream_t>(stream));
 }
 
-int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
-                       const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
-                       int64_t v_sb, int64_t v_sh, const int64_t* pos, void* stream) {
+static int plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                           const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                           int64_t v_sb, int64_t v_sh, const int64_t* pos, const void* rope_cos,
+                           const void* rope_sin, int64_t rope_stride, int32_t rotary_dim, void* stream) {
   if (plan == nullptr || layer < 0 || layer >= plan->n_layer) return PD_ERR_INVALID;
   if (check_rows(q, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
   if (check_rows(out, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
@@ -602,9 +621,32 @@ int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* 
   app.k_strides = plan->k_strides;
   app.v_strides = plan->v_strides;
   app.n_blocks = plan->n_blocks;
+  app.rope_cos = rope_cos;
+  app.rope_sin = rope_sin;
+  app.rope_stride = rope_stride;
+  app.rope_dim = rotary_dim;
   return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
                       plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
                       static_cast<cudaStream_t>(stream), &app);
+}
+
+int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                       const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                       int64_t v_sb, int64_t v_sh, const int64_t* pos, void* stream) {
+  return plan_run_append(plan, layer, q, out, k_new, k_sb, k_sh, v_new, v_sb, v_sh, pos, nullptr, nullptr,
+                         0, 0, stream);
+}
+
+int pd_plan_run_append_rope(const pd_plan* plan, int32_t layer, const void* q, void* out,
+                            const void* k_new, int64_t k_sb, int64_t k_sh, const void* v_new,
+                            int64_t v_sb, int64_t v_sh, const int64_t* pos, const void* rope_cos,
+                            const void* rope_sin, int64_t rope_stride, int32_t rotary_dim, void* stream) {
+  if (plan == nullptr) return PD_ERR_INVALID;
+  const int32_t head_dim = int32_t(plan->q_sh);  // q rows are contiguous (B, H, D)
+  if (!rope_args_ok(rope_cos, rope_sin, rope_stride, rotary_dim, head_dim, plan->dtype, plan->dtype))
+    return PD_ERR_INVALID;
+  return plan_run_append(plan, layer, q, out, k_new, k_sb, k_sh, v_new, v_sb, v_sh, pos, rope_cos, rope_sin,
+                         rope_stride, rotary_dim, stream);
 }
 
 void pd_plan_destroy(pd_plan* plan) { delete plan; }
@@ -729,6 +771,40 @@ int pd_kv_append_table(void* k_pool, void* v_pool, int64_t n_blocks, int32_t blo
   p.n_kv_head = n_kv_head;
   p.head_dim = head_dim;
   p.use_table = 1;
+  return append_common(p, pool_dtype, src_dtype, k_pool_strides, v_pool_strides, k_strides,
+                       v_strides, stream);
+}
+
+int pd_kv_append_table_rope(void* k_pool, void* v_pool, int64_t n_blocks, int32_t block_size,
+                            const int64_t* k_pool_strides, const int64_t* v_pool_strides,
+                            int32_t pool_dtype, const int32_t* block_table, int64_t bt_stride,
+                            int32_t max_blocks, const int64_t* pos, const void* k,
+                            const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            int32_t src_dtype, int32_t batch, int32_t n_kv_head, int32_t head_dim,
+                            const void* rope_cos, const void* rope_sin, int64_t rope_stride,
+                            int32_t rotary_dim, void* stream) {
+  if (!rope_args_ok(rope_cos, rope_sin, rope_stride, rotary_dim, head_dim, src_dtype, pool_dtype))
+    return PD_ERR_INVALID;
+  if (batch > 0 && (block_table == nullptr || pos == nullptr || max_blocks < 1)) return PD_ERR_INVALID;
+  AppendParams p{};
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.n_blocks = n_blocks;
+  p.table = block_table;
+  p.bt_stride = bt_stride;
+  p.max_blocks = max_blocks;
+  p.pos = pos;
+  p.k = k;
+  p.v = v;
+  p.n_tokens = batch;
+  p.block_size = block_size;
+  p.n_kv_head = n_kv_head;
+  p.head_dim = head_dim;
+  p.use_table = 1;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rope_stride = rope_stride;
+  p.rope_dim = rotary_dim;
   return append_common(p, pool_dtype, src_dtype, k_pool_strides, v_pool_strides, k_strides,
                        v_strides, stream);
 }

@@ -9,6 +9,8 @@
 // kernel). Same-dtype copies are bit copies; a dtype change rounds to nearest even, which is
 // what torch's Tensor.to does. A slot or block id outside the pool is skipped and recorded
 // in the device error word (the reference's index_copy_ would raise a device assert).
+// Optionally the K rows get their rotary embedding on the way in (the rotation the model
+// applies just before the write, model/layers.py apply_rotary_emb_partial).
 #include "pd_internal.h"
 
 namespace pd {
@@ -94,11 +96,22 @@ __global__ void __launch_bounds__(256) pd_append_kernel(const AppendParams p) {
       if (rem == 0) atomicOr(p.err, DEVERR_APPEND_RANGE);
       continue;
     }
-    const S* ks = reinterpret_cast<const S*>(p.k) + t * p.k_s0 + h * p.k_s1 + d;
+    const S* krow = reinterpret_cast<const S*>(p.k) + t * p.k_s0 + h * p.k_s1;
     const S* vs = reinterpret_cast<const S*>(p.v) + t * p.v_s0 + h * p.v_s1 + d;
     Dt* kd = reinterpret_cast<Dt*>(p.k_pool) + blk * p.kp_sb + off * p.kp_sn + h * p.kp_sh + d;
     Dt* vd = reinterpret_cast<Dt*>(p.v_pool) + blk * p.vp_sb + off * p.vp_sn + h * p.vp_sh + d;
-    Mover<S, Dt, V>::move(kd, ks);
+    if constexpr (std::is_same<S, Dt>::value) {
+      if (p.rope_cos != nullptr) {  // K rotated first (same dtype throughout, checked on the host)
+        const S* cs = reinterpret_cast<const S*>(p.rope_cos) + t * p.rope_stride;
+        const S* sn = reinterpret_cast<const S*>(p.rope_sin) + t * p.rope_stride;
+#pragma unroll
+        for (int j = 0; j < V; ++j) kd[j] = rope_elem(krow, cs, sn, d + j, p.rope_dim);
+      } else {
+        Mover<S, Dt, V>::move(kd, krow + d);
+      }
+    } else {
+      Mover<S, Dt, V>::move(kd, krow + d);
+    }
     Mover<S, Dt, V>::move(vd, vs);
   }
 }

@@ -213,6 +213,48 @@ struct Elem<__half> {
   __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
 };
 
+// ------------------------------------------------------------------ rotary embedding
+
+// Element e of a head row x after GPT-NeoX rotary embedding over its first rot_dim elements
+// (pairs (i, i + rot_dim / 2); elements past rot_dim pass through), with the rounding of
+// torch's elementwise ops in the row's dtype (model/layers.py apply_rotary_emb_partial):
+//   out[i]        = r(r(x1 * cos) - r(x2 * sin))
+//   out[i + half] = r(r(x1 * sin) + r(x2 * cos))
+// where r() rounds to T. Every operation is an explicitly rounded fp32 op, never contracted
+// into an FMA, so every thread that computes an element gets the same bits.
+template <typename T>
+__device__ __forceinline__ T rope_elem(const T* x, const T* cos, const T* sin, int e, int rot_dim) {
+  using E = Elem<T>;
+  if (e >= rot_dim) return x[e];
+  const int half = rot_dim >> 1;
+  const int i = e < half ? e : e - half;
+  const float x1 = E::to_float(x[i]), x2 = E::to_float(x[i + half]);
+  const float c = E::to_float(cos[i]), s = E::to_float(sin[i]);
+  if (e < half) {
+    const float a = E::to_float(E::from_float(__fmul_rn(x1, c)));
+    const float b = E::to_float(E::from_float(__fmul_rn(x2, s)));
+    return E::from_float(__fsub_rn(a, b));
+  }
+  const float a = E::to_float(E::from_float(__fmul_rn(x1, s)));
+  const float b = E::to_float(E::from_float(__fmul_rn(x2, c)));
+  return E::from_float(__fadd_rn(a, b));
+}
+
+// The 16-byte chunk of the rotated row x that starts at element e0. Kept out of line: the
+// decode kernel calls it only for the appended row of a tile, and inlining it into the
+// streaming loop costs registers there.
+template <typename T>
+__device__ __noinline__ uint4 rope_chunk(const T* x, const T* cos, const T* sin, int e0, int rot_dim) {
+  constexpr int N = 16 / int(sizeof(T));
+  union {
+    T v[N];
+    uint4 u;
+  } out;
+#pragma unroll
+  for (int j = 0; j < N; ++j) out.v[j] = rope_elem(x, cos, sin, e0 + j, rot_dim);
+  return out.u;
+}
+
 // ------------------------------------------------------------------ parameter blocks
 
 // Everything the decode kernel reads besides the two TMA descriptors. Element strides.
@@ -270,6 +312,12 @@ struct DecodeParams {
   int64_t pk_sb, pk_sn, pk_sh;  // pool element strides: block, token, head
   int64_t pv_sb, pv_sn, pv_sh;
   int64_t n_blocks;
+  // Rotary embedding of the appended K rows (rope_cos == nullptr: none). Row b uses
+  // rope_cos/rope_sin + b * rope_stride (rope_dim / 2 entries each, the pool dtype).
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_stride;
+  int32_t rope_dim;
 };
 
 struct AppendParams {
@@ -293,6 +341,12 @@ struct AppendParams {
   int32_t head_dim;
   int32_t use_table;  // 1: slot from block table + pos, 0: from slots
   int32_t slot_i64;
+  // Rotary embedding of the K rows before they are stored (rope_cos == nullptr: none);
+  // source, pool and tables share one dtype. Token t uses rope_cos/rope_sin + t * rope_stride.
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_stride;
+  int32_t rope_dim;
 };
 
 struct MergeParams {

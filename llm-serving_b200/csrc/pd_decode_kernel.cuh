@@ -221,6 +221,13 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   // bytes of these slots (their copies are not ordered after the stores); the consumer
   // overwrites those rows from the source, so the result never depends on which bytes a
   // copy saw.
+  // Chunk c of row b's appended K row, rotated when the launch carries rotary tables (the
+  // patch below computes the same bits for the tile that reads it).
+  auto appended_k_chunk = [&](const T* ksrc, int b, int c) -> uint4 {
+    const T* cs = reinterpret_cast<const T*>(p.rope_cos) + int64_t(b) * p.rope_stride;
+    const T* sn = reinterpret_cast<const T*>(p.rope_sin) + int64_t(b) * p.rope_stride;
+    return rope_chunk(ksrc, cs, sn, c * C::EPC, p.rope_dim);
+  };
   auto store_appended = [&]() {
     if (!p.append) return;
     constexpr int CH = C::CHUNKS;
@@ -249,7 +256,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
                         : reinterpret_cast<const T*>(p.app_k) + int64_t(b) * p.app_k_sb + int64_t(h) * p.app_k_sh;
       T* dst = kv ? reinterpret_cast<T*>(p.pool_v) + blk * p.pv_sb + off * p.pv_sn + int64_t(h) * p.pv_sh
                   : reinterpret_cast<T*>(p.pool_k) + blk * p.pk_sb + off * p.pk_sn + int64_t(h) * p.pk_sh;
-      *reinterpret_cast<uint4*>(dst + c * C::EPC) = __ldg(reinterpret_cast<const uint4*>(src + c * C::EPC));
+      *reinterpret_cast<uint4*>(dst + c * C::EPC) =
+          !kv && p.rope_cos ? appended_k_chunk(src, b, c) : __ldg(reinterpret_cast<const uint4*>(src + c * C::EPC));
     }
   };
 
@@ -724,7 +732,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     for (int i = lane; i < 2 * C::CHUNKS; i += 32) {
       const bool isv = i >= C::CHUNKS;
       const int ci = isv ? i - C::CHUNKS : i;
-      const uint4 x = __ldg(reinterpret_cast<const uint4*>((isv ? vsrc : ksrc) + ci * C::EPC));
+      const uint4 x = !isv && p.rope_cos ? appended_k_chunk(ksrc, c.b, ci)
+                                         : __ldg(reinterpret_cast<const uint4*>((isv ? vsrc : ksrc) + ci * C::EPC));
       *reinterpret_cast<uint4*>((isv ? vrow : krow) + ci * 16) = x;
     }
     fence_proxy_async_smem();  // the stage is refilled by TMA later
@@ -765,76 +774,109 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     auto slot_of = [&](int i) -> int64_t { return i == 0 ? first_slot : pair_of(c_first + i) * 2; };
     const int mh = mitem / p.n_gchunks;
     const int mhq0 = mh * p.group + (mitem - mh * p.n_gchunks) * GT;
-    constexpr int GROUPS = GT * (D / 4);             // float4 groups of the item's output
-    constexpr int NG = GROUPS >= 32 ? GROUPS / 32 : 1;  // groups per lane
-    constexpr int GB = NG < 8 ? NG : 8;              // groups per pass
-    constexpr int MB = GB == 1 ? 8 : (GB == 2 ? 6 : 8 / GB);  // pieces per batch
-    const bool active = lane * NG < GROUPS;
-    const int g = active ? (lane * NG) / (D / 4) : 0;  // the lane's q head within the item
-    const int64_t hrow = int64_t(mb) * p.n_head + mhq0 + g;
-    for (int g0 = 0; g0 < NG; g0 += GB) {
-      float M = -INFINITY, L = 0.f;
+    // The item's output is GROUPS float4 groups, head-major; lane l owns groups t * 32 + l,
+    // so each load instruction of the warp reads 512 contiguous bytes of a partial. Every lane
+    // keeps the running maximum and normaliser of all GT heads (from broadcast loads).
+    constexpr int GROUPS = GT * (D / 4);
+    constexpr int GPH = D / 4;                           // groups per head
+    constexpr int NG = GROUPS >= 32 ? GROUPS / 32 : 1;   // groups per lane
+    constexpr int GB = NG < 8 ? NG : 8;                  // groups per pass
+    constexpr int MB = GB >= 8 ? (GT >= 8 ? 2 : 3) : 16 / GB;  // pieces per batch
+    auto head_of = [&](int t) -> int {  // head of the lane's group t (static when GPH >= 32)
+      return (t * 32) / GPH + (GPH >= 32 ? 0 : lane / GPH);
+    };
+    auto pick = [&](const float (&v)[GT], int g) -> float {
+      float r = v[0];
+#pragma unroll
+      for (int gg = 1; gg < GT; ++gg)
+        if (g == gg) r = v[gg];
+      return r;
+    };
+    const int64_t hrow0 = int64_t(mb) * p.n_head + mhq0;
+    for (int t0 = 0; t0 < NG; t0 += GB) {
+      float M[GT], L[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        M[g] = -INFINITY;
+        L[g] = 0.f;
+      }
       float4 a[GB];
 #pragma unroll
       for (int t = 0; t < GB; ++t) a[t] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int i0 = 0; i0 < npieces; i0 += MB) {
-        float mj[MB], lj[MB];
+        float mj[MB][GT], lj[MB][GT];
         float4 x[MB][GB];
 #pragma unroll
         for (int j = 0; j < MB; ++j) {
           const int64_t sl = slot_of(i0 + j < npieces ? i0 + j : npieces - 1);
-          mj[j] = __ldcg(p.ws_ml + sl * (2 * GT) + g);
-          lj[j] = __ldcg(p.ws_ml + sl * (2 * GT) + GT + g);
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            mj[j][g] = __ldcg(p.ws_ml + sl * (2 * GT) + g);
+            lj[j][g] = __ldcg(p.ws_ml + sl * (2 * GT) + GT + g);
+          }
 #pragma unroll
           for (int t = 0; t < GB; ++t) {
-            const int col = ((lane * NG + g0 + t) & (D / 4 - 1)) * 4;
-            x[j][t] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D) + g * D + col));
+            const int jg = (t0 + t) * 32 + lane;
+            x[j][t] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D)) + (jg < GROUPS ? jg : 0));
           }
         }
-        float Mn = M;
+        float Mn[GT], rs[GT];
 #pragma unroll
-        for (int j = 0; j < MB; ++j)
-          if (i0 + j < npieces) Mn = fmaxf(Mn, mj[j]);
-        const float rescale = M == Mn ? 1.f : exp2f(M - Mn);
-        L *= rescale;
+        for (int g = 0; g < GT; ++g) {
+          Mn[g] = M[g];
+#pragma unroll
+          for (int j = 0; j < MB; ++j)
+            if (i0 + j < npieces) Mn[g] = fmaxf(Mn[g], mj[j][g]);
+          rs[g] = M[g] == Mn[g] ? 1.f : exp2f(M[g] - Mn[g]);
+          L[g] *= rs[g];
+        }
 #pragma unroll
         for (int t = 0; t < GB; ++t) {
-          a[t].x *= rescale;
-          a[t].y *= rescale;
-          a[t].z *= rescale;
-          a[t].w *= rescale;
+          const float r = pick(rs, head_of(t0 + t));
+          a[t].x *= r;
+          a[t].y *= r;
+          a[t].z *= r;
+          a[t].w *= r;
         }
 #pragma unroll
         for (int j = 0; j < MB; ++j) {
           if (i0 + j >= npieces) continue;
-          const float f = mj[j] == -INFINITY ? 0.f : exp2f(mj[j] - Mn);
-          L = fmaf(f, lj[j], L);
+          float f[GT];
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            f[g] = mj[j][g] == -INFINITY ? 0.f : exp2f(mj[j][g] - Mn[g]);
+            L[g] = fmaf(f[g], lj[j][g], L[g]);
+          }
 #pragma unroll
           for (int t = 0; t < GB; ++t) {
-            a[t].x = fmaf(f, x[j][t].x, a[t].x);
-            a[t].y = fmaf(f, x[j][t].y, a[t].y);
-            a[t].z = fmaf(f, x[j][t].z, a[t].z);
-            a[t].w = fmaf(f, x[j][t].w, a[t].w);
+            const float ft = pick(f, head_of(t0 + t));
+            a[t].x = fmaf(ft, x[j][t].x, a[t].x);
+            a[t].y = fmaf(ft, x[j][t].y, a[t].y);
+            a[t].z = fmaf(ft, x[j][t].z, a[t].z);
+            a[t].w = fmaf(ft, x[j][t].w, a[t].w);
           }
         }
-        M = Mn;
+#pragma unroll
+        for (int g = 0; g < GT; ++g) M[g] = Mn[g];
       }
-      if (!active) continue;
 #pragma unroll
       for (int t = 0; t < GB; ++t) {
-        const int col = ((lane * NG + g0 + t) & (D / 4 - 1)) * 4;
+        const int jg = (t0 + t) * 32 + lane;
+        if (jg >= GROUPS) continue;
+        const int g = head_of(t0 + t);
+        const int col = (jg % GPH) * 4;
         if (p.mode == 0) {
-          const float inv = 1.f / fmaxf(L, 1.f);
+          const float inv = 1.f / fmaxf(pick(L, g), 1.f);
           T* o = reinterpret_cast<T*>(p.out) + int64_t(mb) * p.o_sb + int64_t(mhq0 + g) * p.o_sh + col;
           o[0] = E::from_float(a[t].x * inv);
           o[1] = E::from_float(a[t].y * inv);
           o[2] = E::from_float(a[t].z * inv);
           o[3] = E::from_float(a[t].w * inv);
         } else {
-          *reinterpret_cast<float4*>(p.part_acc + hrow * D + col) = a[t];
-          if (g0 == 0 && t == 0 && col == 0) {  // the lane that owns the head's first column
-            p.part_m[hrow] = M;
-            p.part_l[hrow] = L;
+          *reinterpret_cast<float4*>(p.part_acc + (hrow0 + g) * D + col) = a[t];
+          if (col == 0) {  // the lane that owns the head's first column
+            p.part_m[hrow0 + g] = pick(M, g);
+            p.part_l[hrow0 + g] = pick(L, g);
           }
         }
       }

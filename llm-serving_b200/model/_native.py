@@ -78,6 +78,11 @@ _SIGNATURES = {
         ctypes.c_int,
         [_c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr],
     ),
+    "pd_plan_run_append_rope": (
+        ctypes.c_int,
+        [_c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr,
+         _c_ptr, _c_i64, _c_i32, _c_ptr],
+    ),
     "pd_plan_destroy": (None, [_c_ptr]),
     "pd_kv_append_slots": (
         ctypes.c_int,
@@ -88,6 +93,12 @@ _SIGNATURES = {
         ctypes.c_int,
         [_c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_i32, _c_ptr, _c_i64, _c_i32, _c_ptr,
          _c_ptr, _c_i64p, _c_ptr, _c_i64p, _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr],
+    ),
+    "pd_kv_append_table_rope": (
+        ctypes.c_int,
+        [_c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_i32, _c_ptr, _c_i64, _c_i32, _c_ptr,
+         _c_ptr, _c_i64p, _c_ptr, _c_i64p, _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_i64, _c_i32,
+         _c_ptr],
     ),
     "pd_set_decode_tuning": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32]),
     "pd_get_decode_tuning": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 4),
@@ -276,15 +287,23 @@ def append_slots(k_pool, v_pool, slot_ids, k, v) -> None:
     check(status, "pd_kv_append_slots")
 
 
-def append_table(k_pool, v_pool, block_table, pos, k, v) -> None:
+def append_table(k_pool, v_pool, block_table, pos, k, v, rope=None) -> None:
+    """``rope`` = (cos, sin, rotary_dim): rotate the K rows first; cos/sin (B, rotary_dim / 2)
+    with a unit last stride, in the pool dtype."""
     n_blocks, bs, hkv, D = k_pool.shape
-    status = require().pd_kv_append_table(
+    args = (
         k_pool.data_ptr(), v_pool.data_ptr(), n_blocks, bs, strides3(k_pool), strides3(v_pool),
         dtype_code(k_pool.dtype), block_table.data_ptr(), block_table.stride(0),
         block_table.shape[1], pos.data_ptr(), k.data_ptr(), strides3(k), v.data_ptr(), strides3(v),
-        dtype_code(k.dtype), k.shape[0], hkv, D, stream_handle(k_pool.device),
+        dtype_code(k.dtype), k.shape[0], hkv, D,
     )
-    check(status, "pd_kv_append_table")
+    if rope is None:
+        check(require().pd_kv_append_table(*args, stream_handle(k_pool.device)), "pd_kv_append_table")
+        return
+    cos, sin, rotary_dim = rope
+    status = require().pd_kv_append_table_rope(*args, cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+                                               int(rotary_dim), stream_handle(k_pool.device))
+    check(status, "pd_kv_append_table_rope")
 
 
 class NativePlan:
@@ -316,14 +335,21 @@ class NativePlan:
         if status:
             check(status, "pd_plan_run")
 
-    def run_append(self, layer: int, q, out, k_new, v_new, pos, stream: int) -> None:
-        """Append ``k_new``/``v_new`` ``(B, H_kv, D)`` at ``pos`` (int64) and decode, one launch."""
-        status = self._lib.pd_plan_run_append(
-            self._handle, layer, q.data_ptr(), out.data_ptr(), k_new.data_ptr(), k_new.stride(0),
-            k_new.stride(1), v_new.data_ptr(), v_new.stride(0), v_new.stride(1), pos.data_ptr(), stream,
-        )
+    def run_append(self, layer: int, q, out, k_new, v_new, pos, stream: int, rope=None) -> None:
+        """Append ``k_new``/``v_new`` ``(B, H_kv, D)`` at ``pos`` (int64) and decode, one launch;
+        ``rope`` = (cos, sin, rotary_dim) rotates ``k_new`` first (see :func:`append_table`)."""
+        args = (self._handle, layer, q.data_ptr(), out.data_ptr(), k_new.data_ptr(), k_new.stride(0),
+                k_new.stride(1), v_new.data_ptr(), v_new.stride(0), v_new.stride(1), pos.data_ptr())
+        if rope is None:
+            status = self._lib.pd_plan_run_append(*args, stream)
+            name = "pd_plan_run_append"
+        else:
+            cos, sin, rotary_dim = rope
+            status = self._lib.pd_plan_run_append_rope(*args, cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+                                                       int(rotary_dim), stream)
+            name = "pd_plan_run_append_rope"
         if status:
-            check(status, "pd_plan_run_append")
+            check(status, name)
 
     def __del__(self) -> None:
         handle = getattr(self, "_handle", None)

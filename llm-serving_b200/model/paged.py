@@ -229,14 +229,14 @@ class _PendingAppend:
     """One decode-step append recorded by :meth:`PagedKV.write`: consumed by the fused launch
     of the same layer's ``attend``, or launched alone by :meth:`PagedPool.flush`."""
 
-    __slots__ = ("owner", "layer", "k", "v", "stream")
+    __slots__ = ("owner", "layer", "k", "v", "rope", "stream")
 
-    def __init__(self, owner: "PagedKV", layer: int, k: torch.Tensor, v: torch.Tensor, stream) -> None:
-        self.owner, self.layer, self.k, self.v, self.stream = owner, layer, k, v, stream
+    def __init__(self, owner: "PagedKV", layer: int, k: torch.Tensor, v: torch.Tensor, rope, stream) -> None:
+        self.owner, self.layer, self.k, self.v, self.rope, self.stream = owner, layer, k, v, rope, stream
 
     def launch(self) -> None:
         with torch.cuda.stream(self.stream):
-            self.owner._append_now(self.layer, self.k, self.v)
+            self.owner._append_now(self.layer, self.k, self.v, self.rope)
 
 
 def _fusable_rows(t: torch.Tensor, dtype: torch.dtype) -> bool:
@@ -379,8 +379,34 @@ class PagedKV:
             self._slot_cache = blocks * bs + self.pos % bs
         return self._slot_cache
 
-    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
-        """Append this step's token of every row at its own position (one fused launch)."""
+    def _rope_tables(self, rope):
+        """``rope`` = (cos, sin): per-row tables of the step's positions, (B, 1, R/2) as the model
+        hands them to the layer or (B, R/2); returns (cos, sin, R) as (B, R/2) views."""
+        cos, sin = rope
+        if cos.dim() == 3 and cos.shape[1] == 1:
+            cos, sin = cos[:, 0], sin[:, 0]
+        half = cos.shape[-1]
+        if cos.dim() != 2 or tuple(cos.shape) != (self.batch, half) or tuple(sin.shape) != tuple(cos.shape):
+            raise ValueError(f"rope needs cos/sin of shape (B, 1, rotary_dim/2) or (B, rotary_dim/2) with "
+                             f"B={self.batch}, got {tuple(rope[0].shape)} / {tuple(rope[1].shape)}")
+        if not 1 <= half <= self.head_dim // 2:
+            raise ValueError(f"rotary_dim {2 * half} must be in [2, head_dim={self.head_dim}]")
+        for name, t in (("cos", cos), ("sin", sin)):
+            if t.dtype != self.dtype or not _same_device(t.device, self.device):
+                raise ValueError(f"rope {name} must be {self.dtype} on {self.device}, got {t.dtype} on {t.device}")
+        cos, sin = _unit_last_stride(cos), _unit_last_stride(sin)
+        if sin.stride(0) != cos.stride(0):
+            sin = sin.contiguous()
+            cos = cos.contiguous()
+        return cos, sin, 2 * half
+
+    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor, *, rope=None) -> None:
+        """Append this step's token of every row at its own position (one fused launch).
+
+        ``rope`` = (cos, sin) passes K *before* its rotary embedding: the rows are rotated on
+        the way into the pool (GPT-NeoX pairs over the first ``2 * cos.shape[-1]`` dims),
+        bit-identical to the model rotating with torch and then writing
+        (model/layers.py:210-211 followed by this call)."""
         expected = (self.batch, self.n_kv_head, 1, self.head_dim)
         if tuple(k.shape) != expected or tuple(v.shape) != expected:
             raise ValueError(f"write needs {expected}, got {tuple(k.shape)} / {tuple(v.shape)}")
@@ -397,19 +423,22 @@ class PagedKV:
                 raise ValueError(f"{name} dtype must be fp32, fp16 or bf16, got {t.dtype}")
             if not _same_device(t.device, self.device):
                 raise ValueError(f"{name} on {t.device} but the pool is on {self.device}")
+        tables = None if rope is None else self._rope_tables(rope)
+        if tables is not None and k.dtype != self.dtype:
+            raise ValueError(f"a rotated write needs K in the pool dtype {self.dtype}, got {k.dtype}")
         k3, v3 = k[:, :, 0, :], v[:, :, 0, :]
         if self.fuse_append and _fusable_rows(k3, self.dtype) and _fusable_rows(v3, self.dtype):
-            self.pool._record(_PendingAppend(self, layer, k3, v3, torch.cuda.current_stream(self.device)))
+            self.pool._record(_PendingAppend(self, layer, k3, v3, tables, torch.cuda.current_stream(self.device)))
         else:
             self.pool.flush()
-            self._append_now(layer, k3, v3)
+            self._append_now(layer, k3, v3, tables)
         self._step_written = True
 
-    def _append_now(self, layer: int, k3: torch.Tensor, v3: torch.Tensor) -> None:
+    def _append_now(self, layer: int, k3: torch.Tensor, v3: torch.Tensor, rope=None) -> None:
         """The append alone: one ``pd_kv_append_table`` launch on the current stream."""
         with torch.cuda.device(self.pool._keys[layer].device):
             _native.append_table(self.pool._keys[layer], self.pool._values[layer], self._block_table_tensor,
-                                 self.pos, _unit_last_stride(k3), _unit_last_stride(v3.to(k3.dtype)))
+                                 self.pos, _unit_last_stride(k3), _unit_last_stride(v3.to(k3.dtype)), rope)
 
     def flush(self) -> None:
         """Perform a recorded append now (see :meth:`PagedPool.flush`)."""
@@ -444,9 +473,10 @@ class PagedKV:
         pending = self.pool._pending
         if (pending is not None and pending.owner is self and pending.layer == int(layer)
                 and pending.stream == torch.cuda.current_stream(self.device)
-                and plan.can_fuse_append(pending.k, pending.v, self.pos)):
+                and plan.can_fuse_append(pending.k, pending.v, self.pos, pending.rope)):
             self.pool._pending = None
-            return plan.run_append(layer, q3, pending.k, pending.v, self.pos, out=out3).unsqueeze(2)
+            return plan.run_append(layer, q3, pending.k, pending.v, self.pos, out=out3,
+                                   rope=pending.rope).unsqueeze(2)
         self.pool.flush()
         return plan.run(layer, q3, out=out3).unsqueeze(2)
 

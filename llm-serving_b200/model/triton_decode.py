@@ -334,10 +334,20 @@ class PagedDecodePlan:
         self._native_plan.run(layer, q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
         return out
 
-    def can_fuse_append(self, k_new, v_new, pos) -> bool:
+    def can_fuse_append(self, k_new, v_new, pos, rope=None) -> bool:
         """Whether :meth:`run_append` takes these tensors: ``(B, H_kv, D)`` rows in the plan's
-        dtype on its device with a unit last stride and 16-byte aligned rows, and an int64
-        ``(B,)`` contiguous ``pos``."""
+        dtype on its device with a unit last stride and 16-byte aligned rows, an int64
+        ``(B,)`` contiguous ``pos``, and (with ``rope``) ``(B, rotary_dim / 2)`` cos/sin tables
+        in the plan's dtype with a unit last stride."""
+        if rope is not None:
+            cos, sin, rotary_dim = rope
+            half = int(rotary_dim) // 2
+            for t in (cos, sin):
+                if (t.dim() != 2 or tuple(t.shape) != (self.q_shape[0], half) or t.dtype != self.q_dtype
+                        or t.device != self.q_device or t.stride(1) != 1 or t.stride(0) != cos.stride(0)):
+                    return False
+            if not (2 <= int(rotary_dim) <= self.q_shape[2] and int(rotary_dim) % 2 == 0):
+                return False
         b, _, d = self.q_shape
         shape = (b, self._k[0].shape[2], d)
         es = self._k[0].element_size()
@@ -349,23 +359,25 @@ class PagedDecodePlan:
         return (pos.dtype == torch.int64 and tuple(pos.shape) == (b,) and pos.device == self.q_device
                 and pos.stride(0) == 1)
 
-    def run_append(self, layer: int, q, k_new, v_new, pos, *, out=None):
+    def run_append(self, layer: int, q, k_new, v_new, pos, *, out=None, rope=None):
         """Store row ``b``'s new K/V ``(B, H_kv, D)`` at logical position ``pos[b]`` of layer
         ``layer``'s pools and decode that layer, in one launch.
 
         Same result as ``PagedKV.write`` followed by :meth:`run` -- the pools and the output
         are bit-identical -- provided no row reads a slot another row appends (rows do not
-        share blocks they write). Tensors must pass :meth:`can_fuse_append`.
+        share blocks they write). ``rope`` = (cos, sin, rotary_dim) gives ``k_new`` before its
+        rotary embedding, which the launch applies exactly as the model's torch ops would.
+        Tensors must pass :meth:`can_fuse_append`.
         """
         layer = self._check_query(layer, q)
-        if not self.can_fuse_append(k_new, v_new, pos):
+        if not self.can_fuse_append(k_new, v_new, pos, rope):
             raise ValueError(
                 "paged_decode_plan.run_append needs (B, H_kv, D) k/v rows in the plan's dtype with "
                 "16-byte aligned rows and an int64 (B,) pos on the plan's device"
             )
         out = self._output(out)
         self._native_plan.run_append(layer, q, out, k_new, v_new, pos,
-                                     torch.cuda.current_stream(self.q_device).cuda_stream)
+                                     torch.cuda.current_stream(self.q_device).cuda_stream, rope)
         return out
 
 

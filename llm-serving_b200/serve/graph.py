@@ -35,10 +35,12 @@ class PagedStepGraph:
     ``q`` ``(n_layer, B, H, 1, D)`` and ``k``/``v`` ``(n_layer, B, H_kv, 1, D)`` are device
     buffers the caller refills before each :meth:`replay` (their addresses are baked into the
     graph). :attr:`out` ``(n_layer, B, H, 1, D)`` receives every layer's attention output.
+    ``rope`` = (cos, sin) device buffers of the step's per-row rotary tables, (B, 1, R/2):
+    then ``k`` holds K before its rotary embedding, which the fused append applies.
     """
 
     def __init__(self, kv: PagedKV, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
-                 next_token: bool = True) -> None:
+                 next_token: bool = True, rope=None) -> None:
         if not isinstance(kv, PagedKV):
             raise TypeError(f"PagedStepGraph needs a PagedKV, got {type(kv).__name__}")
         n = kv.n_layer
@@ -54,6 +56,7 @@ class PagedStepGraph:
                 raise ValueError(f"{name} must be a {kv.dtype} CUDA tensor, got {t.dtype} on {t.device}")
         self.kv = kv
         self.q, self.k, self.v = q, k, v
+        self.rope = rope
         self.next_token = bool(next_token)
         self.out = torch.empty(q_shape, dtype=kv.dtype, device=q.device)
 
@@ -67,7 +70,7 @@ class PagedStepGraph:
             with torch.cuda.graph(self.graph):
                 kv.build_mask(next_token=self.next_token)
                 for layer in range(n):
-                    kv.write(layer, k[layer], v[layer])
+                    kv.write(layer, k[layer], v[layer], rope=rope)
                     kv.attend(layer, q[layer], out=self.out[layer])
                 kv.advance()
         finally:

@@ -14,6 +14,8 @@ the same allocator the engine uses, so fragmentation is what the serving stack p
 * ``config4``: B=32, every row at 8192 tokens (long-context split-KV). ``shard(rank,
   world)`` keeps rank's contiguous 8192/world token range of every row.
 * ``config5``: 1024 rows, L ~ U[256, 4096], sharded by row index over the ranks.
+* ``qwen35``: the hybrid Qwen3.5-0.8B engine's full-attention layers (H=8, H_kv=2, D=256,
+  four q heads per kv head; 6 layers), B=32 rows at context 2048, block size 16.
 
 K/V/q are N(0, 1) in bf16 (scale 1/sqrt(D)). Large pools are drawn with a CUDA generator.
 """
@@ -195,3 +197,16 @@ def config5(device="cuda", seed=0, dtype=torch.bfloat16, n_layer=1, rank=0, worl
                   seed=seed + 5 + 1000 * rank,
                   meta={"rows": rows, "row_begin": lo, "row_end": hi, "rank": rank, "world": world,
                         "block_size": bs})
+
+
+QWEN35_H, QWEN35_HKV, QWEN35_D = 8, 2, 256
+
+
+def qwen35(device="cuda", seed=0, dtype=torch.bfloat16, n_layer=6, context=2048, batch=32) -> PagedWorkload:
+    """Full-attention decode of the hybrid Qwen3.5 engine at config-2 batch and context."""
+    bs = 16
+    manager = BlockManager(batch * -(-(context + 64) // bs), bs)
+    tables = [manager.reserve(manager.blocks_for(context, 64)) for _ in range(batch)]
+    return _build("qwen35", [context] * batch, tables, manager.n_blocks, n_layer=n_layer, H=QWEN35_H,
+                  H_kv=QWEN35_HKV, D=QWEN35_D, device=device, dtype=dtype, seed=seed + 35,
+                  meta={"B": batch, "context": context, "block_size": bs, "n_blocks": manager.n_blocks})

@@ -41,7 +41,8 @@ def build(force: bool = False) -> Path:
     """Compile ``pd_oracle.c`` with gcc (OpenMP) if the .so is missing or stale."""
     LIB.parent.mkdir(exist_ok=True)
     if force or not LIB.exists() or LIB.stat().st_mtime < SOURCE.stat().st_mtime:
-        cmd = ["gcc", "-O3", "-fopenmp", "-fPIC", "-shared", "-std=c11", str(SOURCE), "-o", str(LIB), "-lm"]
+        cmd = ["gcc", "-O3", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-std=c11", str(SOURCE),
+               "-o", str(LIB), "-lm"]
         subprocess.run(cmd, check=True)
     return LIB
 
@@ -70,6 +71,8 @@ def lib() -> ctypes.CDLL:
         _lib.oracle_seat_decode.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
         _lib.oracle_seat_decode.restype = None
         _lib.oracle_convert.argtypes = [P, I, P, I, I64]
+        _lib.oracle_rope.restype = None
+        _lib.oracle_rope.argtypes = [P, P, P, P, I64, I, I, I64, I64, I]
         _lib.oracle_convert.restype = None
         _lib.oracle_max_threads.argtypes = []
         _lib.oracle_max_threads.restype = I
@@ -202,6 +205,21 @@ def seat_decode(q, slab_k, slab_v, lengths, *, threads: int = 0):
     out = torch.empty(B, H, D, dtype=q.dtype)
     lib().oracle_seat_decode(q.data_ptr(), slab_k.data_ptr(), slab_v.data_ptr(), lengths.data_ptr(), B, H, hkv,
                              D, lpad, _DT[q.dtype], out.data_ptr(), threads)
+    return out
+
+
+def rope(x, cos, sin, rotary_dim: int) -> torch.Tensor:
+    """GPT-NeoX rotary embedding (model/layers.py:59-117 ``apply_rotary_emb_partial``) of
+    ``x`` (..., n_head, head_dim) with one cos/sin row per leading index: cos/sin shaped
+    (..., rotary_dim / 2) matching ``x``'s leading dims without the head axis."""
+    x = _cpu(x).contiguous()
+    cos = _cpu(cos).contiguous().to(x.dtype)
+    sin = _cpu(sin).contiguous().to(x.dtype)
+    head_dim, n_head = x.shape[-1], x.shape[-2]
+    n_rows = x.numel() // head_dim
+    out = torch.empty_like(x)
+    lib().oracle_rope(x.data_ptr(), cos.data_ptr(), sin.data_ptr(), out.data_ptr(), n_rows, head_dim,
+                      int(rotary_dim), rotary_dim // 2, n_head, _DT[x.dtype])
     return out
 
 

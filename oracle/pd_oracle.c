@@ -462,6 +462,38 @@ void oracle_seat_decode(const void* q, const void* slab_k, const void* slab_v, c
 }
 
 /* Round-trip helpers the tests use to pin the conversions against torch. */
+/* GPT-NeoX rotary embedding of rows of length head_dim (model/layers.py:59-117,
+ * apply_rotary_emb / apply_rotary_emb_partial): pairs (i, i + rot_dim / 2) over the first
+ * rot_dim elements, the tail copied. Row r uses cos/sin + r * cs_stride. As torch's
+ * elementwise ops in the row dtype: each product rounded to the dtype, then the difference
+ * (first half) or sum (second half) rounded again. Build with -ffp-contract=off. */
+void oracle_rope(const void* x, const void* cos_t, const void* sin_t, void* out, int64_t n_rows,
+                 int head_dim, int rot_dim, int64_t cs_stride, int64_t rows_per_table_row, int dtype) {
+  const int half = rot_dim / 2;
+  for (int64_t r = 0; r < n_rows; ++r) {
+    const int64_t t = (r / rows_per_table_row) * cs_stride;
+    const int64_t base = r * head_dim;
+    for (int e = 0; e < head_dim; ++e) {
+      float y;
+      if (e >= rot_dim) {
+        y = load_elem(x, base + e, dtype);
+      } else {
+        const int i = e < half ? e : e - half;
+        const float x1 = load_elem(x, base + i, dtype), x2 = load_elem(x, base + i + half, dtype);
+        const float c = load_elem(cos_t, t + i, dtype), s = load_elem(sin_t, t + i, dtype);
+        if (e < half) {
+          const float a = round_to(x1 * c, dtype), b = round_to(x2 * s, dtype);
+          y = a - b;
+        } else {
+          const float a = round_to(x1 * s, dtype), b = round_to(x2 * c, dtype);
+          y = a + b;
+        }
+      }
+      store_elem(out, base + e, dtype, y);
+    }
+  }
+}
+
 void oracle_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n) {
   for (int64_t i = 0; i < n; ++i) store_elem(dst, i, dst_dtype, load_elem(src, i, src_dtype));
 }

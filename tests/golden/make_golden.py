@@ -65,6 +65,7 @@ SEEDS = {"cpu": 3, "cuda": 13}
 def load_reference(root: Path):
     sys.path.insert(0, str(root))
     from model.attention.hand_baddbmm import HandBaddbmmBackend
+    from model.layers import apply_rotary_emb_partial, rope_cos_sin
     from model.paged import PagedPool
     from model.slab import KvSlab
     from serve.block_manager import BlockManager
@@ -78,6 +79,8 @@ def load_reference(root: Path):
         "BlockManager": BlockManager,
         "paged": ref_paged,
         "tests": ref_tests,
+        "apply_rotary_emb_partial": apply_rotary_emb_partial,
+        "rope_cos_sin": rope_cos_sin,
     }
 
 
@@ -199,6 +202,39 @@ def block_manager_goldens(ref, workloads):
     return {"trace": trace, "blocks_for": blocks_for, "config3": cfg3}
 
 
+# Rotary cases: (key, n_kv_head, head_dim, rotary_dim, theta, dtype, positions). The K rows a
+# decode step appends are rotated by the model just before the write; the fused append +
+# decode must store exactly what this produces.
+ROPE_CASES = [
+    ("rope/qwen3-bf16", 8, 128, 128, 1e6, torch.bfloat16, [0, 1, 17, 2047, 5000, 40000]),
+    ("rope/qwen3-f16", 8, 128, 128, 1e6, torch.float16, [3, 900, 31000]),
+    ("rope/qwen3-f32", 8, 128, 128, 1e6, torch.float32, [2, 2048]),
+    ("rope/qwen35-partial-bf16", 2, 256, 64, 1e7, torch.bfloat16, [0, 513, 4095, 100000]),
+]
+
+
+def rope_goldens(ref):
+    """Per-row decode rotation: cos/sin of each row's position from the reference's
+    rope_cos_sin (rows stacked as (B, 1, rotary_dim / 2)), K (B, 1, H_kv, D) rotated by the
+    reference's apply_rotary_emb_partial."""
+    gen = torch.Generator().manual_seed(41)
+    records, tensors = [], {}
+    for key, hkv, d, rot, theta, dtype, positions in ROPE_CASES:
+        rows = [ref["rope_cos_sin"](d, theta, p, 1, dtype=dtype, rotary_dim=None if rot == d else rot)
+                for p in positions]
+        cos = torch.stack([c for c, _ in rows])  # (B, 1, rot / 2)
+        sin = torch.stack([s for _, s in rows])
+        k = torch.randn(len(positions), 1, hkv, d, generator=gen).to(dtype)
+        out = ref["apply_rotary_emb_partial"](k, cos, sin, rot)
+        tensors[key + "/k"] = k
+        tensors[key + "/cos"] = cos
+        tensors[key + "/sin"] = sin
+        tensors[key + "/out"] = out
+        records.append({"key": key, "n_kv_head": hkv, "head_dim": d, "rotary_dim": rot, "theta": theta,
+                        "dtype": str(dtype), "positions": positions})
+    return records, tensors
+
+
 def seat_goldens(ref, workloads):
     """Config 1 through the reference's seat path and oracle (bf16 on CPU)."""
     wl = workloads.config1(device="cpu", seed=0)
@@ -237,9 +273,10 @@ def main(argv=None) -> int:
     app_records, app_tensors = append_goldens(ref)
     bm = block_manager_goldens(ref, workloads)
     seat_record, seat_tensors = seat_goldens(ref, workloads)
-    tensors = {**dec_tensors, **app_tensors, **seat_tensors}
+    rope_records, rope_tensors = rope_goldens(ref)
+    tensors = {**dec_tensors, **app_tensors, **seat_tensors, **rope_tensors}
     torch.save(tensors, HERE / "golden_tensors.pt")
-    meta = {"decode": dec_records, "append": app_records, "seat": seat_record,
+    meta = {"decode": dec_records, "append": app_records, "seat": seat_record, "rope": rope_records,
             "torch": torch.__version__, "generator": "tests/golden/make_golden.py"}
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1))
     (HERE / "block_manager.json").write_text(json.dumps(bm))

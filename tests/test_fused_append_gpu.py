@@ -8,6 +8,9 @@ rows do not share blocks. ``PagedKV`` uses it by default; every other observer o
 
 from __future__ import annotations
 
+import json
+from pathlib import Path
+
 import pytest
 import torch
 
@@ -172,3 +175,54 @@ def test_shared_blocks_disable_fusion(cuda_device):
     pool = PagedPool(1, 8, 16, 2, 8, dtype=torch.bfloat16, device=cuda_device, n_head=4)
     kv = PagedKV(pool, [[3, 1], [3, 2]], [17, 17], rope_len=64, n_head=4)
     assert not kv.fuse_append
+
+
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+ROPE_CASES = json.loads((GOLDEN / "golden_meta.json").read_text())["rope"]
+
+
+@pytest.mark.parametrize("rec", ROPE_CASES, ids=[r["key"] for r in ROPE_CASES])
+@pytest.mark.parametrize("fuse", [True, False], ids=["fused", "two-launch"])
+def test_rotated_append_stores_the_reference_rotation(cuda_device, rec, fuse):
+    """K rows given before RoPE are stored exactly as the reference's apply_rotary_emb_partial
+    rotates them (golden vectors from the reference itself), and the decode over them matches
+    the oracle."""
+    from model.paged import PagedKV, PagedPool
+
+    tensors = torch.load(GOLDEN / "golden_tensors.pt")
+    key = rec["key"]
+    k_pre, cos, sin, k_ref = (tensors[key + part] for part in ("/k", "/cos", "/sin", "/out"))
+    B, _, Hkv, D = k_pre.shape
+    dtype = k_pre.dtype
+    H, bs = 2 * Hkv, 16
+    lengths = [5 + 37 * i for i in range(B)]
+    pages = [-(-(n + 2) // bs) for n in lengths]
+    pool = PagedPool(1, sum(pages) + 2, bs, Hkv, D, dtype=dtype, device=cuda_device, n_head=H)
+    gen = torch.Generator(device=cuda_device).manual_seed(4)
+    for t in pool.keys + pool.values:
+        t.copy_(torch.randn(t.shape, generator=gen, device=cuda_device).to(dtype))
+    tables, at = [], 0
+    for n in pages:
+        tables.append(list(range(at, at + n)))
+        at += n
+    kv = PagedKV(pool, tables, lengths, rope_len=max(lengths) + 4, n_head=H, fuse_append=fuse)
+    kv.build_mask(next_token=True)
+    k_in = k_pre.permute(0, 2, 1, 3).to(cuda_device)  # (B, H_kv, 1, D), as the layer passes it
+    v_in = torch.randn(B, Hkv, 1, D, generator=gen, device=cuda_device).to(dtype)
+    q = torch.randn(B, H, 1, D, generator=gen, device=cuda_device).to(dtype)
+    kv.write(0, k_in, v_in, rope=(cos.to(cuda_device), sin.to(cuda_device)))
+    out = kv.attend(0, q)
+    torch.cuda.synchronize()
+
+    keys = pool.keys[0].cpu()
+    bits = (lambda t: t) if dtype == torch.float32 else (lambda t: t.contiguous().view(torch.uint8))
+    for row, n in enumerate(lengths):
+        stored = keys[tables[row][n // bs], n % bs]
+        assert torch.equal(bits(stored), bits(k_ref[row, 0])), f"row {row}"
+    table = torch.zeros(B, max(pages), dtype=torch.int32)
+    for row, t in enumerate(tables):
+        table[row, : len(t)] = torch.tensor(t, dtype=torch.int32)
+    seqlen = torch.tensor([n + 1 for n in lengths], dtype=torch.int32)
+    ref, _ = oracle.paged_decode(q[:, :, 0].cpu(), keys, pool.values[0].cpu(), table, seqlen)
+    assert_output_close(out[:, :, 0], ref, dtype)

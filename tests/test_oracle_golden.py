@@ -142,3 +142,15 @@ def test_seat_restatement_tracks_the_reference_seat_path():
     out_f32, out = oracle.paged_decode(q, k, v, wl.block_table, wl.seqlen)
     torch.testing.assert_close(out_f32, TENSORS["seat/config1/out_f32"], rtol=0, atol=1e-5)
     assert _within_one_ulp(out, TENSORS["seat/config1/out"], torch.bfloat16)
+
+
+@pytest.mark.parametrize("rec", META["rope"], ids=[r["key"] for r in META["rope"]])
+def test_oracle_rope_reproduces_the_reference_rotation_bit_for_bit(rec):
+    """The rotation a decode step applies to K before the write (apply_rotary_emb_partial on
+    per-row cos/sin from rope_cos_sin), restated in C with explicit roundings."""
+    key = rec["key"]
+    k, cos, sin = TENSORS[key + "/k"], TENSORS[key + "/cos"], TENSORS[key + "/sin"]
+    got = oracle.rope(k[:, 0], cos[:, 0], sin[:, 0], rec["rotary_dim"])
+    assert torch.equal(got.view(torch.uint8) if got.dtype != torch.float32 else got,
+                       TENSORS[key + "/out"][:, 0].contiguous().view(torch.uint8)
+                       if got.dtype != torch.float32 else TENSORS[key + "/out"][:, 0])

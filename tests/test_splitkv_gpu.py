@@ -100,6 +100,14 @@ def test_benchmark_configs_match_the_oracle(cuda_device, name):
     _check_workload(wl)
 
 
+def test_qwen35_full_attention_shape_matches_the_oracle(cuda_device):
+    """Hybrid Qwen3.5 full-attention layers: H=8, H_kv=2, D=256 (4 q heads per kv head)."""
+    from serve import workloads
+
+    wl = workloads.qwen35(cuda_device, n_layer=1, batch=8)
+    _check_workload(wl)
+
+
 def test_config5_subset_and_checksum(cuda_device):
     from serve import workloads
 
