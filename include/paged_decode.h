@@ -268,14 +268,17 @@ int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_
                          int32_t* min_tiles_per_warp);
 
 /* Decode kernel choice for calls and plans made afterwards. mode 0 (default): every warp
- * runs its own TMA pipeline. mode 1: where a row has exactly 8 items (n_kv_head x q-head
+ * runs its own TMA pipeline; with bf16/fp16 pools, head_dim 64..256 and block_size >= 8 its
+ * tile math runs on the tensor cores (mma.sync fed by ldmatrix from 128-byte-swizzled
+ * stages), elsewhere on the CUDA cores. mode 2: per-warp pipelines with CUDA-core tile math
+ * everywhere. mode 1: where a row has exactly 8 items (n_kv_head x q-head
  * chunks, e.g. 8 kv heads with 1-4 q heads each), bf16/fp16 and head_dim >= 64, the CTA
  * shares its pipeline stages -- a producer warp loads whole blocks of all kv heads and 8
- * consumer warps decode one item each; elsewhere the per-warp kernel runs. shared_stages:
+ * consumer warps decode one item each; elsewhere mode 0 applies. shared_stages:
  * stage count of the shared-stage kernel (0 = as many as shared memory holds, at most 8).
  * row_cost (0..64, -1 = keep; default 3): when a row has one item per warp, the work is cut
  * into one range of (row, tile) columns per CTA, each row start counted as row_cost extra
- * columns, so that ranges crossing into a new row carry fewer tiles. Both kernels and every
+ * columns, so that ranges crossing into a new row carry fewer tiles. Every kernel and every
  * row_cost compute the same function; results agree within rounding. Not thread-safe
  * against concurrent launches that size their workspace. No reference counterpart. */
 int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost);

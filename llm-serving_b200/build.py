@@ -32,6 +32,8 @@ SOURCES = [
     "pd_decode_bf16.cu",
     "pd_decode_f16.cu",
     "pd_decode_f32.cu",
+    "pd_decode_mma_bf16.cu",
+    "pd_decode_mma_f16.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

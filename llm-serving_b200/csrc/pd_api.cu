@@ -117,6 +117,7 @@ struct Geometry {
   int tile;        // tokens per stage
   int box_tokens;  // tokens per TMA box
   bool cta;        // shared-stage kernel: one consumer warp per item of a row
+  bool mma;        // per-warp kernel with tensor-core tile math (swizzled 5-D pool maps)
   int box_heads;   // kv heads per TMA box: all of them in the shared-stage kernel, else 1
   int stage_bytes; // K + V bytes of one stage (of one warp, or of the CTA when shared)
 };
@@ -143,6 +144,8 @@ int geometry(int n_head, int n_kv_head, int head_dim, int block_size, int dtype,
   }
   g->cta = mode == 1 && n_kv_head * g->n_gchunks == kCtaConsumerWarps && gt <= 4 &&
            (dtype == PD_BF16 || dtype == PD_F16) && head_dim >= 64;
+  g->mma = !g->cta && mode != 2 && (dtype == PD_BF16 || dtype == PD_F16) && head_dim >= 64 &&
+           g->box_tokens >= 8;
   g->box_heads = g->cta ? n_kv_head : 1;
   g->stage_bytes = 2 * 4096 * g->box_heads;
   return PD_OK;
@@ -151,6 +154,8 @@ int geometry(int n_head, int n_kv_head, int head_dim, int block_size, int dtype,
 DecodeLaunchFn launcher_for(int dtype, const Geometry& g) {
   if (g.cta) return dtype == PD_BF16 ? decode_launcher_cta_bf16(g.d_index, g.gt_index)
                                      : decode_launcher_cta_f16(g.d_index, g.gt_index);
+  if (g.mma) return dtype == PD_BF16 ? decode_launcher_mma_bf16(g.d_index, g.gt_index)
+                                     : decode_launcher_mma_f16(g.d_index, g.gt_index);
   switch (dtype) {
     case PD_F32: return decode_launcher_f32(g.d_index, g.gt_index);
     case PD_F16: return decode_launcher_f16(g.d_index, g.gt_index);
@@ -231,8 +236,14 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
   return w;
 }
 
+// Pool map of the decode kernels. Plain: 4-D (head_dim, head, token-in-block, block), box
+// (head_dim, box_heads, box_tokens, 1). Swizzled (tensor-core kernel, 16-bit head_dim >= 64):
+// 5-D (64 elements, token-in-block, head, 128-byte piece, block) with the 128-byte swizzle and
+// box (64, box_tokens, 1, head_dim / 64, 1), so a box lands piece-major: shared row
+// piece * box_tokens + token, 16-byte units XOR-permuted by the row index.
 int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_size, int n_kv_head,
-                int head_dim, const int64_t* strides, int dtype, int box_tokens, int box_heads) {
+                int head_dim, const int64_t* strides, int dtype, int box_tokens, int box_heads,
+                bool swizzle) {
   if (load_encoder() != PD_OK) return PD_ERR_CUDA;
   const int es = elem_size(dtype);
   if (!aligned16(base)) return PD_ERR_INVALID;
@@ -243,6 +254,20 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
   CUtensorMapDataType t = dtype == PD_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                           : dtype == PD_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (swizzle) {
+    if (es != 2 || head_dim % 64 != 0 || box_heads != 1) return PD_ERR_INVALID;
+    const cuuint64_t dims[5] = {64u, cuuint64_t(block_size), cuuint64_t(n_kv_head), cuuint64_t(head_dim / 64),
+                                cuuint64_t(n_blocks)};
+    // Byte strides of dims 1..4: token-in-block, head, 128-byte piece, block.
+    const cuuint64_t gstr[4] = {cuuint64_t(strides[1] * es), cuuint64_t(strides[2] * es), 128u,
+                                cuuint64_t(strides[0] * es)};
+    const cuuint32_t box[5] = {64u, cuuint32_t(box_tokens), 1u, cuuint32_t(head_dim / 64), 1u};
+    const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+    CUresult r = g_encode(map, t, 5, const_cast<void*>(base), dims, gstr, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? PD_OK : PD_ERR_INVALID;
+  }
   const cuuint64_t dims[4] = {cuuint64_t(head_dim), cuuint64_t(n_kv_head), cuuint64_t(block_size),
                               cuuint64_t(n_blocks)};
   // Byte strides of dims 1..3: head, token-in-block, block.
@@ -441,10 +466,10 @@ int decode_common(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache
     return PD_ERR_INVALID;
   CUtensorMap kmap, vmap;
   st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype,
-                   P.g.box_tokens, P.g.box_heads);
+                   P.g.box_tokens, P.g.box_heads, P.g.mma);
   if (st != PD_OK) return st;
   st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype,
-                   P.g.box_tokens, P.g.box_heads);
+                   P.g.box_tokens, P.g.box_heads, P.g.mma);
   if (st != PD_OK) return st;
   return run_prepared(P, kmap, vmap, q, q_sb, q_sh, out, o_sb, o_sh, pm, pl, pacc, mode, dtype,
                       static_cast<cudaStream_t>(stream));
@@ -576,10 +601,10 @@ int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
     h->k_pools[layer] = const_cast<void*>(k_caches[layer]);
     h->v_pools[layer] = const_cast<void*>(v_caches[layer]);
     st = encode_pool(&h->kmaps[layer], k_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
-                     k_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads);
+                     k_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads, h->P.g.mma);
     if (st == PD_OK)
       st = encode_pool(&h->vmaps[layer], v_caches[layer], n_blocks, block_size, n_kv_head, head_dim,
-                       v_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads);
+                       v_strides, dtype, h->P.g.box_tokens, h->P.g.box_heads, h->P.g.mma);
     if (st != PD_OK) {
       delete h;
       return st;
@@ -824,7 +849,7 @@ int pd_set_decode_tuning(int32_t warps_per_cta, int32_t stages, int32_t ctas_per
 }
 
 int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost) {
-  if (mode < 0 || mode > 1 || shared_stages < 0 || shared_stages > 8 || row_cost < -1 || row_cost > 64)
+  if (mode < 0 || mode > 2 || shared_stages < 0 || shared_stages > 8 || row_cost < -1 || row_cost > 64)
     return PD_ERR_INVALID;
   std::lock_guard<std::mutex> lock(g_mutex);
   g_decode_mode = mode;

@@ -95,6 +95,85 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 5-D tiled TMA load (the 128-byte-swizzled pool map of the tensor-core decode path).
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+// ---- warp-level tensor-core fragments (mma.sync / ldmatrix / movmatrix) ----------------
+// Fragment layouts (g = lane / 4, c = lane % 4), 16-bit elements packed in pairs, the lower
+// column in the low half:
+//   A 16x16 (row-major): a0 (row g, k 2c..2c+1), a1 (row g+8, ..), a2 (row g, k 2c+8..),
+//                        a3 (row g+8, k 2c+8..); A 16x8: a0, a1.
+//   B 16x8 (k x n):      b0 (k 2c..2c+1, n g), b1 (k 2c+8.., n g); B 8x8: b0.
+//   C/D 16x8 fp32:       c0, c1 (row g, cols 2c, 2c+1), c2, c3 (row g+8, same cols).
+// ldmatrix: lane l gives the shared address of row l % 8 of matrix l / 8; register i holds
+// matrix i in the A/B layout above (transposed with .trans). The smem reads are volatile so
+// that they stay after the barrier waits that publish the bytes.
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Transpose of an 8x8 16-bit matrix held one pair per lane (row g, cols 2c..2c+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+template <typename T>
+struct Mma;
+
+template <>
+struct Mma<__nv_bfloat16> {
+  // d += A (16x16) * B (16x8), fp32 accumulation.
+  __device__ __forceinline__ static void m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                  uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  // d += A (16x8) * B (8x8).
+  __device__ __forceinline__ static void m16n8k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+  }
+};
+
+template <>
+struct Mma<__half> {
+  __device__ __forceinline__ static void m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                  uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static void m16n8k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+  }
+};
+
 // Atomic add at GPU scope with release semantics: this thread's earlier writes (and those of
 // threads synchronised with it, e.g. by __syncwarp) are visible before the add is.
 __device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long* p,

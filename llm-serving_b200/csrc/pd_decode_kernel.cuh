@@ -17,12 +17,17 @@
 //    block) that complete on the stage's mbarrier. Lane 0 issues; the warp consumes tile
 //    k while tiles k+1 .. k+stages-1 are in flight, then refills the stage it just read.
 //    There is no block-level synchronisation after the prologue.
-//  * q.K: lanes span head_dim (16 B per lane per row), a warp-wide load covers 32/LPR
-//    rows. Partial dot products for all (token, q head) pairs of the tile are finished by
-//    a butterfly reduce-scatter, so each shuffle carries useful sums. Online softmax in
-//    fp32 per q head, then every lane fetches the probabilities of its own rows by
-//    shuffle and accumulates P.V in fp32 registers. No tensor cores: with a group of 2
-//    heads this is a GEMV at 2 flop/byte and the HBM stream is the roof.
+//  * Tile math, tensor-core consumer (16-bit K/V, head_dim 64..256, the default there):
+//    S^T = K q^T and O^T += V^T P^T as warp-level mma.sync tiles fed by ldmatrix from
+//    128-byte-swizzled stages (pd_decode_mma.cuh). The tensor cores are not there for
+//    flops -- a decode step is a GEMV at 2 flop/byte per q head -- but to cut the issue
+//    slots per tile, which otherwise bound wide heads with several q heads per kv head.
+//  * Tile math, CUDA-core consumer (every dtype and head size): lanes span head_dim (16 B
+//    per lane per row), a warp-wide load covers 32/LPR rows. Partial dot products for all
+//    (token, q head) pairs of the tile are finished by a butterfly reduce-scatter, so each
+//    shuffle carries useful sums. Online softmax in fp32 per q head, then every lane
+//    fetches the probabilities of its own rows by shuffle and accumulates P.V in fp32
+//    registers.
 //  * A worker whose range covers a whole item writes the output directly. A split item
 //    leaves (m, l, acc) in the workspace; the last of its workers to finish (arrival
 //    counter, __threadfence) merges the pieces with the log-sum-exp rule, so split-KV costs
@@ -38,6 +43,7 @@
 #pragma once
 
 #include "pd_common.cuh"
+#include "pd_decode_mma.cuh"
 
 namespace pd {
 
@@ -67,6 +73,20 @@ struct DecodeCfg {
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static_assert(TILE >= RPL, "tile smaller than one warp load");
   static_assert((1 << LOG_TILE) == TILE, "tile must be a power of two");
+};
+
+// Consumer of a worker's tiles: the CUDA-core path above (MMA = false, every dtype and head
+// size) or the tensor-core worker of pd_decode_mma.cuh (16-bit K/V, head_dim 64..256).
+struct NoMmaWorker {};
+template <bool MMA, typename T, int D, int GT>
+struct ConsumerSel {
+  using W = NoMmaWorker;
+  static constexpr int R = DecodeCfg<T, D, GT>::R;
+};
+template <typename T, int D, int GT>
+struct ConsumerSel<true, T, D, GT> {
+  using W = MmaWorker<T, D, GT>;
+  static constexpr int R = MmaCfg<T, D, GT>::R;
 };
 
 // Position of a worker inside the unit sequence.
@@ -179,7 +199,7 @@ __device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) 
 // kv heads (one TMA copy each per block part) into a shared stage, and the consumer warps --
 // warp j streams item j -- read their head's rows from it and release the stage on an
 // "empty" barrier. Contiguous block-sized copies keep the DRAM stream dense.
-template <typename T, int D, int GT, bool CTA>
+template <typename T, int D, int GT, bool CTA, bool MMA>
 __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtensorMap& kmap,
                                             const CUtensorMap& vmap, unsigned char* smem) {
   using C = DecodeCfg<T, D, GT>;
@@ -489,8 +509,13 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       const int off = tok & (bs - 1);
       const int blk = block_of(c.b, page, npages);
       if (lane == 0) {
-        tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, CTA ? 0 : h, off, blk);
-        tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, CTA ? 0 : h, off, blk);
+        if constexpr (MMA) {  // swizzled map: (64 elements, token, head, 128-byte piece, block)
+          tma_load_5d(kdst + j * box_bytes, &kmap, bar, 0, off, h, 0, blk);
+          tma_load_5d(vdst + j * box_bytes, &vmap, bar, 0, off, h, 0, blk);
+        } else {
+          tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, CTA ? 0 : h, off, blk);
+          tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, CTA ? 0 : h, off, blk);
+        }
       }
     }
   };
@@ -558,6 +583,13 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     hold_g[j] = idx % GT;
   }
 
+  // Tensor-core consumer (MMA): its own fragments and running state; RR scores per lane.
+  using Sel = ConsumerSel<MMA, T, D, GT>;
+  constexpr int RR = Sel::R;
+  typename Sel::W mw;
+  const uint32_t stages_addr = smem_addr(my_stages);
+  if constexpr (MMA) mw.init(lane, p.box_tokens, p.log2_box);
+
   // q and the P.V accumulators as pairs of consecutive head_dim elements: every multiply-add
   // below is a packed fp32 FMA (two lanes of fp32 per instruction, same rounding as fmaf).
   float2 qf[GT][C::PPL];
@@ -575,157 +607,176 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
 
   // Phase A of a tile: q.K for every (row, q head) of the stage, reduce-scattered so this
   // lane ends with its R held scores, scaled to log2 units and masked past valid_rows.
-  auto tile_scores = [&](int stage, int valid_rows, float (&sc)[C::R]) {
-    const unsigned char* ks = my_stages + size_t(stage) * stage_stride + head_off;
-    float sv[C::NV];
+  auto tile_scores = [&](int stage, int valid_rows, float (&sc)[RR]) {
+    if constexpr (MMA) {
+      mw.scores(stages_addr + uint32_t(stage) * uint32_t(stage_stride), valid_rows, p.scale_log2, sc);
+    } else {
+      const unsigned char* ks = my_stages + size_t(stage) * stage_stride + head_off;
+      float sv[C::NV];
 #pragma unroll
-    for (int i = 0; i < C::NT; ++i) {
-      const int row = i * C::RPL + rg;
-      float2 kf[C::PPL];
+      for (int i = 0; i < C::NT; ++i) {
+        const int row = i * C::RPL + rg;
+        float2 kf[C::PPL];
 #pragma unroll
-      for (int c = 0; c < C::CPL; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * row_stride + (c * C::LPR + pl) * 16);
-        E::unpack_pairs(raw, &kf[c * (C::EPC / 2)]);
+        for (int c = 0; c < C::CPL; ++c) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(ks + row * row_stride + (c * C::LPR + pl) * 16);
+          E::unpack_pairs(raw, &kf[c * (C::EPC / 2)]);
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+          float2 a = __fmul2_rn(qf[g][0], kf[0]);
+#pragma unroll
+          for (int e = 1; e < C::PPL; ++e) a = __ffma2_rn(qf[g][e], kf[e], a);
+          sv[i * GT + g] = a.x + a.y;
+        }
       }
 #pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float2 a = __fmul2_rn(qf[g][0], kf[0]);
+      for (int lv = 0; lv < C::SL; ++lv) {  // butterfly reduce-scatter over the row group
+        const int o = C::LPR >> (lv + 1);
+        const int half = C::NV >> (lv + 1);
+        const bool up = (lane & o) != 0;
 #pragma unroll
-        for (int e = 1; e < C::PPL; ++e) a = __ffma2_rn(qf[g][e], kf[e], a);
-        sv[i * GT + g] = a.x + a.y;
+        for (int j = 0; j < half; ++j) {
+          const float send = up ? sv[j] : sv[j + half];
+          const float keep = up ? sv[j + half] : sv[j];
+          sv[j] = keep + __shfl_xor_sync(FULL_MASK, send, o);
+        }
       }
-    }
 #pragma unroll
-    for (int lv = 0; lv < C::SL; ++lv) {  // butterfly reduce-scatter over the row group
-      const int o = C::LPR >> (lv + 1);
-      const int half = C::NV >> (lv + 1);
-      const bool up = (lane & o) != 0;
+      for (int lv = C::SL; lv < C::LOG_LPR; ++lv) sv[0] += __shfl_xor_sync(FULL_MASK, sv[0], C::LPR >> (lv + 1));
 #pragma unroll
-      for (int j = 0; j < half; ++j) {
-        const float send = up ? sv[j] : sv[j + half];
-        const float keep = up ? sv[j + half] : sv[j];
-        sv[j] = keep + __shfl_xor_sync(FULL_MASK, send, o);
+      for (int j = 0; j < C::R; ++j) {
+        const float x = sv[j] * p.scale_log2;
+        sc[j] = hold_row[j] < valid_rows ? x : -INFINITY;
       }
-    }
-#pragma unroll
-    for (int lv = C::SL; lv < C::LOG_LPR; ++lv) sv[0] += __shfl_xor_sync(FULL_MASK, sv[0], C::LPR >> (lv + 1));
-#pragma unroll
-    for (int j = 0; j < C::R; ++j) {
-      const float x = sv[j] * p.scale_log2;
-      sc[j] = hold_row[j] < valid_rows ? x : -INFINITY;
     }
   };
 
   // Phase B, part 1: the online-softmax max update. m' = max(m, tile max) and
   // alpha = exp2(m - m') is the identity when no score of the tile exceeds the running max,
   // so the warp max and the rescale run only when one does (same arithmetic as always).
-  auto tile_max_update = [&](const float (&sc)[C::R]) {
-    bool exceeds = false;
-#pragma unroll
-    for (int j = 0; j < C::R; ++j) {
-#pragma unroll
-      for (int g = 0; g < GT; ++g)
-        if (hold_g[j] == g) exceeds |= sc[j] > m_run[g];
-    }
-    if (__builtin_expect(__any_sync(FULL_MASK, exceeds), 0)) {
-      float tmax[GT];
-#pragma unroll
-      for (int g = 0; g < GT; ++g) tmax[g] = -INFINITY;
+  auto tile_max_update = [&](const float (&sc)[RR]) {
+    if constexpr (MMA) {
+      mw.max_update(sc);
+    } else {
+      bool exceeds = false;
 #pragma unroll
       for (int j = 0; j < C::R; ++j) {
 #pragma unroll
         for (int g = 0; g < GT; ++g)
-          if (hold_g[j] == g) tmax[g] = fmaxf(tmax[g], sc[j]);
+          if (hold_g[j] == g) exceeds |= sc[j] > m_run[g];
       }
+      if (__builtin_expect(__any_sync(FULL_MASK, exceeds), 0)) {
+        float tmax[GT];
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) {
+        for (int g = 0; g < GT; ++g) tmax[g] = -INFINITY;
 #pragma unroll
-        for (int g = 0; g < GT; ++g) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(FULL_MASK, tmax[g], o));
+        for (int j = 0; j < C::R; ++j) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g)
+            if (hold_g[j] == g) tmax[g] = fmaxf(tmax[g], sc[j]);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(FULL_MASK, tmax[g], o));
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+          const float mn = fmaxf(m_run[g], tmax[g]);  // finite: the tile has a live row
+          const float alpha = exp2f(m_run[g] - mn);
+          m_run[g] = mn;
+          l_run[g] *= alpha;
+          const float2 alpha2 = make_float2(alpha, alpha);
+#pragma unroll
+          for (int e = 0; e < C::PPL; ++e) acc[g][e] = __fmul2_rn(acc[g][e], alpha2);
+        }
       }
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        const float mn = fmaxf(m_run[g], tmax[g]);  // finite: the tile has a live row
-        const float alpha = exp2f(m_run[g] - mn);
-        m_run[g] = mn;
-        l_run[g] *= alpha;
-        const float2 alpha2 = make_float2(alpha, alpha);
-#pragma unroll
-        for (int e = 0; e < C::PPL; ++e) acc[g][e] = __fmul2_rn(acc[g][e], alpha2);
       }
-    }
   };
 
   // Phase B, part 2: probabilities, their shuffle to the lanes that own each row's V chunk,
   // and P.V into the fp32 accumulators. Rows at or past valid_rows contribute exact zeros
   // (their V is zeroed too, so stale bytes -- even NaN patterns -- never reach acc).
-  auto tile_pv = [&](int stage, const float (&sc)[C::R], int valid_rows, bool full) {
-    float pj[C::R];
+  auto tile_pv = [&](int stage, const float (&sc)[RR], int valid_rows, bool full) {
+    if constexpr (MMA) {
+      mw.pv(stages_addr + uint32_t(stage) * uint32_t(stage_stride) + uint32_t(kv_stage_bytes), sc, valid_rows, full);
+    } else {
+      float pj[C::R];
 #pragma unroll
-    for (int j = 0; j < C::R; ++j) {
-      float mj = m_run[0];
+      for (int j = 0; j < C::R; ++j) {
+        float mj = m_run[0];
 #pragma unroll
-      for (int g = 1; g < GT; ++g)
-        if (hold_g[j] == g) mj = m_run[g];
-      pj[j] = exp2f(sc[j] - mj);
-      if (primary) {
+        for (int g = 1; g < GT; ++g)
+          if (hold_g[j] == g) mj = m_run[g];
+        pj[j] = exp2f(sc[j] - mj);
+        if (primary) {
 #pragma unroll
-        for (int g = 0; g < GT; ++g)
-          if (hold_g[j] == g) l_run[g] += pj[j];
+          for (int g = 0; g < GT; ++g)
+            if (hold_g[j] == g) l_run[g] += pj[j];
+        }
       }
-    }
-    const unsigned char* vs = my_stages + size_t(stage) * stage_stride + kv_stage_bytes + head_off;
+      const unsigned char* vs = my_stages + size_t(stage) * stage_stride + kv_stage_bytes + head_off;
 #pragma unroll
-    for (int i = 0; i < C::NT; ++i) {
-      const int row = i * C::RPL + rg;
-      float2 vf[C::PPL];
+      for (int i = 0; i < C::NT; ++i) {
+        const int row = i * C::RPL + rg;
+        float2 vf[C::PPL];
 #pragma unroll
-      for (int c = 0; c < C::CPL; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * row_stride + (c * C::LPR + pl) * 16);
-        E::unpack_pairs(raw, &vf[c * (C::EPC / 2)]);
-      }
-      if (!full) {
-        const bool live = row < valid_rows;
+        for (int c = 0; c < C::CPL; ++c) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(vs + row * row_stride + (c * C::LPR + pl) * 16);
+          E::unpack_pairs(raw, &vf[c * (C::EPC / 2)]);
+        }
+        if (!full) {
+          const bool live = row < valid_rows;
 #pragma unroll
-        for (int e = 0; e < C::PPL; ++e) vf[e] = live ? vf[e] : make_float2(0.f, 0.f);
-      }
+          for (int e = 0; e < C::PPL; ++e) vf[e] = live ? vf[e] : make_float2(0.f, 0.f);
+        }
 #pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        const int idx = i * GT + g;
-        const int src = (rg << C::LOG_LPR) + ((idx / C::R) << C::AL);
-        const float pv = __shfl_sync(FULL_MASK, pj[idx % C::R], src);
-        const float2 pv2 = make_float2(pv, pv);
+        for (int g = 0; g < GT; ++g) {
+          const int idx = i * GT + g;
+          const int src = (rg << C::LOG_LPR) + ((idx / C::R) << C::AL);
+          const float pv = __shfl_sync(FULL_MASK, pj[idx % C::R], src);
+          const float2 pv2 = make_float2(pv, pv);
 #pragma unroll
-        for (int e = 0; e < C::PPL; ++e) acc[g][e] = __ffma2_rn(pv2, vf[e], acc[g][e]);
+          for (int e = 0; e < C::PPL; ++e) acc[g][e] = __ffma2_rn(pv2, vf[e], acc[g][e]);
+        }
       }
     }
   };
 
   auto start_segment = [&](const Cursor& c) {
-    const int hq = c.h * p.group + c.gc * GT;
-    const T* qrow = reinterpret_cast<const T*>(p.q) + int64_t(c.b) * p.q_sb;
+    if constexpr (MMA) {
+      mw.start(reinterpret_cast<const T*>(p.q) + int64_t(c.b) * p.q_sb, p.q_sh, c.h * p.group + c.gc * GT);
+    } else {
+      const int hq = c.h * p.group + c.gc * GT;
+      const T* qrow = reinterpret_cast<const T*>(p.q) + int64_t(c.b) * p.q_sb;
 #pragma unroll
-    for (int g = 0; g < GT; ++g) {
+      for (int g = 0; g < GT; ++g) {
 #pragma unroll
-      for (int cc = 0; cc < C::CPL; ++cc) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qrow + int64_t(hq + g) * p.q_sh +
-                                                                 (cc * C::LPR + pl) * C::EPC));
-        E::unpack_pairs(raw, &qf[g][cc * (C::EPC / 2)]);
+        for (int cc = 0; cc < C::CPL; ++cc) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qrow + int64_t(hq + g) * p.q_sh +
+                                                                   (cc * C::LPR + pl) * C::EPC));
+          E::unpack_pairs(raw, &qf[g][cc * (C::EPC / 2)]);
+        }
+        m_run[g] = -INFINITY;
+        l_run[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < C::PPL; ++e) acc[g][e] = make_float2(0.f, 0.f);
       }
-      m_run[g] = -INFINITY;
-      l_run[g] = 0.f;
-#pragma unroll
-      for (int e = 0; e < C::PPL; ++e) acc[g][e] = make_float2(0.f, 0.f);
     }
   };
 
   // Fused append: after tile c's copies landed in `stage`, overwrite the appended token's
   // K and V rows with the source rows (16 B per lane), so the tile holds the new token
-  // whatever the copy read from the pool.
+  // whatever the copy read from the pool. (Tensor-core stages hold the row in swizzled
+  // 16-byte units; unit u of token t sits at mw.unit_addr(0, t, u).)
   auto patch = [&](const Cursor& c, int stage) {
     if (!p.append) return;
     const int ap = apos[c.b];
     if (ap < 0 || (ap >> C::LOG_TILE) != c.tile) return;
-    unsigned char* krow = my_stages + size_t(stage) * stage_stride + (ap & (C::TILE - 1)) * row_stride + head_off;
+    const int t = ap & (C::TILE - 1);
+    unsigned char* ktile = my_stages + size_t(stage) * stage_stride;
+    unsigned char* krow = ktile + t * row_stride + head_off;
     unsigned char* vrow = krow + kv_stage_bytes;
     const T* ksrc = reinterpret_cast<const T*>(p.app_k) + int64_t(c.b) * p.app_k_sb + int64_t(c.h) * p.app_k_sh;
     const T* vsrc = reinterpret_cast<const T*>(p.app_v) + int64_t(c.b) * p.app_v_sb + int64_t(c.h) * p.app_v_sh;
@@ -734,7 +785,11 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       const int ci = isv ? i - C::CHUNKS : i;
       const uint4 x = !isv && p.rope_cos ? appended_k_chunk(ksrc, c.b, ci)
                                          : __ldg(reinterpret_cast<const uint4*>((isv ? vsrc : ksrc) + ci * C::EPC));
-      *reinterpret_cast<uint4*>((isv ? vrow : krow) + ci * 16) = x;
+      if constexpr (MMA) {
+        *reinterpret_cast<uint4*>(ktile + (isv ? kv_stage_bytes : 0) + mw.unit_addr(0u, t, ci)) = x;
+      } else {
+        *reinterpret_cast<uint4*>((isv ? vrow : krow) + ci * 16) = x;
+      }
     }
     fence_proxy_async_smem();  // the stage is refilled by TMA later
     __syncwarp();
@@ -886,7 +941,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   // ---- pipelined tile loop: scores of tile k+1 overlap softmax + P.V of tile k ---------
   int s = 0;              // stage of tile k (= k % S)
   uint32_t parity = 0u;   // mbarrier phase parity of tile k (= (k / S) & 1)
-  float sc_cur[C::R], sc_nxt[C::R];
+  float sc_cur[RR], sc_nxt[RR];
   if (!warp_wait_phase(smem_addr(my_bars), 0u, WAIT_LIMIT_NS)) {
     fail_and_drain(0);
     return;
@@ -949,50 +1004,94 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     // ---- segment end ---------------------------------------------------------------------
     const bool seg_end = (k == nunits - 1) || (cur.tile == cur.ntile - 1);
     if (__builtin_expect(seg_end, 0)) {
-      float l_tot[GT];
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float x = l_run[g];
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(FULL_MASK, x, o);
-        l_tot[g] = x;
-      }
-#pragma unroll
-      for (int o = C::LPR; o < 32; o <<= 1) {
+      const bool whole = seg_first_tile == 0 && cur.tile == cur.ntile - 1;
+      // Split item: (m, l, acc) go to this worker's slot and the last arrival merges.
+      const int64_t slot = int64_t(wslot) * 2 + (first_segment ? 0 : 1);
+      if constexpr (MMA) {
+        float lt[2];
+        mw.total_l(lt);
+        if (whole) {
+          if (p.mode == 0) {
+            mw.store_out(reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb + int64_t(hq0) * p.o_sh, p.o_sh, lt);
+          } else {
+            const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
+            mw.store_ml(p.part_m + hrow, p.part_l + hrow, lt);
+            mw.store_acc(p.part_acc + hrow * D);
+          }
+        } else {
+          mw.store_ml(p.ws_ml + slot * (2 * GT), p.ws_ml + slot * (2 * GT) + GT, lt);
+          mw.store_acc(p.ws_acc + slot * (GT * D));
+        }
+      } else {
+        float l_tot[GT];
 #pragma unroll
         for (int g = 0; g < GT; ++g) {
+          float x = l_run[g];
 #pragma unroll
-          for (int e = 0; e < C::PPL; ++e) {
-            acc[g][e].x += __shfl_xor_sync(FULL_MASK, acc[g][e].x, o);
-            acc[g][e].y += __shfl_xor_sync(FULL_MASK, acc[g][e].y, o);
+          for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(FULL_MASK, x, o);
+          l_tot[g] = x;
+        }
+#pragma unroll
+        for (int o = C::LPR; o < 32; o <<= 1) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+#pragma unroll
+            for (int e = 0; e < C::PPL; ++e) {
+              acc[g][e].x += __shfl_xor_sync(FULL_MASK, acc[g][e].x, o);
+              acc[g][e].y += __shfl_xor_sync(FULL_MASK, acc[g][e].y, o);
+            }
           }
         }
-      }
-      const bool whole = seg_first_tile == 0 && cur.tile == cur.ntile - 1;
-      if (whole) {
-        if (p.mode == 0) {
-          if (rg == 0) {
-            T* orow = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb;
+        if (whole) {
+          if (p.mode == 0) {
+            if (rg == 0) {
+              T* orow = reinterpret_cast<T*>(p.out) + int64_t(cur.b) * p.o_sb;
 #pragma unroll
-            for (int g = 0; g < GT; ++g) {
-              const float inv = 1.f / fmaxf(l_tot[g], 1.f);
+              for (int g = 0; g < GT; ++g) {
+                const float inv = 1.f / fmaxf(l_tot[g], 1.f);
 #pragma unroll
-              for (int c = 0; c < C::CPL; ++c) {
-                float o[C::EPC];
+                for (int c = 0; c < C::CPL; ++c) {
+                  float o[C::EPC];
 #pragma unroll
-                for (int e = 0; e < C::EPC; ++e) o[e] = acc_at(g, c * C::EPC + e) * inv;
-                *reinterpret_cast<uint4*>(orow + int64_t(hq0 + g) * p.o_sh + (c * C::LPR + pl) * C::EPC) =
-                    E::pack(o);
+                  for (int e = 0; e < C::EPC; ++e) o[e] = acc_at(g, c * C::EPC + e) * inv;
+                  *reinterpret_cast<uint4*>(orow + int64_t(hq0 + g) * p.o_sh + (c * C::LPR + pl) * C::EPC) =
+                      E::pack(o);
+                }
+              }
+            }
+          } else {
+            const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
+            if (lane == 0) {
+#pragma unroll
+              for (int g = 0; g < GT; ++g) {
+                p.part_m[hrow + g] = m_run[g];
+                p.part_l[hrow + g] = l_tot[g];
+              }
+            }
+            if (rg == 0) {
+#pragma unroll
+              for (int g = 0; g < GT; ++g) {
+#pragma unroll
+                for (int c = 0; c < C::CPL; ++c) {
+                  float* dst = p.part_acc + (hrow + g) * D + (c * C::LPR + pl) * C::EPC;
+#pragma unroll
+                  for (int e = 0; e < C::EPC; e += 4)
+                    *reinterpret_cast<float4*>(dst + e) =
+                        make_float4(acc_at(g, c * C::EPC + e), acc_at(g, c * C::EPC + e + 1),
+                                    acc_at(g, c * C::EPC + e + 2), acc_at(g, c * C::EPC + e + 3));
+                }
               }
             }
           }
         } else {
-          const int64_t hrow = int64_t(cur.b) * p.n_head + hq0;
+          // Split item: park (m, l, acc) in this worker's slot, then the last arrival merges.
+          float* ml = p.ws_ml + slot * (2 * GT);
+          float* wa = p.ws_acc + slot * (GT * D);
           if (lane == 0) {
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
-              p.part_m[hrow + g] = m_run[g];
-              p.part_l[hrow + g] = l_tot[g];
+              ml[g] = m_run[g];
+              ml[GT + g] = l_tot[g];
             }
           }
           if (rg == 0) {
@@ -1000,7 +1099,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
             for (int g = 0; g < GT; ++g) {
 #pragma unroll
               for (int c = 0; c < C::CPL; ++c) {
-                float* dst = p.part_acc + (hrow + g) * D + (c * C::LPR + pl) * C::EPC;
+                float* dst = wa + g * D + (c * C::LPR + pl) * C::EPC;
 #pragma unroll
                 for (int e = 0; e < C::EPC; e += 4)
                   *reinterpret_cast<float4*>(dst + e) =
@@ -1010,32 +1109,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
             }
           }
         }
-      } else {
-        // Split item: park (m, l, acc) in this worker's slot, then the last arrival merges.
-        const int64_t slot = int64_t(wslot) * 2 + (first_segment ? 0 : 1);
-        float* ml = p.ws_ml + slot * (2 * GT);
-        float* wa = p.ws_acc + slot * (GT * D);
-        if (lane == 0) {
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            ml[g] = m_run[g];
-            ml[GT + g] = l_tot[g];
-          }
-        }
-        if (rg == 0) {
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-#pragma unroll
-            for (int c = 0; c < C::CPL; ++c) {
-              float* dst = wa + g * D + (c * C::LPR + pl) * C::EPC;
-#pragma unroll
-              for (int e = 0; e < C::EPC; e += 4)
-                *reinterpret_cast<float4*>(dst + e) =
-                    make_float4(acc_at(g, c * C::EPC + e), acc_at(g, c * C::EPC + e + 1),
-                                acc_at(g, c * C::EPC + e + 2), acc_at(g, c * C::EPC + e + 3));
-            }
-          }
-        }
+      }
+      if (!whole) {
         // Arrive on the item's counter. A segment that ends inside the range arrives now, with
         // a release-ordered add whose answer is read only after the loop (the warp keeps
         // streaming); the other pieces of its item end later, so one of them usually merges.
@@ -1065,7 +1140,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       tile_scores(s_n, nxt.len, sc_nxt);
     }
 #pragma unroll
-    for (int j = 0; j < C::R; ++j) sc_cur[j] = sc_nxt[j];
+    for (int j = 0; j < RR; ++j) sc_cur[j] = sc_nxt[j];
     cur = nxt;
     s = s_n;
     parity = parity_n;
@@ -1089,23 +1164,23 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   }
 }
 
-template <typename T, int D, int GT, bool CTA>
+template <typename T, int D, int GT, bool CTA, bool MMA>
 __global__ void __launch_bounds__(CTA ? 288 : 256, 1)
     pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) unsigned char smem[];
   uint32_t* s_epoch = reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off);
   if (threadIdx.x == 0) *s_epoch = *reinterpret_cast<volatile unsigned*>(p.epoch_word);
-  decode_body<T, D, GT, CTA>(p, kmap, vmap, smem);
+  decode_body<T, D, GT, CTA, MMA>(p, kmap, vmap, smem);
   __syncwarp();
   if ((threadIdx.x & 31) == 0)
     leave_launch(p.exit_counter, p.epoch_word, *s_epoch, gridDim.x * (blockDim.x >> 5), p.err);
 }
 
-template <typename T, int D, int GT, bool CTA = false>
+template <typename T, int D, int GT, bool CTA = false, bool MMA = false>
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                           dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
-  auto fn = pd_decode_kernel<T, D, GT, CTA>;
+  auto fn = pd_decode_kernel<T, D, GT, CTA, MMA>;
   static int attr_smem[64] = {0};  // per-device dynamic-smem opt-in already granted
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);

@@ -11,6 +11,10 @@ DecodeLaunchFn decode_launcher_bf16(int d_index, int gt_index);
 // Shared-stage (CTA) decode kernels: head_dim 64..256 (d_index 3..5), bf16 / fp16.
 DecodeLaunchFn decode_launcher_cta_f16(int d_index, int gt_index);
 DecodeLaunchFn decode_launcher_cta_bf16(int d_index, int gt_index);
+// Tensor-core decode kernels (per-warp stages, 128-byte-swizzled pool maps): head_dim 64..256
+// (d_index 3..5), bf16 / fp16.
+DecodeLaunchFn decode_launcher_mma_f16(int d_index, int gt_index);
+DecodeLaunchFn decode_launcher_mma_bf16(int d_index, int gt_index);
 
 // Append: copies K and V rows into their pool slots. src/dst dtype codes as PD_F32/F16/BF16.
 cudaError_t launch_append(const AppendParams& p, int src_dtype, int dst_dtype, bool vec16,

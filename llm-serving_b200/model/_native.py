@@ -199,7 +199,8 @@ def get_decode_tuning() -> tuple[int, int, int, int]:
 
 
 def set_decode_mode(mode: int, shared_stages: int = 0, row_cost: int = -1) -> None:
-    """0: per-warp kernel everywhere (default), 1: shared-stage kernel where it applies;
+    """0: per-warp kernel, tensor-core tile math where it applies (default); 1: shared-stage
+    kernel where it applies; 2: per-warp kernel with CUDA-core tile math everywhere.
     row_cost: extra columns charged per row start by the column split (-1 keeps it)."""
     check(require().pd_set_decode_mode(int(mode), int(shared_stages), int(row_cost)), "pd_set_decode_mode")
 

@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 #: Output tolerance for bf16/fp16 results against the fp32 oracle. 2e-3 absolute is the
@@ -55,3 +57,18 @@ def assert_output_close(got, ref_f32, dtype):
         f"{int(bad.sum())} elements beyond tolerance; max|delta| {diff.max().item()}"
     )
     return diff.max().item()
+
+
+@contextlib.contextmanager
+def decode_mode(mode: int, shared_stages: int = 0, row_cost: int = -1):
+    """Runs the body with pd_set_decode_mode(mode, ...) and restores the previous choice.
+    0: per-warp kernel with tensor-core tile math where it applies, 1: shared stages where
+    they apply, 2: per-warp kernel with CUDA-core tile math."""
+    from model import _native
+
+    before = _native.get_decode_mode()
+    _native.set_decode_mode(mode, shared_stages, row_cost)
+    try:
+        yield
+    finally:
+        _native.set_decode_mode(*before)

@@ -101,7 +101,9 @@ def test_tuning_is_validated_and_restorable():
 def test_decode_mode_is_validated_and_restorable():
     before = _native.get_decode_mode()
     with pytest.raises(ValueError):
-        _native.set_decode_mode(2)
+        _native.set_decode_mode(3)
+    with pytest.raises(ValueError):
+        _native.set_decode_mode(-1)
     with pytest.raises(ValueError):
         _native.set_decode_mode(1, 9)
     assert _native.get_decode_mode() == before
@@ -111,6 +113,8 @@ def test_decode_mode_is_validated_and_restorable():
     assert _native.get_decode_mode() == (1, 3, 5)
     _native.set_decode_mode(0, 0, -1)
     assert _native.get_decode_mode() == (0, 0, 5)
+    _native.set_decode_mode(2, 0, -1)
+    assert _native.get_decode_mode() == (2, 0, 5)
     _native.set_decode_mode(*before)
     assert _native.get_decode_mode() == before
 

@@ -32,6 +32,12 @@ SHAPES = [
     pytest.param(3, 16, 8, 128, 16, [1, 17, 40], id="qwen3-columns-lt-ctas"),
     pytest.param(2, 16, 8, 64, 16, [4000, 2], id="qwen3-d64-columns"),
     pytest.param(5, 64, 8, 128, 16, [33, 700, 1, 2500, 64], id="gqa8-columns"),
+    # tensor-core tiles made of several TMA boxes (blocks smaller than a tile), and a block
+    # size below 8 tokens (CUDA-core tile math)
+    pytest.param(2, 16, 8, 128, 8, [300, 17], id="d128-bs8-two-boxes"),
+    pytest.param(2, 8, 2, 64, 8, [301, 9], id="d64-bs8-four-boxes"),
+    pytest.param(2, 8, 2, 256, 8, [129, 8], id="d256-bs8"),
+    pytest.param(2, 8, 2, 128, 4, [50, 3], id="d128-bs4"),
 ]
 
 
@@ -60,8 +66,9 @@ def test_decode_matches_oracle(cuda_device, B, H, Hkv, D, bs, lengths, dtype):
     assert _native.device_error() == 0
 
 
-@pytest.mark.parametrize("mode,row_cost", [(0, 2), (1, 2), (0, 0), (0, 7)],
-                         ids=["per-warp", "shared-stage", "per-warp-rowcost0", "per-warp-rowcost7"])
+@pytest.mark.parametrize("mode,row_cost", [(0, 2), (1, 2), (2, 2), (0, 0), (0, 7), (2, 0)],
+                         ids=["tensor-core", "shared-stage", "cuda-core", "tensor-core-rowcost0",
+                              "tensor-core-rowcost7", "cuda-core-rowcost0"])
 @pytest.mark.parametrize("B,H,Hkv,D,bs,lengths", [
     (8, 16, 8, 128, 16, [1664] * 8),
     (6, 16, 8, 128, 16, [0, 5, 3000, 129, 16, 17]),
@@ -69,7 +76,9 @@ def test_decode_matches_oracle(cuda_device, B, H, Hkv, D, bs, lengths, dtype):
     (4, 32, 8, 128, 16, [700, 33, 2048, 1]),     # 4 q heads per kv head
     (2, 16, 8, 64, 32, [4000, 2]),
     (2, 16, 8, 256, 16, [900, 77]),
-    (3, 16, 4, 128, 16, [300, 1, 2100]),         # 4 items per row: per-warp kernel in both modes
+    (3, 16, 4, 128, 16, [300, 1, 2100]),         # 4 items per row: per-warp kernel in every mode
+    (3, 8, 2, 256, 16, [2048, 5, 700]),          # Qwen3.5 full-attention heads
+    (2, 64, 8, 128, 16, [1000, 3]),              # 8 q heads per kv head
 ])
 def test_both_decode_kernels_match_the_oracle(cuda_device, mode, row_cost, B, H, Hkv, D, bs, lengths):
     from model import _native

@@ -14,7 +14,7 @@ from pathlib import Path
 import pytest
 import torch
 
-from helpers import assert_output_close
+from helpers import assert_output_close, decode_mode
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -46,11 +46,13 @@ CASES = [
     pytest.param(2, 32, 2, 64, 16, [90, 300], torch.bfloat16, id="gqa16-chunks"),
     pytest.param(2, 8, 2, 256, 16, [700, 33], torch.bfloat16, id="d256-gqa4"),
     pytest.param(4, 4, 2, 32, 8, [5, 9, 64, 1], torch.float32, id="fp32-d32-bs8"),
+    pytest.param(3, 16, 8, 128, 8, [7, 8, 301], torch.bfloat16, id="d128-bs8-two-boxes"),
 ]
 
 
+@pytest.mark.parametrize("mode", [0, 2], ids=["tensor-core", "cuda-core"])
 @pytest.mark.parametrize("B,H,Hkv,D,bs,lengths,dtype", CASES)
-def test_one_launch_equals_append_then_decode(cuda_device, B, H, Hkv, D, bs, lengths, dtype):
+def test_one_launch_equals_append_then_decode(cuda_device, B, H, Hkv, D, bs, lengths, dtype, mode):
     from model import _native
     from model.triton_decode import paged_decode_plan
 
@@ -60,12 +62,13 @@ def test_one_launch_equals_append_then_decode(cuda_device, B, H, Hkv, D, bs, len
     seqlen = (pos + 1).to(torch.int32)                                   # ... and attend over it
     k2, v2 = k.clone(), v.clone()
 
-    fused = paged_decode_plan(q, [k], [v], table, seqlen)
-    out_fused = fused.run_append(0, q, k_new, v_new, pos)
-    split = paged_decode_plan(q, [k2], [v2], table, seqlen)
-    _native.append_table(k2, v2, table, pos, k_new, v_new)
-    out_split = split.run(0, q)
-    torch.cuda.synchronize()
+    with decode_mode(mode):
+        fused = paged_decode_plan(q, [k], [v], table, seqlen)
+        out_fused = fused.run_append(0, q, k_new, v_new, pos)
+        split = paged_decode_plan(q, [k2], [v2], table, seqlen)
+        _native.append_table(k2, v2, table, pos, k_new, v_new)
+        out_split = split.run(0, q)
+        torch.cuda.synchronize()
     assert torch.equal(out_fused, out_split), (out_fused.float() - out_split.float()).abs().max()
     assert torch.equal(k, k2) and torch.equal(v, v2)
     ref, _ = oracle.paged_decode(q.cpu(), k.cpu(), v.cpu(), table.cpu(), seqlen.cpu())
