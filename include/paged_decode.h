@@ -139,7 +139,9 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * The block table and seqlen are held by address, so in-place updates are seen by the next
  * run (the reference's invariant, model/triton_decode.py:357-363). q and out of every run
  * are contiguous (B, H, D). The plan owns no device memory: `workspace` is the caller's
- * (same contract as pd_decode). The handle is host memory released by pd_plan_destroy.
+ * (same contract as pd_decode); with at least twice pd_decode_workspace_bytes(...) (each
+ * half rounded up to 256 bytes) consecutive launches alternate between its two halves, which
+ * pd_plan_set_overlap requires. The handle is host memory released by pd_plan_destroy.
  */
 typedef struct pd_plan pd_plan;
 
@@ -180,6 +182,19 @@ int pd_plan_run_append_rope(const pd_plan* plan, int32_t layer, const void* q, v
                             int64_t v_sb, int64_t v_sh, const int64_t* pos, const void* rope_cos,
                             const void* rope_sin, int64_t rope_stride, int32_t rotary_dim,
                             void* stream);
+/* pd_plan_set_overlap -- launches of this plan made afterwards (enable = 1) may start
+ * before the previous kernel of their stream has finished (programmatic dependent launch):
+ * the kernel reads seqlen, the append positions, the block table and the pools, computes
+ * its work split and issues its first K/V copies, and only then waits for that kernel
+ * before it reads q or the appended K/V rows, writes any output or touches the workspace.
+ * Contract: the kernel launched just before on the stream writes none of seqlen, the
+ * positions, the block table or this layer's pools (the previous layer's decode of a step,
+ * a projection that produces q and the new rows: yes; a separate append into this layer's
+ * pool, or the step's seqlen update: no). enable = 0 (the default) restores plain launches.
+ * Needs a plan workspace of two halves (pd_plan_create): PD_ERR_WORKSPACE otherwise.
+ * No reference counterpart (the reference launches one Triton kernel per call). */
+int pd_plan_set_overlap(pd_plan* plan, int32_t enable);
+
 void pd_plan_destroy(pd_plan* plan);
 
 /* ---------------------------------------------------------------- split-KV partials

@@ -30,10 +30,10 @@ struct Tuning {
 };
 Tuning g_tuning;
 std::mutex g_mutex;
-// Decode kernel choice: 1 = shared-stage (CTA) kernel wherever a row has exactly one item per
-// consumer warp, 0 = per-warp kernel everywhere (the default: on B200 it streams config-2
-// shapes as fast as the shared-stage kernel with less synchronisation). cta_stages 0 = sized
-// from shared memory.
+// Decode kernel choice: 0 = per-warp kernel, tensor-core tile math where it applies (the
+// default), 1 = shared-stage (CTA) kernel wherever a row has exactly one item per consumer
+// warp, 2 = per-warp kernel with CUDA-core tile math everywhere. cta_stages 0 = sized from
+// shared memory.
 int g_decode_mode = 0;
 int g_cta_stages = 0;
 int g_row_cost = 3;  // column split: virtual columns charged per row start
@@ -289,6 +289,11 @@ struct Prepared {
   WorkspaceLayout ws;
   DecodeLaunchFn fn;
   DecodeParams base;  // q/out/partials pointers filled per launch
+  // The workspace holds `halves` (1 or 2) copies of the layout, half_bytes apart. With two,
+  // consecutive launches alternate between them, so a launch that overlaps the previous one
+  // (programmatic dependent launch) never shares its counters, epoch or partials.
+  int halves = 1;
+  size_t half_bytes = 0;
 };
 
 int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* block_table,
@@ -307,6 +312,8 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   P->ws = workspace_layout(batch, n_kv_head, P->g, head_dim, P->L);
   if (batch > 0) {
     if (workspace == nullptr || workspace_bytes < P->ws.total) return PD_ERR_WORKSPACE;
+    P->half_bytes = round_up(P->ws.total, 256);
+    P->halves = workspace_bytes >= 2 * P->half_bytes ? 2 : 1;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PD_ERR_WORKSPACE;
     if (block_table == nullptr && max_blocks > 0) return PD_ERR_INVALID;
     if (seqlen == nullptr) return PD_ERR_INVALID;
@@ -389,12 +396,20 @@ struct AppendArgs {
 int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& vmap, const void* q,
                  int64_t q_sb, int64_t q_sh, void* out, int64_t o_sb, int64_t o_sh, float* pm,
                  float* pl, float* pacc, int mode, int dtype, cudaStream_t stream,
-                 const AppendArgs* app = nullptr) {
+                 const AppendArgs* app = nullptr, bool overlap = false, uint32_t* seq = nullptr) {
   const int batch = P.base.batch;
   const int es = elem_size(dtype);
   for (int b0 = 0; b0 < batch; b0 += P.L.rows_per_launch) {
     const int rows = batch - b0 < P.L.rows_per_launch ? batch - b0 : P.L.rows_per_launch;
     DecodeParams p = P.base;
+    if (P.halves == 2 && seq != nullptr && ((*seq)++ & 1u)) {  // the workspace's second half
+      const size_t h = P.half_bytes;
+      p.epoch_word = reinterpret_cast<unsigned*>(reinterpret_cast<unsigned char*>(p.epoch_word) + h);
+      p.exit_counter = reinterpret_cast<unsigned long long*>(reinterpret_cast<unsigned char*>(p.exit_counter) + h);
+      p.counters = reinterpret_cast<unsigned long long*>(reinterpret_cast<unsigned char*>(p.counters) + h);
+      p.ws_ml = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(p.ws_ml) + h);
+      p.ws_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(p.ws_acc) + h);
+    }
     p.batch = rows;
     p.mode = mode;
     p.q = static_cast<const unsigned char*>(q) + int64_t(b0) * q_sb * es;
@@ -440,7 +455,7 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
     }
     const size_t smem = smem_for(P.g.cta, P.L.warps, P.L.stages, rows, P.g.stage_bytes, &p.smem_arrays_off,
                                  &p.smem_stage_off);
-    cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream);
+    cudaError_t e = P.fn(p, kmap, vmap, dim3(P.L.grid), dim3(P.L.warps * 32), smem, stream, overlap);
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -491,6 +506,8 @@ struct pd_plan {
   std::vector<CUtensorMap> vmaps;
   std::vector<void*> k_pools;  // for the fused append's stores
   std::vector<void*> v_pools;
+  int32_t overlap = 0;  // launches may overlap the previous kernel (pd_plan_set_overlap)
+  mutable uint32_t seq = 0;  // launches made: selects the workspace half of the next one
 };
 
 extern "C" {
@@ -620,7 +637,14 @@ int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, vo
   if (check_rows(out, plan->q_sb, plan->q_sh, plan->dtype) != PD_OK) return PD_ERR_INVALID;
   return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
                       plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<cudaStream_t>(stream), nullptr, plan->overlap != 0, &plan->seq);
+}
+
+int pd_plan_set_overlap(pd_plan* plan, int32_t enable) {
+  if (plan == nullptr || enable < 0 || enable > 1) return PD_ERR_INVALID;
+  if (enable && plan->P.halves != 2) return PD_ERR_WORKSPACE;
+  plan->overlap = enable;
+  return PD_OK;
 }
 
 static int plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,
@@ -652,7 +676,7 @@ static int plan_run_append(const pd_plan* plan, int32_t layer, const void* q, vo
   app.rope_dim = rotary_dim;
   return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
                       plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
-                      static_cast<cudaStream_t>(stream), &app);
+                      static_cast<cudaStream_t>(stream), &app, plan->overlap != 0, &plan->seq);
 }
 
 int pd_plan_run_append(const pd_plan* plan, int32_t layer, const void* q, void* out,

@@ -174,6 +174,15 @@ struct Mma<__half> {
   }
 };
 
+// Programmatic dependent launch. griddep_wait blocks until the grid this launch depends on
+// (the previous kernel in the stream, when the launch allowed overlapping it) has completed
+// and its memory is visible; without such a dependency it returns at once.
+// griddep_launch_dependents lets the next kernel of the stream start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Atomic add at GPU scope with release semantics: this thread's earlier writes (and those of
 // threads synchronised with it, e.g. by __syncwarp) are visible before the add is.
 __device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long* p,
@@ -443,7 +452,8 @@ struct MergeParams {
 };
 
 // Host-side launcher signatures (one instantiation per dtype / head_dim / group tile).
+// pdl: launch with programmatic stream serialisation (may overlap the previous kernel).
 typedef cudaError_t (*DecodeLaunchFn)(const DecodeParams&, const CUtensorMap&, const CUtensorMap&,
-                                      dim3, dim3, size_t, cudaStream_t);
+                                      dim3, dim3, size_t, cudaStream_t, bool pdl);
 
 }  // namespace pd

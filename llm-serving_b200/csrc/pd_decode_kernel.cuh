@@ -200,8 +200,8 @@ __device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) 
 // warp j streams item j -- read their head's rows from it and release the stage on an
 // "empty" barrier. Contiguous block-sized copies keep the DRAM stream dense.
 template <typename T, int D, int GT, bool CTA, bool MMA>
-__device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtensorMap& kmap,
-                                            const CUtensorMap& vmap, unsigned char* smem) {
+__device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUtensorMap& kmap,
+                                                const CUtensorMap& vmap, unsigned char* smem) {
   using C = DecodeCfg<T, D, GT>;
   using E = Elem<T>;
   const int tid = threadIdx.x;
@@ -327,7 +327,9 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   const uint32_t epoch = *s_epoch;
 
   // Re-tag this launch's item counters (this CTA's share) and, in CTA 0, the exit counter
-  // with the launch's epoch. Arrivals come at least one tile later.
+  // with the launch's epoch. Arrivals come at least one tile later. (The workspace belongs to
+  // this launch alone: an overlapped launch gets the other half of its plan's workspace from
+  // the one it overlaps.)
   {
     const int64_t n_items = int64_t(B) * p.n_kv_head * p.n_gchunks;
     const unsigned long long tag = (unsigned long long)epoch << 32;
@@ -336,29 +338,41 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     if (blockIdx.x == 0 && tid == 0) atomicExch(p.exit_counter, tag);
   }
 
-  const int items_per_row = p.n_kv_head * p.n_gchunks;
-  const int64_t units = int64_t(items_per_row) * pre[B];
-
-  // ---- zero-length rows: exact zeros (mode 0) or an empty triple (mode 1) -------------
-  for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    if (lens[b] != 0) continue;
-    for (int i = tid; i < p.n_head * D; i += blockDim.x) {
-      const int h = i / D, d = i - h * D;
-      if (p.mode == 0) {
-        T* o = reinterpret_cast<T*>(p.out) + int64_t(b) * p.o_sb + int64_t(h) * p.o_sh + d;
-        *o = E::from_float(0.f);
-      } else {
-        p.part_acc[(int64_t(b) * p.n_head + h) * D + d] = 0.f;
-        if (d == 0) {
-          p.part_m[int64_t(b) * p.n_head + h] = -INFINITY;
-          p.part_l[int64_t(b) * p.n_head + h] = 0.f;
+  // ---- the dependency point ------------------------------------------------------------
+  // Everything before it -- the prologue, the work split, the first K/V copies -- reads only
+  // the lengths, positions, block table, pools and this launch's workspace, none of which the
+  // preceding kernel of an overlapped launch writes. Each warp passes this point once, on
+  // whichever path it takes, before it reads q or the appended rows or writes any output:
+  // it waits for the preceding grid, writes its share of the zero-length rows' outputs and
+  // lets the next launch start.
+  auto enter_dependent = [&]() {
+    griddep_wait();
+    // zero-length rows: exact zeros (mode 0) or an empty triple (mode 1)
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+      if (lens[b] != 0) continue;
+      for (int i = tid; i < p.n_head * D; i += blockDim.x) {
+        const int h = i / D, d = i - h * D;
+        if (p.mode == 0) {
+          T* o = reinterpret_cast<T*>(p.out) + int64_t(b) * p.o_sb + int64_t(h) * p.o_sh + d;
+          *o = E::from_float(0.f);
+        } else {
+          p.part_acc[(int64_t(b) * p.n_head + h) * D + d] = 0.f;
+          if (d == 0) {
+            p.part_m[int64_t(b) * p.n_head + h] = -INFINITY;
+            p.part_l[int64_t(b) * p.n_head + h] = 0.f;
+          }
         }
       }
     }
-  }
+    griddep_launch_dependents();
+  };
+
+  const int items_per_row = p.n_kv_head * p.n_gchunks;
+  const int64_t units = int64_t(items_per_row) * pre[B];
   if (units == 0) {
+    enter_dependent();
     store_appended();
-    return;
+    return epoch;
   }
 
   // ---- this warp's share of the work -----------------------------------------------------
@@ -411,8 +425,9 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
   }
   if (u0 >= u1) {
+    enter_dependent();
     store_appended();
-    return;
+    return epoch;
   }
   const int64_t nunits = u1 - u0;
   // Partial-result slot pair of this warp (two: its range's first and last segment).
@@ -545,15 +560,21 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       }
       issue(pc, s);
       advance(pc);
-      if (issued + 1 == (nunits < S ? nunits : S)) store_appended();
+      if (issued + 1 == (nunits < S ? nunits : S)) {
+        enter_dependent();
+        store_appended();
+      }
     }
-    if (issued < (nunits < S ? nunits : S)) store_appended();
+    if (issued < (nunits < S ? nunits : S)) {
+      enter_dependent();
+      store_appended();
+    }
     // Leave only once the copies issued last have landed (bounded): the CTA must not retire
     // with a copy in flight, whatever the consumers did.
     const int64_t from = issued > S ? issued - S : 0;
     for (int64_t j = from; j < issued; ++j)
       warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), WAIT_LIMIT_NS);
-    return;
+    return epoch;
   }
   if (!CTA) {
     const int64_t first = nunits < S ? nunits : S;
@@ -563,6 +584,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       if (pc.tile == 0 && issued + 1 < nunits) prefetch_q(pc);
     }
   }
+  enter_dependent();
   store_appended();
   // This warp's rows inside a stage: per-warp stages hold only its head; shared stages hold
   // every kv head, and the warp's item fixes its head (column mode).
@@ -944,7 +966,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
   float sc_cur[RR], sc_nxt[RR];
   if (!warp_wait_phase(smem_addr(my_bars), 0u, WAIT_LIMIT_NS)) {
     fail_and_drain(0);
-    return;
+    return epoch;
   }
   patch(cur, 0);
   start_segment(cur);
@@ -960,7 +982,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     if (!CTA && has_next) {
       if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
         fail_and_drain(k + 1);
-        return;
+        return epoch;
       }
       patch(nxt, s_n);
     }
@@ -988,7 +1010,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
       if (has_next) {
         if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
           fail_and_drain(k + 1);
-          return;
+          return epoch;
         }
         patch(nxt, s_n);
         tile_scores(s_n, nxt.len - (nxt.tile << C::LOG_TILE), sc_nxt);
@@ -1162,6 +1184,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p, const CUtenso
     merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0));
     if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0));
   }
+  return epoch;
 }
 
 template <typename T, int D, int GT, bool CTA, bool MMA>
@@ -1169,17 +1192,17 @@ __global__ void __launch_bounds__(CTA ? 288 : 256, 1)
     pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  uint32_t* s_epoch = reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off);
-  if (threadIdx.x == 0) *s_epoch = *reinterpret_cast<volatile unsigned*>(p.epoch_word);
-  decode_body<T, D, GT, CTA, MMA>(p, kmap, vmap, smem);
+  if (threadIdx.x == 0) *reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off) =
+      *reinterpret_cast<volatile unsigned*>(p.epoch_word);
+  const uint32_t epoch = decode_body<T, D, GT, CTA, MMA>(p, kmap, vmap, smem);
   __syncwarp();
   if ((threadIdx.x & 31) == 0)
-    leave_launch(p.exit_counter, p.epoch_word, *s_epoch, gridDim.x * (blockDim.x >> 5), p.err);
+    leave_launch(p.exit_counter, p.epoch_word, epoch, gridDim.x * (blockDim.x >> 5), p.err);
 }
 
 template <typename T, int D, int GT, bool CTA = false, bool MMA = false>
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                          dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
+                          dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl) {
   auto fn = pd_decode_kernel<T, D, GT, CTA, MMA>;
   static int attr_smem[64] = {0};  // per-device dynamic-smem opt-in already granted
   int dev = 0;
@@ -1190,8 +1213,24 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& kmap, const 
     if (err != cudaSuccess) return err;
     attr_smem[dev] = int(smem);
   }
-  fn<<<grid, block, smem, stream>>>(p, kmap, vmap);
-  return cudaGetLastError();
+  if (!pdl) {
+    fn<<<grid, block, smem, stream>>>(p, kmap, vmap);
+    return cudaGetLastError();
+  }
+  // Programmatic dependent launch: the kernel may start while the previous kernel of the
+  // stream finishes; it runs its prologue and first K/V copies, then waits for that kernel
+  // (griddep_wait) before it reads q or the appended rows or writes any output.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, p, kmap, vmap);
 }
 
 }  // namespace pd

@@ -84,6 +84,7 @@ _SIGNATURES = {
          _c_ptr, _c_i64, _c_i32, _c_ptr],
     ),
     "pd_plan_destroy": (None, [_c_ptr]),
+    "pd_plan_set_overlap": (ctypes.c_int, [_c_ptr, _c_i32]),
     "pd_kv_append_slots": (
         ctypes.c_int,
         [_c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_i32, _c_ptr, _c_i32, _c_ptr, _c_i64p,
@@ -310,7 +311,7 @@ def append_table(k_pool, v_pool, block_table, pos, k, v, rope=None) -> None:
 class NativePlan:
     """Owner of one ``pd_plan`` handle (host memory); destroyed with the object."""
 
-    __slots__ = ("_handle", "_lib", "__weakref__")
+    __slots__ = ("_handle", "_lib", "_overlap", "__weakref__")
 
     def __init__(self, k_caches, v_caches, block_table, seqlen, batch, n_head, scale_log2,
                  workspace) -> None:
@@ -330,15 +331,26 @@ class NativePlan:
         check(status, "pd_plan_create")
         self._handle = handle
         self._lib = lib_
+        self._overlap = False
 
-    def run(self, layer: int, q, out, stream: int) -> None:
+    def _set_overlap(self, overlap: bool) -> None:
+        if bool(overlap) != self._overlap:
+            check(self._lib.pd_plan_set_overlap(self._handle, int(bool(overlap))), "pd_plan_set_overlap")
+            self._overlap = bool(overlap)
+
+    def run(self, layer: int, q, out, stream: int, overlap: bool = False) -> None:
+        """``overlap``: the launch may start before the previous kernel of the stream ends
+        (pd_plan_set_overlap's contract: that kernel writes no seqlen, table or pool)."""
+        self._set_overlap(overlap)
         status = self._lib.pd_plan_run(self._handle, layer, q.data_ptr(), out.data_ptr(), stream)
         if status:
             check(status, "pd_plan_run")
 
-    def run_append(self, layer: int, q, out, k_new, v_new, pos, stream: int, rope=None) -> None:
+    def run_append(self, layer: int, q, out, k_new, v_new, pos, stream: int, rope=None,
+                   overlap: bool = False) -> None:
         """Append ``k_new``/``v_new`` ``(B, H_kv, D)`` at ``pos`` (int64) and decode, one launch;
         ``rope`` = (cos, sin, rotary_dim) rotates ``k_new`` first (see :func:`append_table`)."""
+        self._set_overlap(overlap)
         args = (self._handle, layer, q.data_ptr(), out.data_ptr(), k_new.data_ptr(), k_new.stride(0),
                 k_new.stride(1), v_new.data_ptr(), v_new.stride(0), v_new.stride(1), pos.data_ptr())
         if rope is None:

@@ -260,7 +260,8 @@ class PagedKV:
     block_table_decode = True
 
     def __init__(self, pool: PagedPool, block_tables, lengths, *, rope_len: int, seats=None,
-                 n_head: int | None = None, check_bounds: bool = True, fuse_append: bool = True) -> None:
+                 n_head: int | None = None, check_bounds: bool = True, fuse_append: bool = True,
+                 overlap_layers: bool = True) -> None:
         if not isinstance(pool, PagedPool):
             raise TypeError(f"PagedKV needs a PagedPool, got {type(pool).__name__}")
         if pool.device.type != "cuda":
@@ -340,6 +341,13 @@ class PagedKV:
         # read a slot another row appends); tables from BlockManager never do.
         owned = [b for table in self.block_tables for b in table]
         self.fuse_append = bool(fuse_append) and len(owned) == len(set(owned))
+        # A fused write + attend right after this container's previous fused attend may start
+        # while that launch finishes (programmatic dependent launch): nothing it reads before
+        # waiting (seqlen, positions, block table, pools) is written in between. Any other
+        # launch of the container (the seqlen update, an append on its own, advance) clears
+        # the flag, so the next attend waits for it as usual.
+        self.overlap_layers = bool(overlap_layers)
+        self._after_attend = False
 
     # ---------------------------------------------------------------- step hooks
     def build_mask(self, *, next_token: bool = False) -> None:
@@ -351,6 +359,7 @@ class PagedKV:
         self._seqlen.copy_((self.pos + int(next_token)).to(torch.int32))
         self._step_written = False
         self._seqlen_ready = True
+        self._after_attend = False
         return None
 
     def _refresh_slots(self) -> None:
@@ -436,6 +445,7 @@ class PagedKV:
 
     def _append_now(self, layer: int, k3: torch.Tensor, v3: torch.Tensor, rope=None) -> None:
         """The append alone: one ``pd_kv_append_table`` launch on the current stream."""
+        self._after_attend = False
         with torch.cuda.device(self.pool._keys[layer].device):
             _native.append_table(self.pool._keys[layer], self.pool._values[layer], self._block_table_tensor,
                                  self.pos, _unit_last_stride(k3), _unit_last_stride(v3.to(k3.dtype)), rope)
@@ -475,14 +485,18 @@ class PagedKV:
                 and pending.stream == torch.cuda.current_stream(self.device)
                 and plan.can_fuse_append(pending.k, pending.v, self.pos, pending.rope)):
             self.pool._pending = None
-            return plan.run_append(layer, q3, pending.k, pending.v, self.pos, out=out3,
-                                   rope=pending.rope).unsqueeze(2)
+            out3 = plan.run_append(layer, q3, pending.k, pending.v, self.pos, out=out3, rope=pending.rope,
+                                   overlap=self.overlap_layers and self._after_attend)
+            self._after_attend = True
+            return out3.unsqueeze(2)
         self.pool.flush()
+        self._after_attend = False
         return plan.run(layer, q3, out=out3).unsqueeze(2)
 
     def advance(self) -> None:
         """Move every active row's cursor one token (device in place, then host mirrors)."""
         self.pool.flush()
+        self._after_attend = False
         self.pos.add_(self.active)
         self.valid.copy_(torch.maximum(self.valid, self.pos))
         for row in range(self.batch):

@@ -296,7 +296,9 @@ class PagedDecodePlan:
             scale = 1.0 / math.sqrt(d)
         with torch.cuda.device(q.device):
             need = _native.workspace_bytes(b, h, k_caches[0].shape[2], d, q.dtype)
-            self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
+            # two halves: consecutive launches alternate, which overlapped launches need
+            half = -(-max(need, 256) // 256) * 256
+            self._workspace = torch.empty(2 * half, dtype=torch.uint8, device=q.device)
             self._native_plan = _native.NativePlan(
                 k_caches, v_caches, block_table, seqlen, b, h, float(scale) * _LOG2E, self._workspace
             )
@@ -326,12 +328,17 @@ class PagedDecodePlan:
             raise ValueError(f"out must be a contiguous {self.q_shape} {self.q_dtype} tensor on {self.q_device}")
         return out
 
-    def run(self, layer: int, q, *, out=None):
+    def run(self, layer: int, q, *, out=None, overlap: bool = False):
         """Launch the kernel for one layer; ``q`` must match the validated layout. ``out``
-        (optional) is a preallocated contiguous ``(B, H, D)`` result buffer."""
+        (optional) is a preallocated contiguous ``(B, H, D)`` result buffer.
+
+        ``overlap=True`` lets the launch start while the previous kernel of the stream
+        finishes (programmatic dependent launch): it reads seqlen, the block table and the
+        pools and issues its first K/V copies before it waits for that kernel, so that kernel
+        must write none of them (the previous layer's decode of a step does not)."""
         layer = self._check_query(layer, q)
         out = self._output(out)
-        self._native_plan.run(layer, q, out, torch.cuda.current_stream(self.q_device).cuda_stream)
+        self._native_plan.run(layer, q, out, torch.cuda.current_stream(self.q_device).cuda_stream, overlap)
         return out
 
     def can_fuse_append(self, k_new, v_new, pos, rope=None) -> bool:
@@ -359,7 +366,7 @@ class PagedDecodePlan:
         return (pos.dtype == torch.int64 and tuple(pos.shape) == (b,) and pos.device == self.q_device
                 and pos.stride(0) == 1)
 
-    def run_append(self, layer: int, q, k_new, v_new, pos, *, out=None, rope=None):
+    def run_append(self, layer: int, q, k_new, v_new, pos, *, out=None, rope=None, overlap: bool = False):
         """Store row ``b``'s new K/V ``(B, H_kv, D)`` at logical position ``pos[b]`` of layer
         ``layer``'s pools and decode that layer, in one launch.
 
@@ -367,7 +374,8 @@ class PagedDecodePlan:
         are bit-identical -- provided no row reads a slot another row appends (rows do not
         share blocks they write). ``rope`` = (cos, sin, rotary_dim) gives ``k_new`` before its
         rotary embedding, which the launch applies exactly as the model's torch ops would.
-        Tensors must pass :meth:`can_fuse_append`.
+        Tensors must pass :meth:`can_fuse_append`. ``overlap`` as in :meth:`run` (``pos`` is
+        read before the wait as well; ``k_new``/``v_new`` and ``q`` after it).
         """
         layer = self._check_query(layer, q)
         if not self.can_fuse_append(k_new, v_new, pos, rope):
@@ -377,7 +385,7 @@ class PagedDecodePlan:
             )
         out = self._output(out)
         self._native_plan.run_append(layer, q, out, k_new, v_new, pos,
-                                     torch.cuda.current_stream(self.q_device).cuda_stream, rope)
+                                     torch.cuda.current_stream(self.q_device).cuda_stream, rope, overlap)
         return out
 
 
