@@ -463,7 +463,9 @@ def config_sweep(reps: int = 5) -> None:
     """The decode kernel alone on every BASELINE config (and the hybrid Qwen3.5 engine's
     full-attention shape): each layer's plan launched once, the
     layers back to back in a CUDA graph (distinct per-layer pools, so every launch reads cold
-    HBM), best and median of ``reps`` replays. One JSON line per config (not the bench line)."""
+    HBM), best and median of ``reps`` replays, once with plain launches and once with layers
+    1.. overlapping their predecessor (programmatic dependent launch, as in a decode step).
+    One JSON line per config (not the bench line)."""
     from model import _native
     from model.triton_decode import paged_decode_plan
     from serve import workloads
@@ -477,28 +479,34 @@ def config_sweep(reps: int = 5) -> None:
         for layer in range(n_layer):
             plan.run(layer, wl.q[layer])
         torch.cuda.synchronize(device)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for layer in range(n_layer):
-                plan.run(layer, wl.q[layer])
-        graph.replay()
-        times = []
-        for _ in range(reps):
-            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            graph.replay()
-            stop.record()
-            torch.cuda.synchronize(device)
-            times.append(start.elapsed_time(stop) * 1e3 / n_layer)
-        if _native.device_error() != 0:
-            raise SystemExit(f"{name}: device error word set")
+        line = {"config": name, "rows": int(wl.q[0].shape[0]), "layers": n_layer}
         kv = wl.kv_bytes_per_layer()
-        best, med = min(times), statistics.median(times)
-        print(json.dumps({"config": name, "rows": int(wl.q[0].shape[0]), "layers": n_layer,
-                          "kv_bytes_per_launch": kv, "us_per_launch_best": round(best, 2),
-                          "us_per_launch_median": round(med, 2), "kv_gbs_best": round(kv / best / 1e3, 1),
-                          "roofline_frac_best": round(kv / best / 1e3 / peak, 4), "peak_gbs": peak}), flush=True)
-        del graph, plan, wl
+        line["kv_bytes_per_launch"] = kv
+        for overlap in (False, True):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for layer in range(n_layer):
+                    plan.run(layer, wl.q[layer], overlap=overlap and layer > 0)
+            graph.replay()
+            times = []
+            for _ in range(reps):
+                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                graph.replay()
+                stop.record()
+                torch.cuda.synchronize(device)
+                times.append(start.elapsed_time(stop) * 1e3 / n_layer)
+            if _native.device_error() != 0:
+                raise SystemExit(f"{name}: device error word set")
+            best, med = min(times), statistics.median(times)
+            tag = "overlapped_" if overlap else ""
+            line.update({f"{tag}us_per_launch_best": round(best, 2), f"{tag}us_per_launch_median": round(med, 2),
+                         f"{tag}kv_gbs_best": round(kv / best / 1e3, 1),
+                         f"{tag}roofline_frac_best": round(kv / best / 1e3 / peak, 4)})
+            del graph
+        line["peak_gbs"] = peak
+        print(json.dumps(line), flush=True)
+        del plan, wl
         torch.cuda.empty_cache()
 
 

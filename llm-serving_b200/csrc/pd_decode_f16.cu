@@ -12,9 +12,9 @@ static const DecodeLaunchFn kTable[6][4] = {PD_ROW(8),  PD_ROW(16),  PD_ROW(32),
                                             PD_ROW(64), PD_ROW(128), PD_ROW(256)};
 #undef PD_ROW
 
+// (8 q heads per item never take the shared-stage kernel: see geometry() in pd_api.cu.)
 #define PD_CTA_ROW(D) \
-  {launch_decode<__half, D, 1, true>, launch_decode<__half, D, 2, true>, launch_decode<__half, D, 4, true>, \
-   launch_decode<__half, D, 8, true>}
+  {launch_decode<__half, D, 1, true>, launch_decode<__half, D, 2, true>, launch_decode<__half, D, 4, true>, nullptr}
 
 static const DecodeLaunchFn kCtaTable[3][4] = {PD_CTA_ROW(64), PD_CTA_ROW(128), PD_CTA_ROW(256)};
 #undef PD_CTA_ROW

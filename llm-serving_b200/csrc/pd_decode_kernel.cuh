@@ -420,6 +420,17 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       const int64_t want = (units + p.min_tiles - 1) / p.min_tiles;
       if (want < workers) workers = int(want < 1 ? 1 : want);
     }
+    // With at most one item per worker, a multiple of the item count makes every item
+    // boundary a range boundary when the rows are equally long: no range then straddles two
+    // items, so items have fewer pieces and every piece is a single segment. Taken when it
+    // idles at most 1/20 of the workers.
+    {
+      const int64_t n_items = int64_t(B) * items_per_row;
+      if (n_items <= workers) {
+        const int aligned = int((workers / n_items) * n_items);
+        if (int64_t(aligned) * 20 >= int64_t(workers) * 19) workers = aligned;
+      }
+    }
     w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
     u0 = w < workers ? int64_t(w) * units / workers : 0;
     u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
@@ -858,7 +869,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     constexpr int GPH = D / 4;                           // groups per head
     constexpr int NG = GROUPS >= 32 ? GROUPS / 32 : 1;   // groups per lane
     constexpr int GB = NG < 8 ? NG : 8;                  // groups per pass
-    constexpr int MB = GB >= 8 ? (GT >= 8 ? 2 : 3) : 16 / GB;  // pieces per batch
+    constexpr int MB = GB >= 8 ? (GT >= 8 ? 2 : 4) : 16 / GB;  // pieces per batch
     auto head_of = [&](int t) -> int {  // head of the lane's group t (static when GPH >= 32)
       return (t * 32) / GPH + (GPH >= 32 ? 0 : lane / GPH);
     };
