@@ -513,7 +513,10 @@ def config_sweep(reps: int = 5) -> None:
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--profile-case", default=None,
-                        help="run a short profiler case (config1..config5) instead of the benchmark")
+                        help="run a short profiler case (config1..config5, qwen35) instead of the benchmark")
+    parser.add_argument("--decode-mode", type=int, default=None, choices=(0, 1, 2),
+                        help="with --profile-case / --configs: pd_set_decode_mode first (0 tensor-core "
+                             "tile math where it applies, 1 shared stages, 2 CUDA-core tile math)")
     parser.add_argument("--configs", action="store_true",
                         help="time the decode kernel alone on every BASELINE config instead of the benchmark")
     parser.add_argument("--gpus", type=int, default=1)
@@ -522,6 +525,11 @@ def main(argv=None) -> int:
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--cpu-sample-layers", type=int, default=2)
     args = parser.parse_args(argv)
+    if args.decode_mode is not None:
+        if not (args.profile_case or args.configs):
+            raise SystemExit("--decode-mode applies to --profile-case and --configs only")
+        from model import _native
+        _native.set_decode_mode(args.decode_mode)
     if args.profile_case:
         profile_case(args.profile_case)
         return 0
