@@ -131,6 +131,28 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
                       int32_t batch, int32_t n_head, int32_t n_kv_head, int32_t head_dim,
                       int32_t dtype, float scale_log2, void* stream);
 
+/* pd_prefill -- chunked-prefill attention reading the paged pool (block-table-aware prefill).
+ *
+ * Row b's new query tokens are q[cu_seqlens_q[b] .. cu_seqlens_q[b+1]) of a packed
+ * (total_q, n_head, head_dim) tensor (token stride q_st, head stride q_sh, unit last stride,
+ * 16-byte aligned rows); their K/V are already in the pool (appended as for decode). Query
+ * token i of a chunk of Sq tokens sits at position seqlen_k[b] - Sq + i and attends causally
+ * to keys 0 .. seqlen_k[b] - Sq + i of the row, token t at block block_table[b, t / bs],
+ * slot t % bs: the causal convention of a varlen flash-attention call with a block table,
+ * bottom-right aligned. softmax(q.k * scale) and P.V in fp32; out (same layout as q, its own
+ * strides) in the pool dtype. A chunk of one token gives pd_decode's result.
+ * max_seqlen_q bounds the chunk lengths (the grid is sized from it).
+ * Supported: bf16 / fp16, head_dim 64 or 128, 1, 2, 4 or 8 q heads per kv head, block_size
+ * >= 8 (PD_ERR_UNSUPPORTED otherwise). No workspace. The reference has no counterpart: its
+ * varlen prefill (flash_attn 2.8.3) never reads the paged cache; this is the
+ * block-table-aware prefill its hot-path notes list as next. */
+int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, const void* v_cache,
+               int64_t n_blocks, int32_t block_size, const int64_t* k_strides, const int64_t* v_strides,
+               const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+               const int32_t* cu_seqlens_q, const int32_t* seqlen_k, void* out, int64_t o_st,
+               int64_t o_sh, int32_t batch, int32_t max_seqlen_q, int32_t n_head, int32_t n_kv_head,
+               int32_t head_dim, int32_t dtype, float scale_log2, void* stream);
+
 /* ---------------------------------------------------------------- decode plan
  *
  * pd_plan_* replaces `PagedDecodePlan` / `paged_decode_plan` (model/triton_decode.py:

@@ -34,6 +34,7 @@ SOURCES = [
     "pd_decode_f32.cu",
     "pd_decode_mma_bf16.cu",
     "pd_decode_mma_f16.cu",
+    "pd_prefill.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

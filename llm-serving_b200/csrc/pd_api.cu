@@ -569,6 +569,62 @@ int pd_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache, co
                        workspace_bytes, stream);
 }
 
+int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, const void* v_cache,
+               int64_t n_blocks, int32_t block_size, const int64_t* k_strides, const int64_t* v_strides,
+               const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
+               const int32_t* cu_seqlens_q, const int32_t* seqlen_k, void* out, int64_t o_st,
+               int64_t o_sh, int32_t batch, int32_t max_seqlen_q, int32_t n_head, int32_t n_kv_head,
+               int32_t head_dim, int32_t dtype, float scale_log2, void* stream) {
+  if (!valid_dtype(dtype) || n_head < 1 || n_kv_head < 1 || n_head % n_kv_head != 0) return PD_ERR_INVALID;
+  if (batch < 0 || max_seqlen_q < 0 || max_blocks < 0 || n_blocks < 1) return PD_ERR_INVALID;
+  if (!pow2(block_size) || !pow2(head_dim)) return PD_ERR_INVALID;
+  const int group = n_head / n_kv_head;
+  if (!prefill_supported(dtype, head_dim, group) || block_size < 8) return PD_ERR_UNSUPPORTED;
+  if (k_strides == nullptr || v_strides == nullptr) return PD_ERR_INVALID;
+  if (max_blocks > 0 && bt_stride < max_blocks) return PD_ERR_INVALID;
+  const int64_t capacity = int64_t(max_blocks) * block_size;
+  if (capacity > (int64_t(1) << 30)) return PD_ERR_INVALID;
+  if (batch == 0 || max_seqlen_q == 0) return PD_OK;
+  if (cu_seqlens_q == nullptr || seqlen_k == nullptr || (block_table == nullptr && max_blocks > 0))
+    return PD_ERR_INVALID;
+  if (check_rows(q, q_st, q_sh, dtype) != PD_OK || check_rows(out, o_st, o_sh, dtype) != PD_OK)
+    return PD_ERR_INVALID;
+  int dev = 0;
+  if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
+  unsigned* err = error_word(dev);
+  if (err == nullptr) return PD_ERR_CUDA;
+  const int box_tokens = block_size < 64 ? block_size : 64;
+  CUtensorMap kmap, vmap;
+  int st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype, box_tokens,
+                       1, true);
+  if (st != PD_OK) return st;
+  st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype, box_tokens, 1,
+                   true);
+  if (st != PD_OK) return st;
+  PrefillParams p{};
+  p.q = q;
+  p.q_st = q_st;
+  p.q_sh = q_sh;
+  p.out = out;
+  p.o_st = o_st;
+  p.o_sh = o_sh;
+  p.cu_q = cu_seqlens_q;
+  p.seqlen_k = seqlen_k;
+  p.table = block_table;
+  p.bt_stride = bt_stride;
+  p.max_blocks = max_blocks;
+  p.capacity = int32_t(capacity);
+  p.block_size = block_size;
+  p.box_tokens = box_tokens;
+  p.scale_log2 = scale_log2;
+  p.err = err;
+  const cudaError_t e = launch_prefill(p, kmap, vmap, dtype, head_dim, group, max_seqlen_q, batch, n_kv_head,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return PD_OK;
+}
+
 int pd_decode_partials(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache,
                        const void* v_cache, int64_t n_blocks, int32_t block_size,
                        const int64_t* k_strides, const int64_t* v_strides,

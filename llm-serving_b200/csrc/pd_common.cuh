@@ -437,6 +437,24 @@ struct AppendParams {
   int32_t rope_dim;
 };
 
+// Chunked prefill over the paged pool (pd_prefill.cu). Element strides.
+struct PrefillParams {
+  const void* q;        // (total_q, H, D)
+  int64_t q_st, q_sh;
+  void* out;            // (total_q, H, D)
+  int64_t o_st, o_sh;
+  const int32_t* cu_q;      // (B + 1) query-token offsets
+  const int32_t* seqlen_k;  // (B) keys per row, the chunk included
+  const int32_t* table;
+  int64_t bt_stride;
+  int32_t max_blocks;
+  int32_t capacity;     // max_blocks * block_size
+  int32_t block_size;
+  int32_t box_tokens;   // min(block_size, 64)
+  float scale_log2;
+  unsigned* err;
+};
+
 struct MergeParams {
   const float* m;
   const float* l;

@@ -50,6 +50,12 @@ _SIGNATURES = {
          _c_i32, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_float,
          _c_ptr, _c_size, _c_ptr],
     ),
+    "pd_prefill": (
+        ctypes.c_int,
+        [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_ptr, _c_i64,
+         _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+         _c_i32, _c_float, _c_ptr],
+    ),
     "pd_decode_noalloc": (
         ctypes.c_int,
         [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_ptr, _c_i64,
@@ -226,6 +232,24 @@ def decode(q, k_cache, v_cache, block_table, seqlen, out, scale_log2, workspace)
         workspace.data_ptr(), workspace.numel(), stream_handle(q.device),
     )
     check(status, "pd_decode")
+
+
+def prefill(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlen_k, max_seqlen_q, out, n_head,
+            scale_log2) -> None:
+    """One pd_prefill launch on the current stream. Tensors are already validated: q/out are
+    packed (total_q, H, D); cu_seqlens_q (B + 1) and seqlen_k (B) int32."""
+    _, bs, hkv, D = k_cache.shape
+    B = seqlen_k.shape[0]
+    status = require().pd_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0], bs,
+        strides3(k_cache), strides3(v_cache),
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        cu_seqlens_q.data_ptr(), seqlen_k.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1),
+        B, int(max_seqlen_q), int(n_head), hkv, D, dtype_code(q.dtype), float(scale_log2),
+        stream_handle(q.device),
+    )
+    check(status, "pd_prefill")
 
 
 def decode_noalloc(q, k_cache, v_cache, block_table, seqlen, out, scale_log2) -> None:

@@ -193,6 +193,49 @@ def _workspace(q: torch.Tensor, n_kv_head: int) -> torch.Tensor:
     return ws
 
 
+def paged_prefill(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlen_k, max_seqlen_q: int, *,
+                  scale: float | None = None):
+    """Chunked-prefill attention reading the paged pool (one kernel launch).
+
+    ``q`` is the packed ``(total_q, H, D)`` query of every row's new tokens, row ``b`` owning
+    ``q[cu_seqlens_q[b]:cu_seqlens_q[b + 1]]``; the chunk's K/V are already in the pools (written
+    with ``PagedPool.write_slots`` / ``PagedKV``). Query token ``i`` of a chunk of ``Sq`` tokens sits
+    at position ``seqlen_k[b] - Sq + i`` and attends causally to keys ``0 .. seqlen_k[b] - Sq + i``
+    of its row (the bottom-right causal convention of varlen flash attention with a block
+    table). ``max_seqlen_q`` bounds the chunk lengths. Returns ``out`` shaped like ``q``.
+
+    bf16 / fp16 pools, head_dim 64 or 128, 1/2/4/8 q heads per kv head, block_size >= 8. The
+    reference's prefill never reads the paged cache; this is the block-table-aware prefill its
+    hot-path notes list as next work, with no reference counterpart to mirror.
+    """
+    _require_backend()
+    _require_cuda_tensors((("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("block_table", block_table),
+                           ("cu_seqlens_q", cu_seqlens_q), ("seqlen_k", seqlen_k)))
+    if q.dim() != 3 or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        raise ValueError("paged_prefill needs q (total_q, H, D) and k_cache/v_cache (n_blocks, bs, H_kv, D)")
+    if q.dtype != k_cache.dtype or v_cache.dtype != k_cache.dtype:
+        raise TypeError(f"dtype mismatch: q {q.dtype}, k_cache {k_cache.dtype}, v_cache {v_cache.dtype}")
+    if q.shape[2] != k_cache.shape[3] or q.shape[1] % k_cache.shape[2] != 0:
+        raise ValueError(f"q {tuple(q.shape)} does not match the pool {tuple(k_cache.shape)}")
+    B = seqlen_k.shape[0]
+    if cu_seqlens_q.shape != (B + 1,) or block_table.dim() != 2 or block_table.shape[0] != B:
+        raise ValueError("paged_prefill needs cu_seqlens_q (B + 1,), seqlen_k (B,) and block_table (B, max_blocks)")
+    q = q.contiguous()
+    out = torch.empty_like(q)
+    if B == 0 or q.shape[0] == 0 or max_seqlen_q <= 0:
+        return out
+    cu32 = cu_seqlens_q.contiguous().to(torch.int32)
+    sk32 = seqlen_k.contiguous().to(torch.int32)
+    if block_table.dtype != torch.int32 or block_table.stride(1) != 1:
+        block_table = block_table.contiguous().to(torch.int32)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[2])
+    with torch.cuda.device(q.device):
+        _native.prefill(q, _kernel_pool(k_cache), _kernel_pool(v_cache), block_table, cu32, sk32,
+                        int(max_seqlen_q), out, q.shape[1], float(scale) * _LOG2E)
+    return out
+
+
 def paged_decode(q, k_cache, v_cache, block_table, seqlen, *, scale: float | None = None):
     """Decode one query token per row against a paged KV pool (one kernel launch)."""
     _require_backend()

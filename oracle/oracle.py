@@ -264,3 +264,43 @@ def dense_decode_py(q, k, v, table, seqlen, scale: float | None = None):
             probs = torch.softmax(scores, dim=-1)
             out[row, head] = probs @ vals[:, hk, :]
     return out
+
+
+def paged_prefill(q, k, v, table, cu_seqlens_q, seqlen_k, *, scale: float | None = None):
+    """Chunked-prefill attention over the paged pool, float64 on the CPU: returns
+    ``(out_f32, out)`` (fp32 and q dtype), ``q``/``out`` packed ``(total_q, H, D)``.
+
+    Row ``b``'s query tokens ``q[cu[b]:cu[b+1]]`` (``Sq`` of them) sit at positions
+    ``seqlen_k[b] - Sq + i`` and attend causally (bottom-right aligned, the varlen causal
+    convention of the reference's prefill kernel, flash_attn 2.8.3 ``flash_attn_varlen_func``
+    with ``causal=True``, model/varlen.py:20) to the row's keys, gathered token by token
+    through the block table as :func:`dense_decode_py` does (tests/reference/paged.py:225-274
+    for one query token). A query with no visible key gives zeros.
+    """
+    q, k, v = _cpu(q), _cpu(k), _cpu(v)
+    table, cu, sk = _cpu(table), _cpu(cu_seqlens_q), _cpu(seqlen_k)
+    T, H, D = q.shape
+    bs, hkv = k.shape[1], k.shape[2]
+    group = H // hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    out = torch.zeros(T, H, D, dtype=torch.float64)
+    for row in range(sk.shape[0]):
+        q0, q1, n = int(cu[row]), int(cu[row + 1]), int(sk[row])
+        sq = q1 - q0
+        if sq <= 0 or n <= 0:
+            continue
+        idx = torch.tensor([int(table[row, t // bs]) for t in range(n)])
+        off = torch.arange(n) % bs
+        keys = k[idx, off].double()  # (n, hkv, D)
+        vals = v[idx, off].double()
+        pos = torch.arange(sq) + (n - sq)            # absolute query positions
+        visible = torch.arange(n)[None, :] <= pos[:, None]  # (sq, n)
+        for head in range(H):
+            hk = head // group
+            scores = (q[q0:q1, head].double() @ keys[:, hk, :].T) * scale
+            scores = scores.masked_fill(~visible, float("-inf"))
+            probs = torch.softmax(scores, dim=-1)
+            probs = torch.nan_to_num(probs, nan=0.0)  # rows with no visible key
+            out[q0:q1, head] = probs @ vals[:, hk, :]
+    return out.float(), out.to(q.dtype)
