@@ -58,8 +58,9 @@ def _peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data.get("bf16_tflops", 1590.0)),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", 1400.0)), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -443,6 +444,26 @@ def profile_case(name: str, launches: int = 4) -> None:
     from serve import workloads
 
     device = torch.device("cuda", 0)
+    if name == "prefill":  # chunked prefill: 4 rows x (2048 cached + 512 new tokens), one layer
+        from model.triton_decode import paged_prefill
+
+        gen = torch.Generator(device=device).manual_seed(11)
+        rows, ctx, chunk = 4, 2048, 512
+        pages = -(-(ctx + chunk) // BS)
+        k = torch.randn(rows * pages + 1, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+        v = torch.randn(rows * pages + 1, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+        table = torch.randperm(rows * pages + 1, generator=gen, device=device)[: rows * pages]
+        table = table.view(rows, pages).to(torch.int32)
+        q = torch.randn(rows * chunk, H, D, generator=gen, device=device, dtype=torch.bfloat16)
+        cu = torch.arange(rows + 1, device=device, dtype=torch.int32) * chunk
+        sk = torch.full((rows,), ctx + chunk, device=device, dtype=torch.int32)
+        for _ in range(launches):
+            paged_prefill(q, k, v, table, cu, sk, chunk)
+        torch.cuda.synchronize()
+        if _native.device_error() != 0:
+            raise SystemExit("device error word set")
+        print(json.dumps({"profile_case": name, "launches": launches, "rows": rows, "context": ctx, "chunk": chunk}))
+        return
     wl = getattr(workloads, name)(device, n_layer=1)
     plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
     B = wl.q[0].shape[0]
@@ -510,15 +531,80 @@ def config_sweep(reps: int = 5) -> None:
         torch.cuda.empty_cache()
 
 
+def prefill_sweep(reps: int = 5) -> None:
+    """Chunked prefill over the paged pool (``paged_prefill``) at Qwen3-0.6B head shapes: each
+    layer's launch once per replay of a CUDA graph, distinct per-layer pools (larger than L2),
+    best of ``reps`` replays. FLOPs are the causal ones: 4 * D per visible (query, key) pair per
+    q head. One JSON line per case (not the bench line)."""
+    from model import _native
+    from model.triton_decode import paged_prefill
+
+    device = torch.device("cuda", 0)
+    peaks = _peaks()
+    gen = torch.Generator(device=device).manual_seed(11)
+    for name, rows, ctx, chunk, n_layer in (("chunk512_ctx2048", 4, 2048, 512, 28),
+                                            ("chunk2048_ctx0", 4, 0, 2048, 28),
+                                            ("chunk128_ctx4096", 16, 4096, 128, 8)):
+        total = ctx + chunk
+        pages = -(-total // BS)
+        n_blocks = rows * pages + 1
+        pools_k = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+                   for _ in range(n_layer)]
+        pools_v = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+                   for _ in range(n_layer)]
+        perm = torch.randperm(n_blocks, generator=gen, device=device)[: rows * pages]
+        table = perm.view(rows, pages).to(torch.int32)
+        q = [torch.randn(rows * chunk, H, D, generator=gen, device=device, dtype=torch.bfloat16)
+             for _ in range(n_layer)]
+        cu = torch.arange(rows + 1, device=device, dtype=torch.int32) * chunk
+        sk = torch.full((rows,), total, device=device, dtype=torch.int32)
+        outs = [paged_prefill(q[i], pools_k[i], pools_v[i], table, cu, sk, chunk) for i in range(n_layer)]
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = [paged_prefill(q[i], pools_k[i], pools_v[i], table, cu, sk, chunk) for i in range(n_layer)]
+        graph.replay()
+        times = []
+        for _ in range(reps):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            graph.replay()
+            stop.record()
+            torch.cuda.synchronize(device)
+            times.append(start.elapsed_time(stop) * 1e3 / n_layer)
+        if _native.device_error() != 0:
+            raise SystemExit(f"{name}: device error word set")
+        best = min(times)
+        pairs = rows * (chunk * ctx + chunk * (chunk + 1) // 2)  # visible (query, key) pairs
+        flops = 4.0 * D * H * pairs
+        kv_bytes = rows * total * H_KV * D * 2 * 2
+        tflops = flops / (best * 1e-6) / 1e12
+        print(json.dumps({
+            "prefill_case": name, "rows": rows, "context": ctx, "chunk": chunk, "layers": n_layer,
+            "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
+            "us_per_launch_best": round(best, 2), "us_per_launch_median": round(statistics.median(times), 2),
+            "causal_tflops": round(tflops, 1),
+            "tensor_roofline_frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
+            "tensor_peak_tflops": peaks["bf16_tflops_sustained"], "kv_gbs": round(kv_bytes / best / 1e3, 1),
+            "hbm_roofline_frac": round(kv_bytes / best / 1e3 / peaks["hbm_gbs"], 4),
+            "peak_source": peaks["source"],
+            "note": "mma.sync tile math with P as hi+lo operands (3 tensor products per pair where "
+                    "a single-precision-P kernel needs 2)"}), flush=True)
+        del graph, outs, pools_k, pools_v, q
+        torch.cuda.empty_cache()
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--profile-case", default=None,
-                        help="run a short profiler case (config1..config5, qwen35) instead of the benchmark")
+                        help="run a short profiler case (config1..config5, qwen35, prefill) instead of the benchmark")
     parser.add_argument("--decode-mode", type=int, default=None, choices=(0, 1, 2),
                         help="with --profile-case / --configs: pd_set_decode_mode first (0 tensor-core "
                              "tile math where it applies, 1 shared stages, 2 CUDA-core tile math)")
     parser.add_argument("--configs", action="store_true",
                         help="time the decode kernel alone on every BASELINE config instead of the benchmark")
+    parser.add_argument("--prefill", action="store_true",
+                        help="time the chunked-prefill kernel (paged_prefill) instead of the benchmark")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=100)
     parser.add_argument("--warmup", type=int, default=5)
@@ -535,6 +621,9 @@ def main(argv=None) -> int:
         return 0
     if args.configs:
         config_sweep()
+        return 0
+    if args.prefill:
+        prefill_sweep()
         return 0
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
