@@ -532,7 +532,8 @@ def config_sweep(reps: int = 5) -> None:
 
 
 def prefill_sweep(reps: int = 5) -> None:
-    """Chunked prefill over the paged pool (``paged_prefill``) at Qwen3-0.6B head shapes: each
+    """Chunked prefill over the paged pool (``paged_prefill``) at Qwen3-0.6B head shapes (and
+    the Qwen3.5 full-attention heads, 8q/2kv, head_dim 256): each
     layer's launch once per replay of a CUDA graph, distinct per-layer pools (larger than L2),
     best of ``reps`` replays. FLOPs are the causal ones: 4 * D per visible (query, key) pair per
     q head. One JSON line per case (not the bench line)."""
@@ -542,9 +543,11 @@ def prefill_sweep(reps: int = 5) -> None:
     device = torch.device("cuda", 0)
     peaks = _peaks()
     gen = torch.Generator(device=device).manual_seed(11)
-    for name, rows, ctx, chunk, n_layer in (("chunk512_ctx2048", 4, 2048, 512, 28),
-                                            ("chunk2048_ctx0", 4, 0, 2048, 28),
-                                            ("chunk128_ctx4096", 16, 4096, 128, 8)):
+    for name, rows, ctx, chunk, n_layer, (H, H_KV, D) in (
+            ("chunk512_ctx2048", 4, 2048, 512, 28, (16, 8, 128)),
+            ("chunk2048_ctx0", 4, 0, 2048, 28, (16, 8, 128)),
+            ("chunk128_ctx4096", 16, 4096, 128, 8, (16, 8, 128)),
+            ("qwen35_chunk512_ctx2048", 4, 2048, 512, 6, (8, 2, 256))):
         total = ctx + chunk
         pages = -(-total // BS)
         n_blocks = rows * pages + 1

@@ -142,7 +142,7 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * bottom-right aligned. softmax(q.k * scale) and P.V in fp32; out (same layout as q, its own
  * strides) in the pool dtype. A chunk of one token gives pd_decode's result.
  * max_seqlen_q bounds the chunk lengths (the grid is sized from it).
- * Supported: bf16 / fp16, head_dim 64 or 128, 1, 2, 4 or 8 q heads per kv head, block_size
+ * Supported: bf16 / fp16, head_dim 64, 128 or 256, 1, 2, 4 or 8 q heads per kv head, block_size
  * >= 8 (PD_ERR_UNSUPPORTED otherwise). No workspace. The reference has no counterpart: its
  * varlen prefill (flash_attn 2.8.3) never reads the paged cache; this is the
  * block-table-aware prefill its hot-path notes list as next. */

@@ -593,7 +593,8 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
   if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
   unsigned* err = error_word(dev);
   if (err == nullptr) return PD_ERR_CUDA;
-  const int box_tokens = block_size < 64 ? block_size : 64;
+  const int tile_tokens = prefill_tile_tokens(head_dim);
+  const int box_tokens = block_size < tile_tokens ? block_size : tile_tokens;
   CUtensorMap kmap, vmap;
   int st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype, box_tokens,
                        1, true);

@@ -20,8 +20,9 @@ DecodeLaunchFn decode_launcher_mma_bf16(int d_index, int gt_index);
 cudaError_t launch_append(const AppendParams& p, int src_dtype, int dst_dtype, bool vec16,
                           cudaStream_t stream);
 
-// Chunked prefill attention over the paged pool (bf16/fp16, head_dim 64/128, group 1/2/4/8).
+// Chunked prefill attention over the paged pool (bf16/fp16, head_dim 64/128/256, group 1/2/4/8).
 bool prefill_supported(int dtype, int head_dim, int group);
+int prefill_tile_tokens(int head_dim);  // key tokens per tile (TMA boxes are at most this long)
 size_t prefill_smem_bytes(int head_dim);
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype,
                            int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,

@@ -1,5 +1,5 @@
 // pd_prefill.cu -- block-table-aware chunked-prefill attention for sm_100a (bf16 / fp16 pools,
-// head_dim 64 or 128, 1, 2, 4 or 8 q heads per kv head).
+// head_dim 64, 128 or 256, 1, 2, 4 or 8 q heads per kv head).
 //
 // What it computes: for every row b, its new query tokens q[cu_q[b] .. cu_q[b+1]) (the chunk,
 // Sq = cu_q[b+1] - cu_q[b] tokens) attend causally to the row's Lk = seqlen_k[b] tokens in the
@@ -11,7 +11,7 @@
 //
 // How (B200): one CTA of 4 warps per (64 query rows, kv head, row); rows are (token, q head)
 // pairs of one kv head's group, token-major, so the group's q heads share every K/V tile.
-//  * K/V tiles of 64 tokens stream through 2 shared-memory stages by TMA from the pool's
+//  * K/V tiles of 64 tokens (32 at head_dim 256) stream through 2 shared-memory stages by TMA from the pool's
 //    128-byte-swizzled 5-D map (one box per block part), completing on mbarriers; thread 0
 //    refills a stage once every warp has consumed it.
 //  * Each warp owns 16 rows: S = Q K^T (m16n8k16, Q fragments held in registers from a
@@ -32,16 +32,21 @@ namespace pd {
 namespace {
 
 constexpr int PF_ROWS = 64;    // query rows per CTA
-constexpr int PF_KT = 64;      // tokens per K/V tile
 constexpr int PF_WARPS = 4;
 
 template <typename T, int D, int G>
 struct PrefillCfg {
-  static_assert(D == 64 || D == 128, "prefill: head_dim 64 or 128");
+  static_assert(D == 64 || D == 128 || D == 256, "prefill: head_dim 64, 128 or 256");
+  static constexpr int KT = D == 256 ? 32 : 64;   // tokens per K/V tile (two CTAs per SM fit)
+  static constexpr int NT = KT / 8;               // 8-token n-tiles of S
+  static constexpr int KK = KT / 16;              // 16-token k-steps of P.V
+  // Q fragments stay in registers up to head_dim 128; at 256 the O accumulators need the
+  // room, and each k-step's fragment is re-read from the shared Q tile per key tile.
+  static constexpr bool HOLD_Q = D <= 128;
   static constexpr int ROW_BYTES = D * 2;
   static constexpr int KS = D / 16;               // q.K k-steps
   static constexpr int DN = D / 8;                // 8-wide head_dim tiles of O
-  static constexpr int TILE_BYTES = PF_KT * ROW_BYTES;  // K (or V) bytes of one tile
+  static constexpr int TILE_BYTES = KT * ROW_BYTES;  // K (or V) bytes of one tile
   static constexpr int Q_BYTES = PF_ROWS * ROW_BYTES;
   static constexpr int TQ = PF_ROWS / G;          // query tokens per CTA
 };
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
   int kend = ctx + tok0 + ntok;
   if (kend > lk) kend = lk;
   if (kend < 0) kend = 0;
-  const int ntiles = (kend + PF_KT - 1) / PF_KT;
+  const int ntiles = (kend + C::KT - 1) / C::KT;
 
   // shared memory: [2 full barriers | pad | Q tile | 2 stages of (K tile, V tile)], 1 KB aligned
   const uint32_t base = smem_addr(smem_raw);
@@ -100,8 +105,8 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
   const int bt = p.box_tokens;  // tokens per TMA box (min(bs, 64))
   const int npages = (lk + bs - 1) / bs;
   auto issue = [&](int kt, int st) {  // thread 0 only
-    const int t0 = kt * PF_KT;
-    const int covered = kend - t0 < PF_KT ? kend - t0 : PF_KT;  // >= 1
+    const int t0 = kt * C::KT;
+    const int covered = kend - t0 < C::KT ? kend - t0 : C::KT;  // >= 1
     const int boxes = (covered + bt - 1) / bt;
     const uint32_t bar = smem_addr(bars + st);
     const uint32_t kdst = st_addr + uint32_t(st) * 2u * C::TILE_BYTES;
@@ -134,11 +139,12 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
     *reinterpret_cast<uint4*>(qs + swz(r, u, PF_ROWS)) = v;
   }
   __syncthreads();
-  uint32_t qa[C::KS][4];
-  {
-    const int r = warp * 16 + (lane & 15);
+  const uint32_t qrow_addr = qs_addr;  // lane's A-fragment row: warp * 16 + (lane & 15)
+  const int qr = warp * 16 + (lane & 15);
+  uint32_t qa[C::HOLD_Q ? C::KS : 1][4];
+  if constexpr (C::HOLD_Q) {
 #pragma unroll
-    for (int ks = 0; ks < C::KS; ++ks) ldsm_x4(qs_addr + swz(r, 2 * ks + (lane >> 4), PF_ROWS), qa[ks]);
+    for (int ks = 0; ks < C::KS; ++ks) ldsm_x4(qrow_addr + swz(qr, 2 * ks + (lane >> 4), PF_ROWS), qa[ks]);
   }
 
   // this thread's rows (g and g + 8 of the warp) and their last visible key
@@ -168,13 +174,13 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
       }
       return;
     }
-    const int t0 = kt * PF_KT;
+    const int t0 = kt * C::KT;
     const uint32_t kaddr = st_addr + uint32_t(st) * 2u * C::TILE_BYTES;
     const uint32_t vaddr = kaddr + C::TILE_BYTES;
-    const int valid = kend - t0 < PF_KT ? kend - t0 : PF_KT;
-    if (valid < PF_KT) {  // zero V rows past the row end (stale or pool bytes)
+    const int valid = kend - t0 < C::KT ? kend - t0 : C::KT;
+    if (valid < C::KT) {  // zero V rows past the row end (stale or pool bytes)
       unsigned char* vs = stages + size_t(st) * 2 * C::TILE_BYTES + C::TILE_BYTES;
-      for (int i = tid; i < (PF_KT - valid) * (D / 8); i += blockDim.x) {
+      for (int i = tid; i < (C::KT - valid) * (D / 8); i += blockDim.x) {
         const int t = valid + i / (D / 8), u = i % (D / 8);
         const int box = t / bt, tb = t - box * bt;
         *reinterpret_cast<uint4*>(vs + box * bt * C::ROW_BYTES + swz(tb, u, bt)) = make_uint4(0u, 0u, 0u, 0u);
@@ -184,26 +190,44 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
     // token t of the tile: box t / bt, row t % bt of that box
     auto krow = [&](int t) -> uint32_t { return uint32_t((t / bt) * bt * C::ROW_BYTES); };
 
-    // ---- S = Q K^T over 8 n-tiles of 8 tokens
-    float s[8][4];
+    // ---- S = Q K^T over the tile's 8-token n-tiles
+    float s[C::NT][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const int t = nt * 8 + (lane & 7);
-      const uint32_t rb = kaddr + krow(t);
-      const int tb = t % bt;
+    for (int nt = 0; nt < C::NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    if constexpr (C::HOLD_Q) {
+#pragma unroll
+      for (int nt = 0; nt < C::NT; ++nt) {
+        const int t = nt * 8 + (lane & 7);
+        const uint32_t rb = kaddr + krow(t);
+        const int tb = t % bt;
+#pragma unroll
+        for (int ks = 0; ks < C::KS; ks += 2) {
+          uint32_t kb[4];
+          ldsm_x4(rb + swz(tb, 2 * ks + (lane >> 3), bt), kb);
+          X::m16n8k16(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[0], kb[1]);
+          X::m16n8k16(s[nt], qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], kb[2], kb[3]);
+        }
+      }
+    } else {
 #pragma unroll
       for (int ks = 0; ks < C::KS; ks += 2) {
-        uint32_t kb[4];
-        ldsm_x4(rb + swz(tb, 2 * ks + (lane >> 3), bt), kb);
-        X::m16n8k16(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[0], kb[1]);
-        X::m16n8k16(s[nt], qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], kb[2], kb[3]);
+        uint32_t q0[4], q1[4];
+        ldsm_x4(qrow_addr + swz(qr, 2 * ks + (lane >> 4), PF_ROWS), q0);
+        ldsm_x4(qrow_addr + swz(qr, 2 * ks + 2 + (lane >> 4), PF_ROWS), q1);
+#pragma unroll
+        for (int nt = 0; nt < C::NT; ++nt) {
+          const int t = nt * 8 + (lane & 7);
+          uint32_t kb[4];
+          ldsm_x4(kaddr + krow(t) + swz(t % bt, 2 * ks + (lane >> 3), bt), kb);
+          X::m16n8k16(s[nt], q0[0], q0[1], q0[2], q0[3], kb[0], kb[1]);
+          X::m16n8k16(s[nt], q1[0], q1[1], q1[2], q1[3], kb[2], kb[3]);
+        }
       }
     }
     // ---- mask, online softmax (rows g and g + 8 of the warp)
     float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < C::NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int hr = e >> 1;
@@ -232,7 +256,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
       o[dn][3] *= alpha[1];
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < C::NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         s[nt][e] = exp2f(s[nt][e] - m_use[e >> 1]);
@@ -241,7 +265,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
     }
     // ---- O += P V: A = P from the S accumulators (hi + lo), B = V^T fragments by ldmatrix.trans
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < C::KK; ++kk) {
       uint32_t ah[4], al[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -326,11 +350,14 @@ cudaError_t launch_prefill_g(const PrefillParams& p, const CUtensorMap& kmap, co
 size_t prefill_smem_bytes(int head_dim) {
   // barriers (1 KB with the alignment slack), the Q tile, 2 stages of K + V tiles, and 1 KB
   // of run-time re-alignment slack
-  return 1024 + size_t(PF_ROWS) * head_dim * 2 + 2 * 2 * size_t(PF_KT) * head_dim * 2 + 1024;
+  return 1024 + size_t(PF_ROWS) * head_dim * 2 + 2 * 2 * size_t(prefill_tile_tokens(head_dim)) * head_dim * 2 +
+         1024;
 }
 
+int prefill_tile_tokens(int head_dim) { return head_dim == 256 ? 32 : 64; }
+
 bool prefill_supported(int dtype, int head_dim, int group) {
-  return (dtype == PD_BF16 || dtype == PD_F16) && (head_dim == 64 || head_dim == 128) &&
+  return (dtype == PD_BF16 || dtype == PD_F16) && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
          (group == 1 || group == 2 || group == 4 || group == 8);
 }
 
@@ -340,10 +367,14 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& kmap, cons
   if (dtype == PD_BF16) {
     if (head_dim == 64)
       return launch_prefill_g<__nv_bfloat16, 64>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+    if (head_dim == 256)
+      return launch_prefill_g<__nv_bfloat16, 256>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
     return launch_prefill_g<__nv_bfloat16, 128>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
   }
   if (head_dim == 64)
     return launch_prefill_g<__half, 64>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+  if (head_dim == 256)
+    return launch_prefill_g<__half, 256>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
   return launch_prefill_g<__half, 128>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
 }
 

@@ -204,7 +204,7 @@ def paged_prefill(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlen_k, max_
     of its row (the bottom-right causal convention of varlen flash attention with a block
     table). ``max_seqlen_q`` bounds the chunk lengths. Returns ``out`` shaped like ``q``.
 
-    bf16 / fp16 pools, head_dim 64 or 128, 1/2/4/8 q heads per kv head, block_size >= 8. The
+    bf16 / fp16 pools, head_dim 64, 128 or 256, 1/2/4/8 q heads per kv head, block_size >= 8. The
     reference's prefill never reads the paged cache; this is the block-table-aware prefill its
     hot-path notes list as next work, with no reference counterpart to mirror.
     """

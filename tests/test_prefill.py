@@ -3,7 +3,8 @@
 CPU tests pin the oracle (a one-token chunk is the paged decode; a long chunk equals the
 same rows processed as separate shorter chunks) and the entry point's refusals. GPU tests
 compare the sm_100a kernel with the oracle on the same seeded inputs: several group sizes,
-head dims, block sizes (one and several TMA boxes per key tile), ragged chunks and contexts,
+head dims (64, 128, 256), block sizes (one and several TMA boxes per key tile, and key
+tiles within a block), ragged chunks and contexts,
 empty rows, and pools whose unused slots hold NaN. Tolerance: the decode suite's (fp32-exact
 reference, output rounded to the pool dtype).
 """
@@ -75,7 +76,7 @@ def test_entry_point_refuses_unsupported_shapes_without_touching_memory():
 
     lib = _native.require()
     strides = (ctypes.c_int64 * 3)(16 * 8 * 256, 8 * 256, 256)
-    args = dict(batch=1, max_q=4, n_head=8, n_kv=8, head_dim=256, dtype=2)
+    args = dict(batch=1, max_q=4, n_head=8, n_kv=8, head_dim=512, dtype=2)
 
     def call(**kw):
         a = {**args, **kw}
@@ -83,7 +84,7 @@ def test_entry_point_refuses_unsupported_shapes_without_touching_memory():
                               None, 0, 0, a["batch"], a["max_q"], a["n_head"], a["n_kv"], a["head_dim"],
                               a["dtype"], 1.0, None)
 
-    assert call() == 2                      # head_dim 256: PD_ERR_UNSUPPORTED
+    assert call() == 2                      # head_dim 512: PD_ERR_UNSUPPORTED
     assert call(head_dim=128, dtype=0) == 2  # fp32 pools
     assert call(head_dim=128, n_head=24, n_kv=2) == 2  # 12 q heads per kv head
     assert call(head_dim=128, n_head=12, n_kv=8) == 1  # heads not a multiple: PD_ERR_INVALID
@@ -100,6 +101,8 @@ CASES = [
     pytest.param(16, 2, 128, 8, [17, 0], [40, 8], id="g8-d128-bs8"),
     pytest.param(16, 8, 64, 128, [2000, 3], [300, 3], id="qwen3-d64-bs128"),
     pytest.param(8, 8, 128, 16, [0, 9], [0, 20], id="empty-row"),
+    pytest.param(8, 2, 256, 16, [0, 700, 33], [96, 40, 1], id="qwen35-d256-g4"),
+    pytest.param(16, 2, 256, 64, [100, 0], [70, 33], id="d256-g8-bs64"),
 ]
 
 
