@@ -164,3 +164,41 @@ def test_long_chunk_over_a_long_context(cuda_device):
     assert_output_close(got, ref_f32, torch.bfloat16)
     assert _native.device_error() == 0
     assert math.isfinite(got.float().abs().max().item())
+
+
+@pytest.mark.gpu
+def test_chunked_prefill_through_the_engine_pool(cuda_device):
+    """The engine's flow: a request's prompt K/V go into the pool with
+    ``PagedPool.write_prefill`` chunk by chunk, and each chunk's queries attend over the pool
+    with ``paged_prefill`` (earlier chunks included)."""
+    from model import _native
+    from model.paged import PagedPool
+    from model.triton_decode import paged_prefill
+
+    gen = torch.Generator().manual_seed(8)
+    H, Hkv, D, bs = 16, 8, 128, 16
+    pool = PagedPool(1, 64, bs, Hkv, D, dtype=torch.bfloat16, device=cuda_device, n_head=H)
+    tables = [list(range(0, 64, 2)), list(range(1, 31, 2))]  # 32 and 15 interleaved, disjoint blocks
+    table = torch.zeros(2, 32, dtype=torch.int32)
+    for row, t in enumerate(tables):
+        table[row, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    done = [0, 0]
+    for chunks in ([300, 150], [200, 90]):
+        qs = []
+        for row, n in enumerate(chunks):
+            k = torch.randn(n, Hkv, D, generator=gen).to(torch.bfloat16).to(cuda_device)
+            v = torch.randn(n, Hkv, D, generator=gen).to(torch.bfloat16).to(cuda_device)
+            pool.write_prefill(0, tables[row], done[row], k, v)
+            qs.append(torch.randn(n, H, D, generator=gen).to(torch.bfloat16))
+        for row, n in enumerate(chunks):
+            done[row] += n
+        q = torch.cat(qs)
+        cu = torch.tensor([0, chunks[0], chunks[0] + chunks[1]], dtype=torch.int32)
+        sk = torch.tensor(done, dtype=torch.int32)
+        kp, vp = pool.keys[0], pool.values[0]
+        got = paged_prefill(q.to(cuda_device), kp, vp, table.to(cuda_device), cu.to(cuda_device),
+                            sk.to(cuda_device), max(chunks))
+        torch.cuda.synchronize()
+        ref_f32, _ = oracle.paged_prefill(q, kp.cpu(), vp.cpu(), table, cu, sk)
+        assert_output_close(got, ref_f32, torch.bfloat16)
+    assert _native.device_error() == 0
