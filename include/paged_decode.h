@@ -141,7 +141,8 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * slot t % bs: the causal convention of a varlen flash-attention call with a block table,
  * bottom-right aligned. softmax(q.k * scale) and P.V in fp32; out (same layout as q, its own
  * strides) in the pool dtype. A chunk of one token gives pd_decode's result.
- * max_seqlen_q bounds the chunk lengths (the grid is sized from it).
+ * max_seqlen_q must be at least the longest chunk (the grid is sized from it; the kernel does
+ * not read cu_seqlens_q on the host): query tokens of a longer chunk past it are not written.
  * Supported: bf16 / fp16, head_dim 64, 128 or 256, 1, 2, 4 or 8 q heads per kv head, block_size
  * >= 8 (PD_ERR_UNSUPPORTED otherwise). No workspace. The reference has no counterpart: its
  * varlen prefill (flash_attn 2.8.3) never reads the paged cache; this is the

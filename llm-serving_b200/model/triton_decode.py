@@ -202,7 +202,9 @@ def paged_prefill(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlen_k, max_
     with ``PagedPool.write_slots`` / ``PagedKV``). Query token ``i`` of a chunk of ``Sq`` tokens sits
     at position ``seqlen_k[b] - Sq + i`` and attends causally to keys ``0 .. seqlen_k[b] - Sq + i``
     of its row (the bottom-right causal convention of varlen flash attention with a block
-    table). ``max_seqlen_q`` bounds the chunk lengths. Returns ``out`` shaped like ``q``.
+    table). ``max_seqlen_q`` must be at least the longest chunk (it sizes the launch without a
+    host read of ``cu_seqlens_q``; tokens of a longer chunk past it are left unwritten), as in
+    varlen flash attention. Returns ``out`` shaped like ``q``.
 
     bf16 / fp16 pools, head_dim 64, 128 or 256, 1/2/4/8 q heads per kv head, block_size >= 8. The
     reference's prefill never reads the paged cache; this is the block-table-aware prefill its
