@@ -108,3 +108,25 @@ def test_overlap_switch_is_per_launch(cuda_device):
     c = plan.run(1, q0)
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_paged_kv_overlaps_only_fused_layers_after_its_own_attend(cuda_device, monkeypatch):
+    """In a decode step, layer 0 follows the seqlen update and must wait for it; layers 1.. of
+    the fused path follow the previous layer's decode and may overlap it. The unfused path
+    (a separate append just before each decode) never overlaps."""
+    from model import _native
+    from test_fused_append_gpu import _container_steps
+
+    seen = []
+    original = _native.NativePlan._set_overlap
+
+    def spy(self, overlap):
+        seen.append(bool(overlap))
+        return original(self, overlap)
+
+    monkeypatch.setattr(_native.NativePlan, "_set_overlap", spy)
+    _container_steps(cuda_device, fuse=True, steps=2, n_layer=3)
+    assert seen[-6:] == [False, True, True] * 2
+    seen.clear()
+    _container_steps(cuda_device, fuse=False, steps=2, n_layer=3)
+    assert seen and not any(seen)
