@@ -167,8 +167,8 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
       failed = true;
     }
     if (__syncthreads_or(failed)) {
-      if (tid == 0) {
-        atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
+      if (warp == 0) {  // the whole warp: the bounded wait is a warp-collective
+        if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
         for (int k2 = kt; k2 < ntiles && k2 < kt + 2; ++k2)  // copies possibly in flight
           warp_wait_phase(smem_addr(bars + (k2 & 1)), uint32_t((k2 >> 1) & 1), DRAIN_LIMIT_NS);
       }
