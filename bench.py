@@ -597,6 +597,120 @@ def prefill_sweep(reps: int = 5) -> None:
         torch.cuda.empty_cache()
 
 
+class _SeatStep:
+    """The reference's seat decode step, restated in torch as the cost comparator (it is not
+    the product and not the numeric oracle). Per step: the additive bias of the dense slab is
+    built once (``KvSlab.build_mask(next_token=True)``, model/slab.py:302-328, with
+    ``additive_bias``, model/attention/hand_baddbmm.py:129-149). Per layer: the token's K/V are
+    scattered into column ``pos`` of the layer's ``(B, H_kv, width, D)`` slab (slab.py:251-266),
+    then ``HandBaddbmmBackend.decode`` (hand_baddbmm.py:80-126) runs: q scaled by 1/sqrt(D),
+    ``baddbmm(bias, q, K^T)`` over the whole slab width, a bf16 softmax and ``bmm`` with V, with
+    the GQA group as the GEMM's row dimension. The slab width is a 64-column bucket."""
+
+    def __init__(self, device, lengths, budget: int, gen):
+        self.B = len(lengths)
+        self.G = H // H_KV
+        self.width = -(-(max(lengths) + budget) // 64) * 64
+        shape = (self.B, H_KV, self.width, D)
+        self.keys = [torch.randn(shape, generator=gen, device=device).to(torch.bfloat16) for _ in range(N_LAYER)]
+        self.values = [torch.randn(shape, generator=gen, device=device).to(torch.bfloat16) for _ in range(N_LAYER)]
+        self.pos = torch.tensor(lengths, device=device, dtype=torch.int64)
+        self.columns = torch.arange(self.width, device=device)
+        self.bias = torch.empty(self.B * H_KV, self.G, self.width, device=device, dtype=torch.bfloat16)
+        self.out = torch.empty(N_LAYER, self.B * H_KV, self.G, D, device=device, dtype=torch.bfloat16)
+
+    def step(self, q_buf, k_buf, v_buf) -> None:
+        B, G, W = self.B, self.G, self.width
+        allowed = self.columns.view(1, W) < (self.pos + 1).view(B, 1)
+        bias = torch.where(allowed, 0.0, float("-inf")).to(torch.bfloat16)
+        self.bias.copy_(bias.view(B, 1, 1, W).expand(B, H_KV, G, W).reshape(B * H_KV, G, W))
+        index = self.pos.view(B, 1, 1, 1).expand(B, H_KV, 1, D)
+        for layer in range(N_LAYER):
+            self.keys[layer].scatter_(2, index, k_buf[layer])
+            self.values[layer].scatter_(2, index, v_buf[layer])
+            qg = (q_buf[layer] * (1.0 / math.sqrt(D))).reshape(B * H_KV, G, D)
+            k_t = self.keys[layer].transpose(-2, -1).reshape(B * H_KV, D, W)
+            probs = torch.softmax(torch.baddbmm(self.bias, qg, k_t), dim=-1)
+            torch.bmm(probs, self.values[layer].reshape(B * H_KV, W, D), out=self.out[layer])
+        self.pos += 1
+
+
+def seat_sweep(reps: int = 10) -> None:
+    """Decode-step cost of the paged arm against the seat arm at Qwen3-0.6B head shapes, both
+    steps (28 layers of K/V append + attention, with the step's bookkeeping) captured once as
+    CUDA graphs and replayed, best of ``reps`` replays. Cases: config 2 (B=32 at 2048 tokens)
+    and the reference's own paged/seat comparison size (B=8, contexts up to 1645 tokens;
+    seeded uniform in [1024, 1645] here). One JSON line per case (not the bench line)."""
+    from model import _native
+    from model.paged import PagedKV, PagedPool
+    from serve.block_manager import BlockManager
+    from serve.graph import PagedStepGraph
+
+    device = torch.device("cuda", 0)
+    eager, budget = 3, 3 + 2 + reps + 2
+    for name, lengths in (("config2_b32_ctx2048", [CONTEXT] * BATCH),
+                          ("b8_ctx1024_1645", torch.randint(1024, 1646, (8,), generator=torch.Generator().manual_seed(5)).tolist())):
+        B = len(lengths)
+        gen = torch.Generator(device=device).manual_seed(21)
+        q_buf = torch.randn(N_LAYER, B, H, 1, D, generator=gen, device=device).to(torch.bfloat16)
+        k_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+        v_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+
+        def timed(replay) -> list[float]:
+            times = []
+            for _ in range(reps):
+                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                replay()
+                stop.record()
+                torch.cuda.synchronize(device)
+                times.append(start.elapsed_time(stop) * 1e3 / N_LAYER)
+            return times
+
+        manager = BlockManager(sum(-(-(n + budget) // BS) for n in lengths), BS)
+        tables = [manager.reserve(manager.blocks_for(n, budget)) for n in lengths]
+        pool = PagedPool(N_LAYER, manager.n_blocks, BS, H_KV, D, dtype=torch.bfloat16, device=device, n_head=H)
+        for t in pool.keys + pool.values:
+            t.copy_(torch.randn(t.shape, generator=gen, device=device))
+        kv = PagedKV(pool, tables, lengths, rope_len=max(lengths) + budget, n_head=H)
+        for _ in range(eager):
+            kv.build_mask(next_token=True)
+            for layer in range(N_LAYER):
+                kv.write(layer, k_buf[layer], v_buf[layer])
+                kv.attend(layer, q_buf[layer])
+            kv.advance()
+        graph = PagedStepGraph(kv, q_buf, k_buf, v_buf)
+        for _ in range(2):
+            graph.replay()
+        paged = timed(graph.replay)
+        if _native.device_error() != 0:
+            raise SystemExit(f"{name}: device error word set")
+        del graph, kv, pool
+        torch.cuda.empty_cache()
+
+        seat = _SeatStep(device, lengths, budget, gen)
+        for _ in range(eager):
+            seat.step(q_buf, k_buf, v_buf)
+        torch.cuda.synchronize(device)
+        seat_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(seat_graph):
+            seat.step(q_buf, k_buf, v_buf)
+        for _ in range(2):
+            seat_graph.replay()
+        seat_times = timed(seat_graph.replay)
+        print(json.dumps({
+            "seat_case": name, "rows": B, "contexts": f"{min(lengths)}..{max(lengths)} (+step)",
+            "layers": N_LAYER, "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
+            "paged_us_per_layer_step": round(min(paged), 2), "seat_us_per_layer_step": round(min(seat_times), 2),
+            "paged_over_seat": round(min(paged) / min(seat_times), 3),
+            "paged_median": round(statistics.median(paged), 2), "seat_median": round(statistics.median(seat_times), 2),
+            "seat_slab_width": seat.width,
+            "note": "attention part of the decode step (append + attention + step bookkeeping), both arms as "
+                    "CUDA graphs; the reference's own paged/seat figure is a whole-model step"}), flush=True)
+        del seat_graph, seat
+        torch.cuda.empty_cache()
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--profile-case", default=None,
@@ -608,6 +722,8 @@ def main(argv=None) -> int:
                         help="time the decode kernel alone on every BASELINE config instead of the benchmark")
     parser.add_argument("--prefill", action="store_true",
                         help="time the chunked-prefill kernel (paged_prefill) instead of the benchmark")
+    parser.add_argument("--seat", action="store_true",
+                        help="time the paged decode step against the seat (dense slab) step instead of the benchmark")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=100)
     parser.add_argument("--warmup", type=int, default=5)
@@ -627,6 +743,9 @@ def main(argv=None) -> int:
         return 0
     if args.prefill:
         prefill_sweep()
+        return 0
+    if args.seat:
+        seat_sweep()
         return 0
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
