@@ -137,6 +137,23 @@ def test_prefill_ignores_nan_in_slots_no_row_reads(cuda_device):
 
 
 @pytest.mark.gpu
+def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device):
+    """Engines pass a bucketed bound; the extra query tiles of the grid have no tokens."""
+    from model import _native
+    from model.triton_decode import paged_prefill
+
+    q, k, v, table, cu, sk = prefill_case(16, 8, 128, 16, [40, 0, 500], [3, 70, 33], seed=9)
+    dev = [t.to(cuda_device) for t in (q, k, v, table, cu, sk)]
+    tight = paged_prefill(*dev, 70)
+    loose = paged_prefill(*dev, 1000)
+    torch.cuda.synchronize()
+    assert torch.equal(tight, loose)
+    ref_f32, _ = oracle.paged_prefill(q, k, v, table, cu, sk)
+    assert_output_close(loose, ref_f32, torch.bfloat16)
+    assert _native.device_error() == 0
+
+
+@pytest.mark.gpu
 def test_one_token_chunks_agree_with_the_decode_kernel(cuda_device):
     from model.triton_decode import paged_decode, paged_prefill
 
