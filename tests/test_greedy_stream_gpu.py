@@ -1,10 +1,12 @@
-"""Greedy decode of a 28-layer Qwen3-0.6B-shaped model through ``PagedKV`` (config 2).
+"""Greedy decode of random-init models through ``PagedKV`` at the two attention shapes the
+engines drive: config 2's 28-layer Qwen3-0.6B (16 q / 8 kv heads, head_dim 128, full RoPE), and
+Qwen3.5-0.8B's 6 full-attention layers (8 q / 2 kv heads, head_dim 256, RoPE on the first 64
+dims; its linear-attention layers are outside this path and left out).
 
-The model has random-init weights, no checkpoint (hidden 1024, 16 q / 8 kv heads, head_dim 128,
-SwiGLU 3072, vocab 151936, RMSNorm with per-head q/k norms, RoPE theta 1e6, bf16, tied
-embeddings). It runs B=32 requests, each with a 2048-token prompt in paged KV (block size 16,
-blocks assigned by a seeded permutation), for 64 greedy steps. The arms share every tensor
-op except attention:
+The models have no checkpoint: hidden 1024, SwiGLU 3072, vocab 151936, RMSNorm with per-head
+q/k norms, RoPE theta 1e6, bf16, tied embeddings. Each runs B=32 requests, each with a
+2048-token prompt in paged KV (block size 16, blocks assigned by a seeded permutation), for
+64 greedy steps. The arms share every tensor op except attention:
 
 * the product arm appends each step's K/V and attends through ``PagedKV.write`` /
   ``PagedKV.attend``: the fused sm_100a append + decode launch, overlapped launches included;
@@ -15,7 +17,7 @@ op except attention:
 A third arm, the same gather attention in float64, is the noise floor: it is as correct
 as the fp32 reference, and it still differs from it by a bf16 ulp in some attention outputs.
 Each arm computes its new K/V from its own hidden state, so such differences compound over
-28 layers and 64 steps. Random weights give flat logits (top-2 gaps of a few thousandths
+the layers and 64 steps. Random weights give flat logits (top-2 gaps of a few thousandths
 are common), so near-ties flip in the floor arm too.
 
 The prompt K/V come from one shared bf16 prefill and are written into every arm. Decoding is
@@ -30,6 +32,7 @@ floor's own deviation could flip.
 from __future__ import annotations
 
 import math
+from typing import NamedTuple
 
 import pytest
 import torch
@@ -37,7 +40,7 @@ import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
 
-VOCAB, HIDDEN, N_LAYER, H, HKV, D, INTER = 151936, 1024, 28, 16, 8, 128, 3072
+VOCAB, HIDDEN, INTER = 151936, 1024, 3072
 THETA, EPS = 1e6, 1e-6
 B, PROMPT, STEPS, BS = 32, 2048, 64, 16
 
@@ -45,27 +48,44 @@ FLOOR_FACTOR = 2.0
 MISMATCH_SLACK = 8
 
 
+class Shape(NamedTuple):
+    n_layer: int
+    h: int       # q heads
+    hkv: int     # kv heads
+    d: int       # head_dim
+    rotary: int  # leading dims that RoPE rotates
+
+
+SHAPES = [
+    pytest.param(Shape(28, 16, 8, 128, 128), id="qwen3-28-layers"),
+    pytest.param(Shape(6, 8, 2, 256, 64), id="qwen35-6-full-attention-layers"),
+]
+
+
 def _rms(x, w):
     xf = x.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + EPS)).to(x.dtype) * w
 
 
-def _rope_tables(n_pos, device):
-    inv = 1.0 / (THETA ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+def _rope_tables(n_pos, rot, device):
+    inv = 1.0 / (THETA ** (torch.arange(0, rot, 2, device=device, dtype=torch.float32) / rot))
     freqs = torch.outer(torch.arange(n_pos, device=device, dtype=torch.float32), inv)
     emb = torch.cat([freqs, freqs], dim=-1)
     return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
 
 
 def _rope(x, cos, sin):
-    """x (..., n, D) with cos/sin (n, D): GPT-NeoX rotation over the whole head."""
-    half = x.shape[-1] // 2
-    rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
-    return x * cos + rot * sin
+    """x (..., n, D) with cos/sin (n, R): GPT-NeoX rotation of the first R dims, the rest kept."""
+    r = cos.shape[-1]
+    xr, half = x[..., :r], r // 2
+    rotated = torch.cat([-xr[..., half:], xr[..., :half]], dim=-1)
+    return torch.cat([xr * cos + rotated * sin, x[..., r:]], dim=-1)
 
 
 class _Model:
-    def __init__(self, device, seed=0):
+    def __init__(self, device, shape: Shape, seed=0):
+        self.s = S = shape
+        H, HKV, D = S.h, S.hkv, S.d
         gen = torch.Generator(device=device).manual_seed(seed)
 
         def w(*shape):
@@ -78,13 +98,14 @@ class _Model:
             dict(ln1=ones(HIDDEN), wq=w(H * D, HIDDEN), wk=w(HKV * D, HIDDEN), wv=w(HKV * D, HIDDEN),
                  qn=ones(D), kn=ones(D), wo=w(HIDDEN, H * D), ln2=ones(HIDDEN), wg=w(INTER, HIDDEN),
                  wu=w(INTER, HIDDEN), wd=w(HIDDEN, INTER))
-            for _ in range(N_LAYER)
+            for _ in range(S.n_layer)
         ]
         self.norm = ones(HIDDEN)
-        self.cos, self.sin = _rope_tables(PROMPT + STEPS, device)
+        self.cos, self.sin = _rope_tables(PROMPT + STEPS, S.rotary, device)
 
     def qkv(self, L, x, pos):
         """x (B, n, HIDDEN) at positions pos (n,) -> q (B, H, n, D), k / v (B, HKV, n, D)."""
+        H, HKV, D = self.s.h, self.s.hkv, self.s.d
         h = _rms(x, L["ln1"])
         n = x.shape[1]
         q = _rms((h @ L["wq"].T).view(B, n, H, D), L["qn"]).transpose(1, 2)
@@ -96,7 +117,7 @@ class _Model:
     def finish(self, L, x, attn):
         """attn (B, H, n, D): output projection, residual and the MLP."""
         n = x.shape[1]
-        x = x + attn.transpose(1, 2).reshape(B, n, H * D) @ L["wo"].T
+        x = x + attn.transpose(1, 2).reshape(B, n, self.s.h * self.s.d) @ L["wo"].T
         h = _rms(x, L["ln2"])
         return x + (F.silu(h @ L["wg"].T) * (h @ L["wu"].T)) @ L["wd"].T
 
@@ -108,6 +129,7 @@ class _Model:
 def _ref_attend(q, kc, vc, n_keys, dtype=torch.float32):
     """Attention of q (B, H, 1, D) over the first n_keys of the dense cache, computed in
     `dtype` and rounded to bf16."""
+    H, HKV, D = q.shape[1], kc.shape[1], q.shape[-1]
     k = kc[:, :, :n_keys].to(dtype)
     v = vc[:, :, :n_keys].to(dtype)
     qg = q.to(dtype).view(B, HKV, H // HKV, D)
@@ -115,14 +137,14 @@ def _ref_attend(q, kc, vc, n_keys, dtype=torch.float32):
     return torch.einsum("bkgt,bktd->bkgd", p, v).reshape(B, H, 1, D).to(torch.bfloat16)
 
 
-def run_streams(device):
+def run_streams(device, shape: Shape):
     """All arms over the 64 steps; returns per-step tensors (steps, B) of the product and
     float64 arms' tokens, the fp32 reference's tokens and top-2 gaps, and each arm's largest
     logit deviation from the fp32 reference."""
     from model.paged import PagedKV, PagedPool
 
-    torch.manual_seed(0)
-    model = _Model(device)
+    H, HKV, D, N_LAYER = shape.h, shape.hkv, shape.d, shape.n_layer
+    model = _Model(device, shape)
     gen = torch.Generator(device=device).manual_seed(1)
     prompt = torch.randint(0, VOCAB, (B, PROMPT), generator=gen, device=device)
 
@@ -187,10 +209,11 @@ def run_streams(device):
                 logit_std=lr.std().item())
 
 
-def test_greedy_streams_agree_through_paged_kv(cuda_device):
+@pytest.mark.parametrize("shape", SHAPES)
+def test_greedy_streams_agree_through_paged_kv(cuda_device, shape):
     from model import _native
 
-    s = run_streams(cuda_device)
+    s = run_streams(cuda_device, shape)
     mismatch = s["ours"] != s["ref"]
     n_mis, n_floor = int(mismatch.sum()), int((s["exact"] != s["ref"]).sum())
     worst_gap = float(s["gap"][mismatch].max()) if n_mis else 0.0
