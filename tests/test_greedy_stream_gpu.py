@@ -9,7 +9,10 @@ q/k norms, RoPE theta 1e6, bf16, tied embeddings. Each runs B=32 requests, each 
 64 greedy steps. The arms share every tensor op except attention:
 
 * the product arm appends each step's K/V and attends through ``PagedKV.write`` /
-  ``PagedKV.attend``: the fused sm_100a append + decode launch, overlapped launches included;
+  ``PagedKV.attend``: the fused sm_100a append + decode launch, overlapped launches included.
+  It hands K over *before* its rotary embedding with ``rope=(cos, sin)``, so the append
+  rotates it on the way into the pool (the reference arms rotate K in torch, in the
+  reference's arithmetic);
 * the reference arm keeps a dense per-request cache and attends in fp32 over the gathered
   keys (softmax(q k^T / sqrt(d)) V, rounded to bf16), which is the reference's torch
   paged-gather attention.
@@ -103,8 +106,9 @@ class _Model:
         self.norm = ones(HIDDEN)
         self.cos, self.sin = _rope_tables(PROMPT + STEPS, S.rotary, device)
 
-    def qkv(self, L, x, pos):
-        """x (B, n, HIDDEN) at positions pos (n,) -> q (B, H, n, D), k / v (B, HKV, n, D)."""
+    def qkv(self, L, x, pos, rotate_k=True):
+        """x (B, n, HIDDEN) at positions pos (n,) -> q (B, H, n, D), k / v (B, HKV, n, D);
+        k is returned before its rotary embedding when ``rotate_k`` is False."""
         H, HKV, D = self.s.h, self.s.hkv, self.s.d
         h = _rms(x, L["ln1"])
         n = x.shape[1]
@@ -112,7 +116,13 @@ class _Model:
         k = _rms((h @ L["wk"].T).view(B, n, HKV, D), L["kn"]).transpose(1, 2)
         v = (h @ L["wv"].T).view(B, n, HKV, D).transpose(1, 2)
         cos, sin = self.cos[pos], self.sin[pos]
-        return _rope(q, cos, sin), _rope(k, cos, sin), v
+        return _rope(q, cos, sin), (_rope(k, cos, sin) if rotate_k else k), v
+
+    def rope_rows(self, p):
+        """The (B, R/2) cos/sin rows of position p that a rotated ``PagedKV.write`` takes."""
+        half = self.s.rotary // 2
+        return (self.cos[p, :half].expand(B, half).contiguous(),
+                self.sin[p, :half].expand(B, half).contiguous())
 
     def finish(self, L, x, attn):
         """attn (B, H, n, D): output projection, residual and the MLP."""
@@ -182,8 +192,8 @@ def run_streams(device, shape: Shape):
             kv.build_mask(next_token=True)
             xo = xr = xx = model.embed[tok].unsqueeze(1)
             for li, L in enumerate(model.layers):
-                q, k, v = model.qkv(L, xo, pos)
-                kv.write(li, k, v)
+                q, k, v = model.qkv(L, xo, pos, rotate_k=False)
+                kv.write(li, k, v, rope=model.rope_rows(p))
                 xo = model.finish(L, xo, kv.attend(li, q))
                 q, k, v = model.qkv(L, xr, pos)
                 kc[li][:, :, p:p + 1] = k
@@ -194,6 +204,9 @@ def run_streams(device, shape: Shape):
                 vx[li][:, :, p:p + 1] = v
                 xx = model.finish(L, xx, _ref_attend(q, kx[li], vx[li], p + 1, torch.float64))
             kv.advance()
+            if step == 0:  # layer 0 of step 0 sees the same hidden state in every arm
+                rope_bitwise = all(
+                    torch.equal(pool.keys[0][tables[r][p // BS], p % BS], kc[0][r, :, p]) for r in range(B))
             lo, lr, lx = model.logits(xo), model.logits(xr), model.logits(xx)
             top2 = lr.topk(2, dim=-1).values
             ours_tok.append(lo.argmax(-1))
@@ -206,7 +219,7 @@ def run_streams(device, shape: Shape):
     torch.cuda.synchronize()
     return dict(ours=torch.stack(ours_tok), ref=torch.stack(ref_tok), exact=torch.stack(x_tok),
                 gap=torch.stack(gaps), delta=torch.stack(deltas), exact_delta=torch.stack(x_deltas),
-                logit_std=lr.std().item())
+                logit_std=lr.std().item(), rope_bitwise=rope_bitwise)
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -222,6 +235,7 @@ def test_greedy_streams_agree_through_paged_kv(cuda_device, shape):
               f"arm: {n_floor}); worst top-2 gap at a mismatch {worst_gap:.4f}; max |logit delta| "
               f"{delta:.4f} (float64 arm: {floor:.4f}); logit std {s['logit_std']:.3f}")
     assert _native.device_error() == 0
+    assert s["rope_bitwise"], "K rotated by the fused append differs from K rotated in torch"
     assert delta <= FLOOR_FACTOR * floor, detail
     assert n_mis <= FLOOR_FACTOR * n_floor + MISMATCH_SLACK, detail
     assert worst_gap < 2 * floor, detail
