@@ -378,7 +378,7 @@ def _finish(dist):
 
 def _cpu_sample(sample_layers: int, seed: int = 0):
     """Config-2 shapes for ``sample_layers`` layers on the CPU (bf16 K/V, same generator)."""
-    from serve import workloads
+    import workloads
 
     wl = workloads.config2("cpu", seed=seed, n_layer=sample_layers)
     return wl
@@ -441,7 +441,7 @@ def profile_case(name: str, launches: int = 4) -> None:
     kernel; each appends the same token again), nothing else on the GPU afterwards."""
     from model import _native
     from model.triton_decode import paged_decode_plan
-    from serve import workloads
+    import workloads
 
     device = torch.device("cuda", 0)
     if name == "prefill":  # chunked prefill: 4 rows x (2048 cached + 512 new tokens), one layer
@@ -489,7 +489,7 @@ def config_sweep(reps: int = 5) -> None:
     One JSON line per config (not the bench line)."""
     from model import _native
     from model.triton_decode import paged_decode_plan
-    from serve import workloads
+    import workloads
 
     device = torch.device("cuda", 0)
     peak = _peaks()["hbm_gbs"]

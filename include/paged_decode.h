@@ -77,10 +77,13 @@ int pd_device_error(unsigned int* bits, int clear);
  *   out      (B, H, D)       strides o_sb, o_sh
  *   scale_log2 = scale * log2(e)  (model/triton_decode.py:291-292)
  *   workspace: device memory of at least pd_decode_workspace_bytes(...) bytes, 256-byte
- *     aligned, with arbitrary contents (no clearing needed: split rows are counted with
- *     per-launch epochs that the kernel keeps in the workspace and advances itself, so
- *     launches replayed from a captured CUDA graph stay correct). One workspace must not be
- *     used by two launches that may run concurrently.
+ *     aligned, with any contents -- zero-filled, garbage, or left by earlier launches of any
+ *     shape (no clearing needed: split rows are counted with per-launch epochs that the kernel
+ *     keeps in the workspace and advances itself, and the counters' tags are odd and salted
+ *     per layout, so stale memory never carries a live tag; launches replayed from a captured
+ *     CUDA graph stay correct). One workspace must not be used by two launches that may run
+ *     concurrently. After a launch that recorded PD_DEVERR_WAIT_TIMEOUT the workspace is
+ *     still usable as is.
  *
  * Row b, head h reads only the first ceil(seqlen[b] / block_size) table entries;
  * zero-length rows produce exact zeros (model/triton_decode.py:639).
@@ -116,8 +119,9 @@ int pd_decode(const void* q, int64_t q_sb, int64_t q_sh,
  * heads per kv head) are rejected with PD_ERR_WORKSPACE and a message in
  * pd_last_error_string(); use pd_decode with a workspace for those.
  *
- * The array keeps whatever the previous call left; nothing in it has to start at zero (split
- * rows are counted with per-launch epochs). All calls on one device share the array, so two
+ * The array keeps whatever the previous call left and starts out zero-filled; neither needs
+ * clearing (split rows are counted with per-launch epochs and odd counter tags, which zeroed
+ * or stale memory never carries). All calls on one device share the array, so two
  * calls whose kernels can overlap on the GPU (different streams without ordering between
  * them) race and may return wrong results: issue them on one stream or order them.
  */
@@ -145,8 +149,8 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * not read cu_seqlens_q on the host): query tokens of a longer chunk past it are not written.
  * Supported: bf16 / fp16, head_dim 64, 128 or 256, 1, 2, 4 or 8 q heads per kv head, block_size
  * >= 8 (PD_ERR_UNSUPPORTED otherwise). No workspace. The reference has no counterpart: its
- * varlen prefill (flash_attn 2.8.3) never reads the paged cache; this is the
- * block-table-aware prefill its hot-path notes list as next. */
+ * packed varlen prefill (flash_attn 2.8.3, model/attention/varlen.py:317-357; docs/decisions.md
+ * D7) writes the paged pool but never reads it, so a chunk cannot attend to cached keys. */
 int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, const void* v_cache,
                int64_t n_blocks, int32_t block_size, const int64_t* k_strides, const int64_t* v_strides,
                const int32_t* block_table, int64_t bt_stride, int32_t max_blocks,
@@ -321,6 +325,17 @@ int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_
  * against concurrent launches that size their workspace. No reference counterpart. */
 int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost);
 int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost);
+
+/* Time limit, in nanoseconds, of the kernels' waits on a pipeline stage (mbarrier) or on a
+ * split item's arrival counter, for launches made afterwards (default 1 s; 0 restores it;
+ * at most 10 s). A wait that runs out records PD_DEVERR_WAIT_TIMEOUT in the device error word,
+ * waits for its own copies still in flight (always with a fixed 0.1 s limit) and returns, so
+ * the launch ends and the context stays usable; outputs of that launch are then unspecified.
+ * A limit below 1000 ns makes a stage wait probe once without blocking and give up if the copy
+ * has not landed yet, so the waits run out on purpose: that is how a test exercises this error
+ * path without a hang or a fault. No reference counterpart (its kernel has no waits). */
+int pd_set_wait_limit(uint64_t limit_ns);
+uint64_t pd_get_wait_limit(void);
 
 #ifdef __cplusplus
 }

@@ -40,9 +40,15 @@ int g_row_cost = 3;  // column split: virtual columns charged per row start
 constexpr int kCtaConsumerWarps = 8;
 
 thread_local char g_last_error[256] = "";
+// Workspace bytes the last prepare() on this thread found missing (PD_ERR_WORKSPACE).
+thread_local size_t g_last_ws_need = 0;
 
 // Kernels launched by this library in this process (pd_launch_count).
 std::atomic<unsigned long long> g_launches{0};
+
+// Limit of the kernels' mbarrier and arrival-counter waits, read at every launch
+// (pd_set_wait_limit).
+std::atomic<unsigned long long> g_wait_limit_ns{WAIT_LIMIT_NS};
 
 // Records a failed CUDA call for pd_last_error_string and returns PD_ERR_CUDA.
 int cuda_fail(cudaError_t e, const char* where) {
@@ -281,6 +287,19 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
   return r == CUDA_SUCCESS ? PD_OK : PD_ERR_INVALID;
 }
 
+// Even 32-bit salt of a workspace layout and half for the counters' tags: two layouts (or the two
+// halves of one plan's workspace) that reuse the same bytes get unrelated tags, so a counter
+// one of them left behind does not carry a tag the other is using.
+uint32_t layout_salt(const WorkspaceLayout& w, int batch, int items_per_row, int half) {
+  uint64_t x = uint64_t(w.total) * 0x9E3779B97F4A7C15ull;
+  x ^= (uint64_t(uint32_t(batch)) << 32 | uint32_t(items_per_row)) * 0xC2B2AE3D27D4EB4Full;
+  x ^= uint64_t(half + 1) * 0x165667B19E3779F9ull;
+  x ^= x >> 29;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 32;
+  return uint32_t(x) & ~1u;
+}
+
 // Everything fixed for one (pool layout, table, seqlen, batch) -- shared by pd_decode,
 // pd_decode_partials and the plan.
 struct Prepared {
@@ -311,10 +330,19 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   if (st != PD_OK) return st;
   P->ws = workspace_layout(batch, n_kv_head, P->g, head_dim, P->L);
   if (batch > 0) {
-    if (workspace == nullptr || workspace_bytes < P->ws.total) return PD_ERR_WORKSPACE;
+    if (workspace == nullptr || workspace_bytes < P->ws.total) {
+      g_last_ws_need = P->ws.total;
+      snprintf(g_last_error, sizeof(g_last_error),
+               "workspace of %zu bytes is smaller than the %zu bytes this shape needs", workspace_bytes,
+               P->ws.total);
+      return PD_ERR_WORKSPACE;
+    }
     P->half_bytes = round_up(P->ws.total, 256);
     P->halves = workspace_bytes >= 2 * P->half_bytes ? 2 : 1;
-    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return PD_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+      snprintf(g_last_error, sizeof(g_last_error), "workspace is not 256-byte aligned");
+      return PD_ERR_WORKSPACE;
+    }
     if (block_table == nullptr && max_blocks > 0) return PD_ERR_INVALID;
     if (seqlen == nullptr) return PD_ERR_INVALID;
   }
@@ -332,6 +360,7 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.epoch_word = reinterpret_cast<unsigned*>(ws);
   p.exit_counter = reinterpret_cast<unsigned long long*>(ws + 8);
+  p.tag_salt = layout_salt(P->ws, batch, n_kv_head * P->g.n_gchunks, 0);
   p.counters = reinterpret_cast<unsigned long long*>(ws + P->ws.counters_off);
   p.ws_ml = reinterpret_cast<float*>(ws + P->ws.ml_off);
   p.ws_acc = reinterpret_cast<float*>(ws + P->ws.acc_off);
@@ -409,9 +438,11 @@ int run_prepared(const Prepared& P, const CUtensorMap& kmap, const CUtensorMap& 
       p.counters = reinterpret_cast<unsigned long long*>(reinterpret_cast<unsigned char*>(p.counters) + h);
       p.ws_ml = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(p.ws_ml) + h);
       p.ws_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(p.ws_acc) + h);
+      p.tag_salt = layout_salt(P.ws, P.base.batch, P.base.n_kv_head * P.base.n_gchunks, 1);
     }
     p.batch = rows;
     p.mode = mode;
+    p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
     p.q = static_cast<const unsigned char*>(q) + int64_t(b0) * q_sb * es;
     p.q_sb = q_sb;
     p.q_sh = q_sh;
@@ -619,6 +650,7 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
   p.box_tokens = box_tokens;
   p.scale_log2 = scale_log2;
   p.err = err;
+  p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
   const cudaError_t e = launch_prefill(p, kmap, vmap, dtype, head_dim, group, max_seqlen_q, batch, n_kv_head,
                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
@@ -947,6 +979,14 @@ int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost)
   return PD_OK;
 }
 
+int pd_set_wait_limit(uint64_t limit_ns) {
+  if (limit_ns > 10ull * WAIT_LIMIT_NS) return PD_ERR_INVALID;
+  g_wait_limit_ns.store(limit_ns == 0 ? WAIT_LIMIT_NS : limit_ns, std::memory_order_relaxed);
+  return PD_OK;
+}
+
+uint64_t pd_get_wait_limit(void) { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
 int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_per_sm,
                          int32_t* min_tiles_per_warp) {
   std::lock_guard<std::mutex> lock(g_mutex);
@@ -988,26 +1028,21 @@ int pd_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const void* k_c
                       int64_t bt_stride, int32_t max_blocks, const int32_t* seqlen, void* out,
                       int64_t o_sb, int64_t o_sh, int32_t batch, int32_t n_head, int32_t n_kv_head,
                       int32_t head_dim, int32_t dtype, float scale_log2, void* stream) {
-  const size_t need = pd_decode_workspace_bytes(batch, n_head, n_kv_head, head_dim, dtype);
-  if (need == 0) {
-    Geometry g;
-    const int st = geometry(n_head, n_kv_head, head_dim, block_size, dtype, &g);
-    return st != PD_OK ? st : PD_ERR_CUDA;
-  }
-  if (need > size_t(PD_NOALLOC_SCRATCH_BYTES)) {
-    snprintf(g_last_error, sizeof(g_last_error),
-             "pd_decode_noalloc: this shape needs %zu bytes of scratch but the built-in array "
-             "holds %u; call pd_decode with a workspace instead",
-             need, unsigned(PD_NOALLOC_SCRATCH_BYTES));
-    return PD_ERR_WORKSPACE;
-  }
   void* scratch = nullptr;
-  const int st = noalloc_scratch(&scratch);
+  int st = noalloc_scratch(&scratch);
   if (st != PD_OK) return st;
-  return decode_common(q, q_sb, q_sh, k_cache, v_cache, n_blocks, block_size, k_strides, v_strides,
-                       block_table, bt_stride, max_blocks, seqlen, out, o_sb, o_sh, nullptr, nullptr,
-                       nullptr, 0, batch, n_head, n_kv_head, head_dim, dtype, scale_log2, scratch,
-                       size_t(PD_NOALLOC_SCRATCH_BYTES), stream);
+  // The size check is the one pd_decode makes against its workspace, done by the same prepare()
+  // that lays the scratch out, so the refusal always matches the layout actually used.
+  st = decode_common(q, q_sb, q_sh, k_cache, v_cache, n_blocks, block_size, k_strides, v_strides,
+                     block_table, bt_stride, max_blocks, seqlen, out, o_sb, o_sh, nullptr, nullptr,
+                     nullptr, 0, batch, n_head, n_kv_head, head_dim, dtype, scale_log2, scratch,
+                     size_t(PD_NOALLOC_SCRATCH_BYTES), stream);
+  if (st == PD_ERR_WORKSPACE)
+    snprintf(g_last_error, sizeof(g_last_error),
+             "pd_decode_noalloc: this shape needs %zu bytes of scratch but the built-in scratch array "
+             "holds %u; call pd_decode with a workspace instead",
+             g_last_ws_need, unsigned(PD_NOALLOC_SCRATCH_BYTES));
+  return st;
 }
 
 }  // extern "C"

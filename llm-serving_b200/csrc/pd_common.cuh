@@ -18,8 +18,12 @@ constexpr unsigned FULL_MASK = 0xffffffffu;
 constexpr unsigned DEVERR_WAIT_TIMEOUT = 1u;
 constexpr unsigned DEVERR_APPEND_RANGE = 2u;
 
-// A bounded mbarrier wait gives up after this many nanoseconds of %globaltimer.
-constexpr unsigned long long WAIT_LIMIT_NS = 1000000000ull;      // 1 s
+// A bounded wait on an mbarrier or an arrival counter gives up after this many nanoseconds of
+// %globaltimer (the launch's `wait_ns`, which pd_set_wait_limit can shorten to exercise the
+// error path). The drain of copies still in flight after such a failure, and a warp's exit
+// bookkeeping, always use the fixed limits below, so that a CTA never retires with a copy in
+// flight and the workspace epoch always advances.
+constexpr unsigned long long WAIT_LIMIT_NS = 1000000000ull;      // 1 s (default wait_ns, exit)
 constexpr unsigned long long DRAIN_LIMIT_NS = 100000000ull;      // 0.1 s per stage
 
 constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x >> 1); }
@@ -67,10 +71,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Limits below this are test limits (pd_set_wait_limit): the wait then probes once without
+// blocking and gives up if the phase is not complete, so that a copy still in flight makes it
+// run out deterministically.
+constexpr unsigned long long PROBE_LIMIT_NS = 1000ull;
+
 // Warp-collective bounded wait: returns true once every lane has observed the phase with
 // the given parity complete, false (uniformly) once `limit_ns` has elapsed.
 __device__ __forceinline__ bool warp_wait_phase(uint32_t bar, uint32_t parity,
                                                 unsigned long long limit_ns) {
+  if (limit_ns < PROBE_LIMIT_NS) return __all_sync(FULL_MASK, mbar_test_wait(bar, parity));
   bool done = mbar_try_wait(bar, parity);
   if (__all_sync(FULL_MASK, done)) return true;
   unsigned long long start = global_timer_ns();
@@ -385,6 +408,8 @@ struct DecodeParams {
   // replays of a captured CUDA graph included -- never share an epoch.
   unsigned* epoch_word;
   unsigned long long* exit_counter;
+  uint32_t tag_salt;  // even; mixed into the counters' tags (counter_tag in pd_decode_kernel.cuh)
+  unsigned long long wait_ns;  // limit of mbarrier and arrival-counter waits
   // Fused append (append != 0): before the decode reads them, row b's new K and V rows
   // (app_k/app_v, same dtype as the pool, 16-byte aligned) are stored at logical position
   // app_pos[b] of the row, i.e. pool block table[b, pos / bs], slot pos % bs, and the tile
@@ -453,6 +478,7 @@ struct PrefillParams {
   int32_t box_tokens;   // min(block_size, 64)
   float scale_log2;
   unsigned* err;
+  unsigned long long wait_ns;  // limit of the stage waits
 };
 
 struct MergeParams {

@@ -135,22 +135,34 @@ __device__ __forceinline__ void cursor_advance_col(Cursor& c, const int* pre, co
   }
 }
 
+// Tag that a launch of epoch `epoch` writes into the high word of its counters. It is odd, so
+// it never equals the high word of memory in the states stale memory is usually found in:
+// zero-filled (a fresh allocation, a zeroed buffer, the library's static scratch array) or
+// holding float partials (+-0, +-inf and 1.0 all have even bit patterns). The even `salt`
+// (host-chosen per workspace layout and half) separates the tags of different layouts that
+// reuse one buffer, and tags of consecutive epochs differ, so the counters a finished launch
+// leaves behind never carry the next launch's tag either.
+__device__ __forceinline__ uint32_t counter_tag(uint32_t epoch, uint32_t salt) {
+  return ((epoch << 1) | 1u) ^ salt;
+}
+
 // Arrival on the counter shared by the pieces of one split item; returns how many pieces of
 // this launch arrived before. Counters live in workspace memory that is never cleared and hold
-// (epoch << 32) | count. Every launch re-tags its item counters with its own epoch in the
+// (tag << 32) | count. Every launch re-tags its item counters with its own tag in the
 // prologue (each CTA a share of them), so an arrival is one atomicAdd with no contention
-// beyond the hardware's. An arrival that beats its counter's re-tag sees another epoch; its
+// beyond the hardware's. An arrival that beats its counter's re-tag sees another tag; its
 // add lands on a value the re-tag overwrites, so it waits for the re-tag and adds again
 // (bounded: on expiry it records DEVERR_WAIT_TIMEOUT and returns -1, i.e. "not last").
-__device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t epoch, unsigned* err) {
+__device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t tag, unsigned* err,
+                                           unsigned long long limit_ns) {
   unsigned long long t0 = 0;
   for (;;) {
     const unsigned long long old = atomicAdd(counter, 1ull);  // callers fence before arriving
-    if (uint32_t(old >> 32) == epoch) return int(uint32_t(old));
+    if (uint32_t(old >> 32) == tag) return int(uint32_t(old));
     const unsigned long long now = global_timer_ns();
     if (t0 == 0) {
       t0 = now;
-    } else if (now - t0 > WAIT_LIMIT_NS) {
+    } else if (now - t0 > limit_ns) {
       atomicOr(err, DEVERR_WAIT_TIMEOUT);
       return -1;
     }
@@ -160,14 +172,16 @@ __device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t
 
 // Leaving the launch (lane 0 of every warp, on every path): one arrival on the exit counter.
 // The last of the launch's `total_warps` arrivals advances the workspace epoch for the next
-// launch. An arrival that beats CTA 0's re-tag of the counter sees another epoch; like
+// launch. An arrival that beats CTA 0's re-tag of the counter sees another tag; like
 // take_ticket it waits (bounded) for the re-tag and arrives again.
 __device__ __forceinline__ void leave_launch(unsigned long long* exit_counter, unsigned* epoch_word,
-                                             uint32_t epoch, unsigned total_warps, unsigned* err) {
+                                             uint32_t epoch, uint32_t salt, unsigned total_warps,
+                                             unsigned* err) {
+  const uint32_t tag = counter_tag(epoch, salt);
   unsigned long long t0 = 0;
   for (;;) {
     const unsigned long long old = atomicAdd(exit_counter, 1ull);
-    if (uint32_t(old >> 32) == epoch) {
+    if (uint32_t(old >> 32) == tag) {
       if (uint32_t(old) == total_warps - 1u) atomicExch(epoch_word, epoch + 1u);
       return;
     }
@@ -327,12 +341,12 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   const uint32_t epoch = *s_epoch;
 
   // Re-tag this launch's item counters (this CTA's share) and, in CTA 0, the exit counter
-  // with the launch's epoch. Arrivals come at least one tile later. (The workspace belongs to
+  // with the launch's tag (counter_tag). Arrivals come at least one tile later. (The workspace belongs to
   // this launch alone: an overlapped launch gets the other half of its plan's workspace from
   // the one it overlaps.)
   {
     const int64_t n_items = int64_t(B) * p.n_kv_head * p.n_gchunks;
-    const unsigned long long tag = (unsigned long long)epoch << 32;
+    const unsigned long long tag = (unsigned long long)counter_tag(epoch, p.tag_salt) << 32;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + tid; i < n_items; i += int64_t(gridDim.x) * blockDim.x)
       atomicExch(p.counters + i, tag);
     if (blockIdx.x == 0 && tid == 0) atomicExch(p.exit_counter, tag);
@@ -565,7 +579,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     for (; issued < nunits; ++issued) {
       const int s = int(issued % S);
       if (issued >= S &&
-          !warp_wait_phase(smem_addr(empty_bars + s), uint32_t(((issued / S) - 1) & 1), WAIT_LIMIT_NS)) {
+          !warp_wait_phase(smem_addr(empty_bars + s), uint32_t(((issued / S) - 1) & 1), p.wait_ns)) {
         if (lane == 0) atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
         break;
       }
@@ -584,7 +598,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     // with a copy in flight, whatever the consumers did.
     const int64_t from = issued > S ? issued - S : 0;
     for (int64_t j = from; j < issued; ++j)
-      warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), WAIT_LIMIT_NS);
+      warp_wait_phase(smem_addr(my_bars + int(j % S)), uint32_t((j / S) & 1), DRAIN_LIMIT_NS);
     return epoch;
   }
   if (!CTA) {
@@ -975,7 +989,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   int s = 0;              // stage of tile k (= k % S)
   uint32_t parity = 0u;   // mbarrier phase parity of tile k (= (k / S) & 1)
   float sc_cur[RR], sc_nxt[RR];
-  if (!warp_wait_phase(smem_addr(my_bars), 0u, WAIT_LIMIT_NS)) {
+  if (!warp_wait_phase(smem_addr(my_bars), 0u, p.wait_ns)) {
     fail_and_drain(0);
     return epoch;
   }
@@ -991,7 +1005,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     const int s_n = s + 1 == S ? 0 : s + 1;
     const uint32_t parity_n = s + 1 == S ? parity ^ 1u : parity;
     if (!CTA && has_next) {
-      if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
+      if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, p.wait_ns)) {
         fail_and_drain(k + 1);
         return epoch;
       }
@@ -1019,7 +1033,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       // Hand the stage just consumed back to the producer, then take the next one.
       if (lane == 0) mbar_arrive(smem_addr(empty_bars + s));
       if (has_next) {
-        if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, WAIT_LIMIT_NS)) {
+        if (!warp_wait_phase(smem_addr(my_bars + s_n), parity_n, p.wait_ns)) {
           fail_and_drain(k + 1);
           return epoch;
         }
@@ -1187,10 +1201,11 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     int t0 = 0, t1 = 0;
     if (lane == 0) {
       // An early add that beat the counter's re-tag was overwritten by it: arrive again.
-      t0 = early && uint32_t(early_old >> 32) == epoch
+      const uint32_t tag = counter_tag(epoch, p.tag_salt);
+      t0 = early && uint32_t(early_old >> 32) == tag
                ? int(uint32_t(early_old))
-               : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, epoch, p.err);
-      if (n_pend > 1) t1 = take_ticket(p.counters + int64_t(pend_b1) * items_per_row + pend_item1, epoch, p.err);
+               : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, tag, p.err, p.wait_ns);
+      if (n_pend > 1) t1 = take_ticket(p.counters + int64_t(pend_b1) * items_per_row + pend_item1, tag, p.err, p.wait_ns);
     }
     merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0));
     if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0));
@@ -1208,7 +1223,7 @@ __global__ void __launch_bounds__(CTA ? 288 : 256, 1)
   const uint32_t epoch = decode_body<T, D, GT, CTA, MMA>(p, kmap, vmap, smem);
   __syncwarp();
   if ((threadIdx.x & 31) == 0)
-    leave_launch(p.exit_counter, p.epoch_word, epoch, gridDim.x * (blockDim.x >> 5), p.err);
+    leave_launch(p.exit_counter, p.epoch_word, epoch, p.tag_salt, gridDim.x * (blockDim.x >> 5), p.err);
 }
 
 template <typename T, int D, int GT, bool CTA = false, bool MMA = false>

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 1)
   bool failed = false;
   for (int kt = 0; kt < ntiles; ++kt) {
     const int st = kt & 1;
-    if (!warp_wait_phase(smem_addr(bars + st), uint32_t((kt >> 1) & 1), WAIT_LIMIT_NS)) {
+    if (!warp_wait_phase(smem_addr(bars + st), uint32_t((kt >> 1) & 1), p.wait_ns)) {
       failed = true;
     }
     if (__syncthreads_or(failed)) {

@@ -111,6 +111,8 @@ _SIGNATURES = {
     "pd_get_decode_tuning": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 4),
     "pd_set_decode_mode": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "pd_get_decode_mode": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 3),
+    "pd_set_wait_limit": (ctypes.c_int, [ctypes.c_uint64]),
+    "pd_get_wait_limit": (ctypes.c_uint64, []),
 }
 
 #: Names exported by the library (the header's entry points); tests check all resolve.
@@ -216,6 +218,16 @@ def get_decode_mode() -> tuple[int, int, int]:
     vals = [_c_i32(0) for _ in range(3)]
     check(require().pd_get_decode_mode(*[ctypes.byref(v) for v in vals]), "pd_get_decode_mode")
     return tuple(int(v.value) for v in vals)
+
+
+def set_wait_limit(limit_ns: int) -> None:
+    """Limit of the kernels' stage and arrival-counter waits for later launches (0: the 1 s
+    default). A wait that runs out sets DEVERR_WAIT_TIMEOUT and the launch returns."""
+    check(require().pd_set_wait_limit(int(limit_ns)), "pd_set_wait_limit")
+
+
+def get_wait_limit() -> int:
+    return int(require().pd_get_wait_limit())
 
 
 def decode(q, k_cache, v_cache, block_table, seqlen, out, scale_log2, workspace) -> None:

@@ -207,8 +207,8 @@ def paged_prefill(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlen_k, max_
     varlen flash attention. Returns ``out`` shaped like ``q``.
 
     bf16 / fp16 pools, head_dim 64, 128 or 256, 1/2/4/8 q heads per kv head, block_size >= 8. The
-    reference's prefill never reads the paged cache; this is the block-table-aware prefill its
-    hot-path notes list as next work, with no reference counterpart to mirror.
+    reference has no counterpart to mirror: its packed varlen prefill (model/attention/varlen.py:
+    317-357, docs/decisions.md D7) writes the paged pool but never reads it.
     """
     _require_backend()
     _require_cuda_tensors((("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("block_table", block_table),

@@ -10,7 +10,7 @@ Everything here is computed by the reference's OWN functions, imported from its 
 ``tests/unit/test_triton_decode.py``, ``model/paged.py::PagedPool`` (CPU prefill writes),
 ``serve/block_manager.py::BlockManager`` and the seat path ``model/slab.py::KvSlab`` +
 ``model/attention/hand_baddbmm.py::HandBaddbmmBackend``. This repository's
-``serve/workloads.py`` is loaded by file path so its seeded recipes run against the
+``workloads.py`` (repository root) is loaded by file path so its seeded recipes run against the
 reference's allocator. Outputs (small) go to ``tests/golden/``; large inputs are not stored:
 the tests regenerate them from the recorded seeds and compare a SHA-256 of the bytes.
 """
@@ -86,7 +86,7 @@ def load_reference(root: Path):
 
 def load_workloads():
     spec = importlib.util.spec_from_file_location(
-        "repo_workloads", REPO / "llm-serving_b200" / "serve" / "workloads.py"
+        "repo_workloads", REPO / "workloads.py"
     )
     module = importlib.util.module_from_spec(spec)
     sys.modules["repo_workloads"] = module  # dataclasses resolve their module by name

@@ -72,3 +72,15 @@ def decode_mode(mode: int, shared_stages: int = 0, row_cost: int = -1):
         yield
     finally:
         _native.set_decode_mode(*before)
+
+
+def oracle_rows(oracle, q, k, v, table, seqlen, rows):
+    """fp32 oracle output of ``rows`` only, from a CPU copy of just the pool blocks those rows
+    use (the full pools of the large configs are GBs)."""
+    tab = table[rows].long()
+    ids = torch.unique(tab)
+    remap = torch.full((int(ids.max()) + 1,), -1, dtype=torch.long, device=tab.device)
+    remap[ids] = torch.arange(ids.numel(), device=tab.device)
+    local = remap[tab].to(torch.int32).cpu()
+    ref, _ = oracle.paged_decode(q[rows].cpu(), k[ids].cpu(), v[ids].cpu(), local, seqlen[rows].cpu())
+    return ref

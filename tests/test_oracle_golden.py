@@ -127,7 +127,7 @@ def test_oracle_conversion_rounds_like_torch(dtype):
 
 def test_seat_restatement_tracks_the_reference_seat_path():
     """The timed CPU baseline (gather + seat decode) against the reference's hand_baddbmm."""
-    import serve.workloads as workloads
+    import workloads
 
     rec = META["seat"]
     wl = workloads.config1(device="cpu", seed=0)

@@ -15,7 +15,7 @@ import math
 import pytest
 import torch
 
-from helpers import assert_output_close, build_case
+from helpers import assert_output_close, build_case, oracle_rows
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -93,7 +93,7 @@ def _check_workload(wl, rows=None):
 
 @pytest.mark.parametrize("name", ["config1", "config2", "config3", "config4"])
 def test_benchmark_configs_match_the_oracle(cuda_device, name):
-    from serve import workloads
+    import workloads
 
     kwargs = {"n_layer": 1} if name != "config2" else {"n_layer": 1}
     wl = getattr(workloads, name)(cuda_device, **kwargs)
@@ -102,14 +102,14 @@ def test_benchmark_configs_match_the_oracle(cuda_device, name):
 
 def test_qwen35_full_attention_shape_matches_the_oracle(cuda_device):
     """Hybrid Qwen3.5 full-attention layers: H=8, H_kv=2, D=256 (4 q heads per kv head)."""
-    from serve import workloads
+    import workloads
 
     wl = workloads.qwen35(cuda_device, n_layer=1, batch=8)
     _check_workload(wl)
 
 
 def test_config5_subset_and_checksum(cuda_device):
-    from serve import workloads
+    import workloads
 
     wl = workloads.config5(cuda_device)
     rows = torch.arange(0, 1024, 8)
@@ -122,11 +122,12 @@ def test_config5_subset_and_checksum(cuda_device):
 
 
 def test_config4_context_parallel_split_matches_the_whole(cuda_device):
-    """Config 4 (B=32 x 8192) split over 4 simulated ranks == the single-GPU decode."""
+    """Config 4 (B=32 x 8192) split over 4 simulated ranks: the merged output is within the
+    suite's tolerance of the fp32 oracle (on every 4th row) and close to the single-GPU decode."""
     from model import _native
     from model.parallel_decode import ContextParallelDecode
     from model.triton_decode import paged_decode
-    from serve import workloads
+    import workloads
 
     whole = workloads.config4(cuda_device)
     out_whole = paged_decode(whole.q[0], whole.k_pools[0], whole.v_pools[0], whole.block_table, whole.seqlen)
@@ -145,4 +146,8 @@ def test_config4_context_parallel_split_matches_the_whole(cuda_device):
     out = torch.empty_like(out_whole)
     _native.lse_merge(m_p, l_p, acc_p, out)
     torch.cuda.synchronize()
-    assert (out.float() - out_whole.float()).abs().max() < 4e-3
+    rows = torch.arange(0, B, 4)
+    ref = oracle_rows(oracle, whole.q[0], whole.k_pools[0], whole.v_pools[0], whole.block_table, whole.seqlen,
+                      rows)
+    assert_output_close(out[rows], ref, torch.bfloat16)
+    assert_output_close(out_whole[rows], ref, torch.bfloat16)

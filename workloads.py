@@ -18,6 +18,9 @@ the same allocator the engine uses, so fragmentation is what the serving stack p
   four q heads per kv head; 6 layers), B=32 rows at context 2048, block size 16.
 
 K/V/q are N(0, 1) in bf16 (scale 1/sqrt(D)). Large pools are drawn with a CUDA generator.
+
+This is benchmark and test input generation, not part of the library: ``bench.py`` and
+``tests/`` import it (with ``llm-serving_b200/`` on the import path for the block manager).
 """
 
 from __future__ import annotations
