@@ -23,11 +23,20 @@ second stream overlapping the neighbouring steps (two step graphs alternate);
 ``cpu_baseline`` = the reference's CPU gather + seat-decode path (ported, oracle/) on a
 bounded sample of the same workload using every host core.
 
+The same line carries the rest of the metric, each measured after the headline's timed region:
+``decode_step`` / ``decode_tok_s`` = config 2's whole decode step (a random-init Qwen3-0.6B
+around the same ``PagedKV`` calls, 64 greedy steps, CUDA graph per step) and the attention
+share of it; ``seat`` / ``paged_over_seat`` = the attention part of the config-2 step against
+the reference's seat (dense slab) step restated in torch, both as CUDA graphs; ``config5`` =
+1024 rows sharded by index over the ranks (strong scaling, no collective); ``config4_cp`` =
+32 x 8192 rows split by context over the ranks with one NCCL all-gather per layer-step,
+compute and collective timed apart. Both sharded blocks carry an fp32 parity field.
+
 ``--impl reference`` times that CPU port alone (the reference's own CPU implementation of this
 path; rank 0 only) and prints the same line with ``"impl": "reference"``.
 
-Multi-GPU (``torchrun --nproc-per-node N``): rows shard by sequence with no collective, so
-every rank decodes its own B=32 batch (weak scaling); time is the max over ranks.
+Multi-GPU (``torchrun --nproc-per-node N``): for the headline, rows shard by sequence with no
+collective, so every rank decodes its own B=32 batch (weak scaling); time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -244,6 +253,17 @@ def run_gpu(args) -> dict | None:
 
     # ---- end to end through the public API with host buffers ---------------------------
     e2e = _run_e2e(kv, graph, device, stream, rank, steps, dist)
+    del graph, kv, q_buf, k_buf, v_buf
+    torch.cuda.empty_cache()
+
+    # ---- the rest of the metric: config 2's whole decode step, the paged/seat step ratio,
+    # and the two sharded configs (every rank takes the same collective steps in order)
+    decode_step = run_decode_step(device, rank, dist)
+    decode_step["attention_share"] = round((ms / steps) / decode_step["ms_per_step"], 3)
+    sharded_reps = max(5, min(steps, 20))
+    config5 = run_config5(device, rank, world, dist, reps=sharded_reps)
+    config4_cp = run_config4_cp(device, rank, world, dist, steps=sharded_reps)
+    seat = seat_case(device, "config2_b32_ctx2048", [CONTEXT] * BATCH) if rank == 0 else None
 
     if rank != 0:
         _finish(dist)
@@ -289,6 +309,12 @@ def run_gpu(args) -> dict | None:
         "e2e": e2e,
         "gpu_launches": launches,
         "clocks": clocks.summary(),
+        "decode_tok_s": decode_step["decode_tok_s"],
+        "decode_step": decode_step,
+        "paged_over_seat": seat["paged_over_seat"],
+        "seat": seat,
+        "config5": config5,
+        "config4_cp": config4_cp,
     }
     line["cpu_baseline"] = cpu_baseline(sample_layers=args.cpu_sample_layers)
     _finish(dist)
@@ -371,6 +397,244 @@ def _finish(dist):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------ sharded configs
+
+
+def _fp32_attention(q, keys, values) -> torch.Tensor:
+    """softmax(q K^T / sqrt(D)) V in fp32 for one row: q (H, D), keys/values (L, H_kv, D) -- the
+    arithmetic of the reference's reference_paged_decode (tests/reference/paged.py:225-274) in
+    torch on the device, as the bench line's own parity field."""
+    h, d = q.shape
+    hkv = keys.shape[1]
+    qg = q.float().view(hkv, h // hkv, d)
+    scores = torch.einsum("kgd,tkd->kgt", qg, keys.float()) / math.sqrt(d)
+    probs = torch.softmax(scores, dim=-1)
+    return torch.einsum("kgt,tkd->kgd", probs, values.float()).reshape(h, d)
+
+
+def _max_abs_vs_fp32_rows(q, k_pool, v_pool, table, seqlen, rows, out) -> float:
+    """Largest |out - fp32 reference| over ``rows`` of a paged decode (rows gathered through the
+    block table)."""
+    bs, hkv, d = k_pool.shape[1], k_pool.shape[2], k_pool.shape[3]
+    worst = 0.0
+    for r in rows.tolist():
+        n = int(seqlen[r])
+        blocks = table[r, :-(-n // bs)].long()
+        keys = k_pool[blocks].reshape(-1, hkv, d)[:n]
+        values = v_pool[blocks].reshape(-1, hkv, d)[:n]
+        ref = _fp32_attention(q[r], keys, values)
+        worst = max(worst, (out[r].float() - ref).abs().max().item())
+    return worst
+
+
+def _time_replays(fn, reps: int, stream) -> float:
+    """Device time in ms of ``reps`` back-to-back calls of ``fn`` (CUDA events on ``stream``)."""
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        fn()
+    stop.record(stream)
+    stop.synchronize()
+    return start.elapsed_time(stop)
+
+
+def run_config5(device, rank: int, world: int, dist, reps: int) -> dict:
+    """1024 rows, L ~ U[256, 4096], sharded by row index over the ranks (each
+    its own pool, table and seqlen; no collective on the data path), strong scaling. Two layers
+    with distinct pools (each layer's K/V larger than L2 at every world size) are launched back
+    to back in a CUDA graph, the second overlapping the first; ``reps`` replays are timed."""
+    from model import _native
+    from model.triton_decode import paged_decode_plan
+    import workloads
+
+    n_layer = 2
+    wl = workloads.config5(device, rank=rank, world=world, n_layer=n_layer)
+    plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
+    outs = [torch.empty_like(q) for q in wl.q]
+    graph = torch.cuda.CUDAGraph()
+    for layer in range(n_layer):
+        plan.run(layer, wl.q[layer], out=outs[layer])
+    torch.cuda.synchronize(device)
+    with torch.cuda.graph(graph):
+        for layer in range(n_layer):
+            plan.run(layer, wl.q[layer], out=outs[layer], overlap=layer > 0)
+    stream = torch.cuda.current_stream(device)
+    graph.replay()
+    _barrier(dist, device)
+    ms_local = _time_replays(graph.replay, reps, stream)
+    _barrier(dist, device)
+    assert _native.device_error() == 0, "device error word set in config 5"
+    kv_local = wl.kv_bytes_per_layer() * n_layer * reps
+    ms = _max_over_ranks(dist, ms_local, device)
+    total = _sum_over_ranks(dist, float(kv_local), device)
+    gbs_local = kv_local / (ms_local * 1e-3) / 1e9
+    gbs_min = -_max_over_ranks(dist, -gbs_local, device)
+    # parity of the device's output: a subset of this rank's rows against an fp32 reference
+    rows = torch.arange(0, wl.q[0].shape[0], max(1, wl.q[0].shape[0] // 8))
+    err = _max_abs_vs_fp32_rows(wl.q[0], wl.k_pools[0], wl.v_pools[0], wl.block_table, wl.seqlen, rows, outs[0])
+    err = _max_over_ranks(dist, err, device)
+    peak = _peaks()["hbm_gbs"]
+    line = {
+        "workload": "BASELINE configs[4]: 1024 rows, L~U[256,4096], Qwen3-0.6B heads, bf16, rows sharded by "
+                    "index over the ranks (own pool/table per rank, no collective); strong scaling",
+        "rows_per_gpu": int(wl.q[0].shape[0]), "layers_per_replay": n_layer, "replays": reps,
+        "us_per_layer_step": round(ms * 1e3 / (reps * n_layer), 2),
+        "aggregate_kv_gbs": round(total / (ms * 1e-3) / 1e9, 1),
+        "kv_gbs_per_gpu_min": round(gbs_min, 1),
+        "roofline_frac_per_gpu_min": round(gbs_min / peak, 4),
+        "max_abs_vs_fp32_reference": err, "checked_rows_per_gpu": int(rows.numel()),
+        "timing": "CUDA events around the replays, max over ranks; per-GPU GB/s = that rank's KV bytes / its time",
+    }
+    del graph, plan, wl, outs
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_config4_cp(device, rank: int, world: int, dist, steps: int) -> dict:
+    """BASELINE config 4, context parallel: B=32 rows of 8192 tokens; rank r owns the contiguous
+    8192 / world token slice of every row (its own pool and table). Per layer and step, inside
+    the timed region: one ``pd_decode_partials`` launch over the slice, ONE NCCL
+    ``all_gather_into_tensor`` of the packed fp32 (acc | m | l) buffer, one ``pd_lse_merge``
+    (every rank ends with the full output). Four layers with distinct pools per step. CUDA
+    events separate compute (partials + merge) from the collective; each is the max over
+    ranks. The merged output of a row subset is checked against an fp32 reference over the
+    whole 8192-token rows in fp32 (their slices all-gathered to every rank, outside the timed
+    region)."""
+    from model import _native
+    from model.parallel_decode import ContextParallelDecode
+    import workloads
+
+    n_layer, B, ctx = 4, BATCH, 8192
+    wl = workloads.config4(device, n_layer=n_layer, rank=rank, world=world)
+    gen = torch.Generator(device=device).manual_seed(4444)  # q is the same on every rank
+    qs = [torch.randn(B, H, D, generator=gen, device=device).to(torch.bfloat16) for _ in range(n_layer)]
+    outs = [torch.empty_like(q) for q in qs]
+    cp = ContextParallelDecode()
+    scale = 1.0 / math.sqrt(D)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_layer * steps)]
+
+    def step(ev=None):
+        for layer in range(n_layer):
+            cp(qs[layer], wl.k_pools[layer], wl.v_pools[layer], wl.block_table, wl.seqlen, scale=scale,
+               out=outs[layer], events=None if ev is None else ev[layer])
+
+    for _ in range(3):
+        step()
+    stream = torch.cuda.current_stream(device)
+    _barrier(dist, device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        step(events[i * n_layer:(i + 1) * n_layer])
+    stop.record(stream)
+    _barrier(dist, device)
+    assert _native.device_error() == 0, "device error word set in config 4"
+    ms_local = start.elapsed_time(stop)
+    compute = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in events)
+    collective = sum(e[1].elapsed_time(e[2]) for e in events)
+    ms = _max_over_ranks(dist, ms_local, device)
+    compute_max = _max_over_ranks(dist, compute, device)
+    collective_max = _max_over_ranks(dist, collective, device)
+    kv_local = wl.kv_bytes_per_layer() * n_layer * steps
+    total = _sum_over_ranks(dist, float(kv_local), device)
+    layer_steps = n_layer * steps
+
+    # parity: rows 0, 8, 16, 24 of layer 0, whole 8192-token rows gathered from every rank's slice
+    rows = list(range(0, B, 8))
+    span = ctx // world
+    pages = span // BS
+    kk = torch.stack([wl.k_pools[0][wl.block_table[r, :pages].long()] for r in rows])  # (R, pages, bs, Hkv, D)
+    vv = torch.stack([wl.v_pools[0][wl.block_table[r, :pages].long()] for r in rows])
+    if dist is not None:
+        kk_all = torch.empty((world,) + tuple(kk.shape), dtype=kk.dtype, device=device)
+        vv_all = torch.empty_like(kk_all)
+        dist.all_gather_into_tensor(kk_all, kk.contiguous())
+        dist.all_gather_into_tensor(vv_all, vv.contiguous())
+        kk = kk_all.permute(1, 0, 2, 3, 4, 5).reshape(len(rows), world * pages, BS, H_KV, D)
+        vv = vv_all.permute(1, 0, 2, 3, 4, 5).reshape(len(rows), world * pages, BS, H_KV, D)
+    err = 0.0
+    for i, r in enumerate(rows):
+        ref = _fp32_attention(qs[0][r], kk[i].reshape(-1, H_KV, D), vv[i].reshape(-1, H_KV, D))
+        err = max(err, (outs[0][r].float() - ref).abs().max().item())
+    err = _max_over_ranks(dist, err, device)
+    identical = True
+    if dist is not None:
+        mine = outs[0].contiguous()
+        everyone = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=device)
+        dist.all_gather_into_tensor(everyone, mine)
+        identical = all(torch.equal(everyone[0], everyone[r]) for r in range(world))
+    peak = _peaks()["hbm_gbs"]
+    compute_us = compute_max * 1e3 / layer_steps
+    line = {
+        "workload": "BASELINE configs[3] context-parallel: B=32 x 8192 tokens, Qwen3-0.6B heads, bf16; each rank "
+                    "owns 8192/N tokens of every row; pd_decode_partials + one NCCL all_gather_into_tensor of "
+                    "(acc|m|l) + pd_lse_merge per layer-step",
+        "tokens_per_gpu_per_row": span, "layers_per_step": n_layer, "steps": steps,
+        "us_per_layer_step": round(ms * 1e3 / layer_steps, 2),
+        "compute_us_per_layer_step": round(compute_us, 2),
+        "allgather_us_per_layer_step": round(collective_max * 1e3 / layer_steps, 2),
+        "allgather_bytes_per_rank": B * H * (D + 2) * 4,
+        "aggregate_kv_gbs": round(total / (ms * 1e-3) / 1e9, 1),
+        "compute_kv_gbs_per_gpu": round(kv_local / layer_steps / (compute_us * 1e-6) / 1e9, 1),
+        "compute_roofline_frac_per_gpu": round(kv_local / layer_steps / (compute_us * 1e-6) / 1e9 / peak, 4),
+        "limiter": "allgather" if collective_max > compute_max else "compute",
+        "max_abs_vs_fp32_reference": err, "checked_rows": rows, "identical_on_all_ranks": identical,
+        "timing": "CUDA events on the launching stream around each stage, summed, max over ranks",
+    }
+    del wl, qs, outs, cp, kk, vv
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_decode_step(device, rank: int, dist, steps: int = NEW_TOKENS) -> dict:
+    """BASELINE config 2's whole decode step: a random-init Qwen3-0.6B-shaped model
+    (``decode_model.PagedDecoder``: 28 layers of norms, projections, RoPE, SwiGLU; tied lm_head
+    and greedy argmax) whose attention is ``PagedKV.write`` + ``attend`` (the fused sm_100a
+    append + decode, K rotated in the append, layers overlapped). B=32 rows at context 2048
+    (K/V of the prompts drawn N(0, 1)), greedy for ``steps`` steps; the step is captured once
+    as a CUDA graph and every timed step is one replay (next token = this step's argmax on
+    the device)."""
+    from decode_model import PagedDecoder
+    from model import _native
+    from serve.graph import DecodeStepGraph
+
+    warm = 3
+    budget = steps + warm + 2 + 1
+    kv = _container(device, budget, seed=100 + rank)
+    model = PagedDecoder(kv, n_layer=N_LAYER, n_head=H, n_kv_head=H_KV, head_dim=D, rotary=D,
+                         max_pos=CONTEXT + budget + 1, seed=7, device=device)
+    gen = torch.Generator(device=device).manual_seed(8 + rank)
+    model.tok.copy_(torch.randint(0, 151936, (BATCH,), generator=gen, device=device))
+    with torch.no_grad():
+        for _ in range(warm):
+            kv.build_mask(next_token=True)
+            model.step()
+            kv.advance()
+        graph = DecodeStepGraph(kv, model.step, model.prepare_q)
+        for _ in range(2):
+            graph.replay()
+        stream = torch.cuda.current_stream(device)
+        _barrier(dist, device)
+        ms_local = _time_replays(graph.replay, steps, stream)
+        _barrier(dist, device)
+    assert _native.device_error() == 0, "device error word set in the decode step"
+    ms = _max_over_ranks(dist, ms_local, device)
+    world = 1 if dist is None else dist.get_world_size()
+    line = {
+        "workload": "BASELINE configs[1] whole decode step: random-init Qwen3-0.6B (28 layers, hidden 1024, "
+                    "16q/8kv, D=128, SwiGLU 3072, vocab 151936, tied lm_head), B=32 at context 2048, "
+                    f"{steps} greedy steps, attention through PagedKV; CUDA graph per step",
+        "decode_tok_s": round(world * BATCH * steps / (ms * 1e-3), 1),
+        "ms_per_step": round(ms / steps, 4),
+        "steps": steps, "context": f"{CONTEXT + warm + 2}..{CONTEXT + warm + 2 + steps}",
+        "library_launches_per_step": graph.launches_per_step,
+        "reference_decode_only_tok_s_rtx4090": 1230.5,
+    }
+    del graph, model, kv
+    torch.cuda.empty_cache()
+    return line
 
 
 # ------------------------------------------------------------------------------ CPU arm
@@ -635,80 +899,87 @@ class _SeatStep:
         self.pos += 1
 
 
-def seat_sweep(reps: int = 10) -> None:
+def seat_case(device, name: str, lengths: list[int], reps: int = 10) -> dict:
     """Decode-step cost of the paged arm against the seat arm at Qwen3-0.6B head shapes, both
     steps (28 layers of K/V append + attention, with the step's bookkeeping) captured once as
-    CUDA graphs and replayed, best of ``reps`` replays. Cases: config 2 (B=32 at 2048 tokens)
-    and the reference's own paged/seat comparison size (B=8, contexts up to 1645 tokens;
-    seeded uniform in [1024, 1645] here). One JSON line per case (not the bench line)."""
+    CUDA graphs and replayed, best of ``reps`` replays, for rows of the given lengths."""
     from model import _native
     from model.paged import PagedKV, PagedPool
     from serve.block_manager import BlockManager
     from serve.graph import PagedStepGraph
 
-    device = torch.device("cuda", 0)
     eager, budget = 3, 3 + 2 + reps + 2
-    for name, lengths in (("config2_b32_ctx2048", [CONTEXT] * BATCH),
-                          ("b8_ctx1024_1645", torch.randint(1024, 1646, (8,), generator=torch.Generator().manual_seed(5)).tolist())):
-        B = len(lengths)
-        gen = torch.Generator(device=device).manual_seed(21)
-        q_buf = torch.randn(N_LAYER, B, H, 1, D, generator=gen, device=device).to(torch.bfloat16)
-        k_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
-        v_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    B = len(lengths)
+    gen = torch.Generator(device=device).manual_seed(21)
+    q_buf = torch.randn(N_LAYER, B, H, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    k_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    v_buf = torch.randn(N_LAYER, B, H_KV, 1, D, generator=gen, device=device).to(torch.bfloat16)
 
-        def timed(replay) -> list[float]:
-            times = []
-            for _ in range(reps):
-                start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                start.record()
-                replay()
-                stop.record()
-                torch.cuda.synchronize(device)
-                times.append(start.elapsed_time(stop) * 1e3 / N_LAYER)
-            return times
+    def timed(replay) -> list[float]:
+        times = []
+        for _ in range(reps):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            replay()
+            stop.record()
+            torch.cuda.synchronize(device)
+            times.append(start.elapsed_time(stop) * 1e3 / N_LAYER)
+        return times
 
-        manager = BlockManager(sum(-(-(n + budget) // BS) for n in lengths), BS)
-        tables = [manager.reserve(manager.blocks_for(n, budget)) for n in lengths]
-        pool = PagedPool(N_LAYER, manager.n_blocks, BS, H_KV, D, dtype=torch.bfloat16, device=device, n_head=H)
-        for t in pool.keys + pool.values:
-            t.copy_(torch.randn(t.shape, generator=gen, device=device))
-        kv = PagedKV(pool, tables, lengths, rope_len=max(lengths) + budget, n_head=H)
-        for _ in range(eager):
-            kv.build_mask(next_token=True)
-            for layer in range(N_LAYER):
-                kv.write(layer, k_buf[layer], v_buf[layer])
-                kv.attend(layer, q_buf[layer])
-            kv.advance()
-        graph = PagedStepGraph(kv, q_buf, k_buf, v_buf)
-        for _ in range(2):
-            graph.replay()
-        paged = timed(graph.replay)
-        if _native.device_error() != 0:
-            raise SystemExit(f"{name}: device error word set")
-        del graph, kv, pool
-        torch.cuda.empty_cache()
+    manager = BlockManager(sum(-(-(n + budget) // BS) for n in lengths), BS)
+    tables = [manager.reserve(manager.blocks_for(n, budget)) for n in lengths]
+    pool = PagedPool(N_LAYER, manager.n_blocks, BS, H_KV, D, dtype=torch.bfloat16, device=device, n_head=H)
+    for t in pool.keys + pool.values:
+        t.copy_(torch.randn(t.shape, generator=gen, device=device))
+    kv = PagedKV(pool, tables, lengths, rope_len=max(lengths) + budget, n_head=H)
+    for _ in range(eager):
+        kv.build_mask(next_token=True)
+        for layer in range(N_LAYER):
+            kv.write(layer, k_buf[layer], v_buf[layer])
+            kv.attend(layer, q_buf[layer])
+        kv.advance()
+    graph = PagedStepGraph(kv, q_buf, k_buf, v_buf)
+    for _ in range(2):
+        graph.replay()
+    paged = timed(graph.replay)
+    if _native.device_error() != 0:
+        raise SystemExit(f"{name}: device error word set")
+    del graph, kv, pool
+    torch.cuda.empty_cache()
 
-        seat = _SeatStep(device, lengths, budget, gen)
-        for _ in range(eager):
-            seat.step(q_buf, k_buf, v_buf)
-        torch.cuda.synchronize(device)
-        seat_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(seat_graph):
-            seat.step(q_buf, k_buf, v_buf)
-        for _ in range(2):
-            seat_graph.replay()
-        seat_times = timed(seat_graph.replay)
-        print(json.dumps({
-            "seat_case": name, "rows": B, "contexts": f"{min(lengths)}..{max(lengths)} (+step)",
-            "layers": N_LAYER, "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
-            "paged_us_per_layer_step": round(min(paged), 2), "seat_us_per_layer_step": round(min(seat_times), 2),
-            "paged_over_seat": round(min(paged) / min(seat_times), 3),
-            "paged_median": round(statistics.median(paged), 2), "seat_median": round(statistics.median(seat_times), 2),
-            "seat_slab_width": seat.width,
-            "note": "attention part of the decode step (append + attention + step bookkeeping), both arms as "
-                    "CUDA graphs; the reference's own paged/seat figure is a whole-model step"}), flush=True)
-        del seat_graph, seat
-        torch.cuda.empty_cache()
+    seat = _SeatStep(device, lengths, budget, gen)
+    for _ in range(eager):
+        seat.step(q_buf, k_buf, v_buf)
+    torch.cuda.synchronize(device)
+    seat_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(seat_graph):
+        seat.step(q_buf, k_buf, v_buf)
+    for _ in range(2):
+        seat_graph.replay()
+    seat_times = timed(seat_graph.replay)
+    line = {
+        "seat_case": name, "rows": B, "contexts": f"{min(lengths)}..{max(lengths)} (+step)",
+        "layers": N_LAYER, "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
+        "paged_us_per_layer_step": round(min(paged), 2), "seat_us_per_layer_step": round(min(seat_times), 2),
+        "paged_over_seat": round(min(paged) / min(seat_times), 3),
+        "paged_median": round(statistics.median(paged), 2), "seat_median": round(statistics.median(seat_times), 2),
+        "seat_slab_width": seat.width,
+        "note": "attention part of the decode step (append + attention + step bookkeeping), both arms as "
+                "CUDA graphs; the reference's own paged/seat figure is a whole-model step"}
+    del seat_graph, seat
+    torch.cuda.empty_cache()
+    return line
+
+
+def seat_sweep(reps: int = 10) -> None:
+    """:func:`seat_case` for config 2 (B=32 at 2048 tokens) and the reference's own paged/seat
+    comparison size (B=8, contexts up to 1645 tokens; seeded uniform in [1024, 1645] here). One
+    JSON line per case (not the bench line)."""
+    device = torch.device("cuda", 0)
+    cases = (("config2_b32_ctx2048", [CONTEXT] * BATCH),
+             ("b8_ctx1024_1645", torch.randint(1024, 1646, (8,), generator=torch.Generator().manual_seed(5)).tolist()))
+    for name, lengths in cases:
+        print(json.dumps(seat_case(device, name, lengths, reps)), flush=True)
 
 
 def main(argv=None) -> int:

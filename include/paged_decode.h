@@ -331,9 +331,9 @@ int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost)
  * at most 10 s). A wait that runs out records PD_DEVERR_WAIT_TIMEOUT in the device error word,
  * waits for its own copies still in flight (always with a fixed 0.1 s limit) and returns, so
  * the launch ends and the context stays usable; outputs of that launch are then unspecified.
- * A limit below 1000 ns makes a stage wait probe once without blocking and give up if the copy
- * has not landed yet, so the waits run out on purpose: that is how a test exercises this error
- * path without a hang or a fault. No reference counterpart (its kernel has no waits). */
+ * Under a limit below 1000 ns every such wait gives up at once, complete or not: that is how a
+ * test runs this error path deterministically, without a hang or a fault. No reference
+ * counterpart (its kernel has no waits). */
 int pd_set_wait_limit(uint64_t limit_ns);
 uint64_t pd_get_wait_limit(void);
 

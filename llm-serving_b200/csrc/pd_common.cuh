@@ -71,29 +71,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking probe of the phase with the given parity.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred P1;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, P1;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Limits below this are test limits (pd_set_wait_limit): the wait then probes once without
-// blocking and gives up if the phase is not complete, so that a copy still in flight makes it
-// run out deterministically.
-constexpr unsigned long long PROBE_LIMIT_NS = 1000ull;
+// Limits below this are test limits (pd_set_wait_limit): every wait under such a limit gives
+// up at once, whether or not its phase is complete, so a test can run the error path
+// deterministically (the drains after it use DRAIN_LIMIT_NS and always finish).
+constexpr unsigned long long TEST_LIMIT_NS = 1000ull;
 
 // Warp-collective bounded wait: returns true once every lane has observed the phase with
 // the given parity complete, false (uniformly) once `limit_ns` has elapsed.
 __device__ __forceinline__ bool warp_wait_phase(uint32_t bar, uint32_t parity,
                                                 unsigned long long limit_ns) {
-  if (limit_ns < PROBE_LIMIT_NS) return __all_sync(FULL_MASK, mbar_test_wait(bar, parity));
+  if (limit_ns < TEST_LIMIT_NS) return false;
   bool done = mbar_try_wait(bar, parity);
   if (__all_sync(FULL_MASK, done)) return true;
   unsigned long long start = global_timer_ns();

@@ -160,7 +160,7 @@ __device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t
     const unsigned long long old = atomicAdd(counter, 1ull);  // callers fence before arriving
     if (uint32_t(old >> 32) == tag) return int(uint32_t(old));
     const unsigned long long now = global_timer_ns();
-    if (t0 == 0) {
+    if (t0 == 0 && limit_ns >= TEST_LIMIT_NS) {
       t0 = now;
     } else if (now - t0 > limit_ns) {
       atomicOr(err, DEVERR_WAIT_TIMEOUT);

@@ -52,26 +52,34 @@ class ContextParallelDecode:
 
     ``partials`` and ``merge`` default to the sm_100a kernels; a test on CPU ranks may pass
     callables with the same signatures (this is how the gloo tests drive the exchange logic).
+    Without an initialised process group the object stands for a world of one: the step is the
+    partials launch and the merge of that single part, with no collective.
+
+    Every buffer (the send and gathered partials, the workspace and, unless the caller passes
+    ``out``, the result) is allocated on the first call and reused while the shape stays, so a
+    steady decode loop allocates nothing and its step can be captured in a CUDA graph (the
+    NCCL all-gather included, as torch supports).
     """
 
     def __init__(self, group=None, *, partials: Callable | None = None, merge: Callable | None = None):
         import torch.distributed as dist
 
-        self.dist = dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = self.dist.get_world_size(group) if self.dist is not None else 1
+        self.rank = self.dist.get_rank(group) if self.dist is not None else 0
         self._partials = partials or self._native_partials
         self._merge = merge or self._native_merge
         self._workspace: torch.Tensor | None = None
         self._send: torch.Tensor | None = None
         self._recv: torch.Tensor | None = None
+        self._out: torch.Tensor | None = None
 
     # ---------------------------------------------------------------- default kernels
     def _native_partials(self, q, k_cache, v_cache, block_table, seqlen, m, l, acc, scale):
         B, H, D = q.shape
         need = _native.workspace_bytes(B, H, k_cache.shape[2], D, q.dtype)
-        if self._workspace is None or self._workspace.numel() < need:
+        if self._workspace is None or self._workspace.numel() < need or self._workspace.device != q.device:
             self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
         _native.decode_partials(q, k_cache, v_cache, block_table, seqlen, m, l, acc, scale * _LOG2E,
                                 self._workspace)
@@ -82,10 +90,13 @@ class ContextParallelDecode:
 
     # ---------------------------------------------------------------- step
     def buffers(self, B: int, H: int, D: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """The packed send buffer of this rank and the gathered buffer of all ranks (the same
+        tensor in a world of one)."""
         n = B * H * (D + 2)
         if self._send is None or self._send.numel() != n or self._send.device != torch.device(device):
             self._send = torch.empty(n, dtype=torch.float32, device=device)
-            self._recv = torch.empty(self.world * n, dtype=torch.float32, device=device)
+            self._recv = (self._send if self.world == 1
+                          else torch.empty(self.world * n, dtype=torch.float32, device=device))
         return self._send, self._recv
 
     @staticmethod
@@ -101,17 +112,33 @@ class ContextParallelDecode:
         return acc, m, l
 
     def __call__(self, q, k_cache, v_cache, block_table, local_seqlen, *, scale: float | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-        """``q`` (B, H, D) is the same on every rank; ``local_seqlen`` counts this rank's tokens."""
+                 out: torch.Tensor | None = None, events=None) -> torch.Tensor:
+        """``q`` (B, H, D) is the same on every rank; ``local_seqlen`` counts this rank's tokens.
+
+        ``events`` (optional): four CUDA events recorded on the current stream before the
+        partials launch, after it, after the all-gather and after the merge, so a caller can
+        time the compute and the collective apart."""
         B, H, D = q.shape
         if scale is None:
             scale = 1.0 / math.sqrt(D)
         send, recv = self.buffers(B, H, D, q.device)
         acc, m, l = self.views(send, B, H, D)
+        if events is not None:
+            events[0].record()
         self._partials(q, k_cache, v_cache, block_table, local_seqlen, m, l, acc, scale)
-        self.dist.all_gather_into_tensor(recv, send, group=self.group)
+        if events is not None:
+            events[1].record()
+        if self.world > 1:
+            self.dist.all_gather_into_tensor(recv, send, group=self.group)
+        if events is not None:
+            events[2].record()
         acc_p, m_p, l_p = self.views(recv, B, H, D, parts=self.world)
         if out is None:
-            out = torch.empty_like(q)
+            if (self._out is None or self._out.shape != q.shape or self._out.dtype != q.dtype
+                    or self._out.device != q.device):
+                self._out = torch.empty_like(q)
+            out = self._out
         self._merge(m_p, l_p, acc_p, out)
+        if events is not None:
+            events[3].record()
         return out

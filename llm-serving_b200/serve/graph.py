@@ -1,11 +1,12 @@
-"""CUDA-graph capture of the paged decode step's attention.
+"""CUDA-graph capture of a paged decode step: its attention alone, or the whole model's step.
 
 One decode step of the engine's paged arm issues, per step, ``build_mask`` (``seqlen :=
 pos + 1``), then for every layer ``PagedKV.write`` + ``PagedKV.attend`` (one fused append +
 decode launch each), then ``advance``. The Python work around those launches costs about as
 much host time per layer as the kernel takes on the GPU, so an eager step can leave the GPU
 waiting. :class:`PagedStepGraph` captures the step once and replays it: one graph launch per
-step, the GPU never waits on Python.
+step, the GPU never waits on Python. :class:`DecodeStepGraph` does the same for a whole
+model's step (projections, norms, MLP, sampling) around the same container calls.
 
 Capture is possible because everything the step touches has a stable address: the pools,
 the int32 block table and seqlen, the int64 ``pos``/``valid``/``active`` tensors (all updated
@@ -26,7 +27,46 @@ import torch
 from model import _native
 from model.paged import PagedKV
 
-__all__ = ["PagedStepGraph"]
+__all__ = ["PagedStepGraph", "DecodeStepGraph"]
+
+
+class DecodeStepGraph:
+    """One captured decode step of a whole model that drives a :class:`PagedKV` container.
+
+    ``body()`` issues the step's device work between ``build_mask`` and ``advance``: every
+    layer's projections, ``kv.write`` / ``kv.attend`` and the rest of the model, reading and
+    writing only tensors with stable addresses (inputs the caller refills before each
+    :meth:`replay`, outputs it reads after). ``prepare`` is a query-shaped tensor for the
+    container's decode plan (``(B, H, 1, D)``, any contents). The container's host-side
+    bookkeeping runs around each replay, as in :class:`PagedStepGraph`.
+    """
+
+    def __init__(self, kv: PagedKV, body, prepare: torch.Tensor, *, next_token: bool = True) -> None:
+        if not isinstance(kv, PagedKV):
+            raise TypeError(f"DecodeStepGraph needs a PagedKV, got {type(kv).__name__}")
+        self.kv = kv
+        self.next_token = bool(next_token)
+        kv.pool.flush()
+        kv.prepare(prepare)
+        torch.cuda.synchronize(prepare.device)
+        snapshot = kv._host_snapshot()
+        self.graph = torch.cuda.CUDAGraph()
+        before = _native.launch_count()
+        try:
+            with torch.cuda.graph(self.graph):
+                kv.build_mask(next_token=self.next_token)
+                body()
+                kv.advance()
+        finally:
+            kv._host_restore(snapshot)
+        #: Library kernels launched by one replay.
+        self.launches_per_step = _native.launch_count() - before
+
+    def replay(self) -> None:
+        kv = self.kv
+        kv._replayed_step(self.next_token)
+        self.graph.replay()
+        kv._replayed_advance()
 
 
 class PagedStepGraph:

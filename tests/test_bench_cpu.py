@@ -43,3 +43,19 @@ def test_seat_step_appends_at_pos_and_attends_over_the_allowed_columns():
 def test_fewer_than_three_warmup_steps_are_refused():
     with pytest.raises(SystemExit, match="warmup"):
         bench.main(["--warmup", "2"])
+
+
+def test_bench_parity_reference_equals_the_oracle():
+    """The bench line's own parity field (an fp32 torch restatement of the reference's
+    reference_paged_decode) agrees with the pinned oracle on a paged case."""
+    from helpers import build_case
+    from oracle import oracle
+
+    q, k, v, table, seqlen = build_case(3, 16, 8, 128, 16, [40, 300, 17], dtype=torch.bfloat16, seed=4)
+    ref, _ = oracle.paged_decode(q, k, v, table, seqlen)
+    got = torch.stack([
+        bench._fp32_attention(q[r], k[table[r, :-(-int(seqlen[r]) // 16)].long()].reshape(-1, 8, 128)[:int(seqlen[r])],
+                              v[table[r, :-(-int(seqlen[r]) // 16)].long()].reshape(-1, 8, 128)[:int(seqlen[r])])
+        for r in range(3)])
+    assert (got - ref).abs().max().item() < 1e-5
+    assert bench._max_abs_vs_fp32_rows(q, k, v, table, seqlen, torch.arange(3), ref) < 1e-5

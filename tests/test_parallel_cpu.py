@@ -158,3 +158,33 @@ def test_shard_helpers_tile_their_ranges():
         assert all(lo % 16 == 0 for lo, _ in spans)
     with pytest.raises(ValueError):
         shard_rows(8, 3, 2)
+
+
+def test_a_world_of_one_merges_its_single_part_without_a_process_group():
+    """Without an initialised process group the context-parallel step is the partials of the
+    whole rows and the merge of that one part (no collective), and it reuses its buffers."""
+    sys.path.insert(0, str(ROOT / "llm-serving_b200"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    from helpers import build_case
+    from model.parallel_decode import ContextParallelDecode
+    from oracle import oracle
+
+    q, k, v, table, seqlen = build_case(4, 8, 2, 32, 16, [100, 0, 33, 64], seed=3)
+    whole, _ = oracle.paged_decode(q, k, v, table, seqlen)
+
+    def partials(q_, k_, v_, table_, seqlen_, m, l, acc, scale):
+        mm, ll, aa = oracle.decode_partials(q_, k_, v_, table_, seqlen_, scale=scale)
+        m.copy_(mm), l.copy_(ll), acc.copy_(aa)
+
+    def merge(m_p, l_p, acc_p, out):
+        merged, _ = oracle.lse_merge(m_p.contiguous(), l_p.contiguous(), acc_p.contiguous())
+        out.copy_(merged)
+
+    cp = ContextParallelDecode(partials=partials, merge=merge)
+    assert cp.world == 1 and cp.dist is None
+    first = cp(q, k, v, table, seqlen)
+    send, recv = cp.buffers(*q.shape, q.device)
+    assert recv is send
+    again = cp(q, k, v, table, seqlen)
+    assert again is first  # the result buffer is reused
+    assert (again - whole).abs().max().item() < 2e-6
