@@ -800,12 +800,24 @@ def prefill_sweep(reps: int = 5) -> None:
     the Qwen3.5 full-attention heads, 8q/2kv, head_dim 256): each
     layer's launch once per replay of a CUDA graph, distinct per-layer pools (larger than L2),
     best of ``reps`` replays. FLOPs are the causal ones: 4 * D per visible (query, key) pair per
-    q head. One JSON line per case (not the bench line)."""
+    q head. Each case runs on both prefill kernels (tcgen05 / TMEM, the default, and the
+    mma.sync kernel). One JSON line per case and kernel (not the bench line)."""
     from model import _native
-    from model.triton_decode import paged_prefill
 
     device = torch.device("cuda", 0)
     peaks = _peaks()
+    for mode, kernel in ((0, "tcgen05"), (1, "mma_sync")):
+        _native.set_prefill_mode(mode)
+        try:
+            _prefill_cases(device, peaks, reps, kernel)
+        finally:
+            _native.set_prefill_mode(0)
+
+
+def _prefill_cases(device, peaks, reps, kernel) -> None:
+    from model import _native
+    from model.triton_decode import paged_prefill
+
     gen = torch.Generator(device=device).manual_seed(11)
     for name, rows, ctx, chunk, n_layer, (H, H_KV, D) in (
             ("chunk512_ctx2048", 4, 2048, 512, 28, (16, 8, 128)),
@@ -847,7 +859,7 @@ def prefill_sweep(reps: int = 5) -> None:
         kv_bytes = rows * total * H_KV * D * 2 * 2
         tflops = flops / (best * 1e-6) / 1e12
         print(json.dumps({
-            "prefill_case": name, "rows": rows, "context": ctx, "chunk": chunk, "layers": n_layer,
+            "prefill_case": name, "kernel": kernel, "rows": rows, "context": ctx, "chunk": chunk, "layers": n_layer,
             "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
             "us_per_launch_best": round(best, 2), "us_per_launch_median": round(statistics.median(times), 2),
             "causal_tflops": round(tflops, 1),
@@ -855,8 +867,8 @@ def prefill_sweep(reps: int = 5) -> None:
             "tensor_peak_tflops": peaks["bf16_tflops_sustained"], "kv_gbs": round(kv_bytes / best / 1e3, 1),
             "hbm_roofline_frac": round(kv_bytes / best / 1e3 / peaks["hbm_gbs"], 4),
             "peak_source": peaks["source"],
-            "note": "mma.sync tile math with P as hi+lo operands (3 tensor products per pair where "
-                    "a single-precision-P kernel needs 2)"}), flush=True)
+            "note": "P as hi+lo 16-bit operands: 3 tensor products per (query, key, d) where a "
+                    "16-bit-P kernel needs 2; tcgen05: S and O in TMEM, mma_sync: warp-level tiles"}), flush=True)
         del graph, outs, pools_k, pools_v, q
         torch.cuda.empty_cache()
 

@@ -326,6 +326,13 @@ int pd_get_decode_tuning(int32_t* warps_per_cta, int32_t* stages, int32_t* ctas_
 int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost);
 int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost);
 
+/* Prefill kernel for calls made afterwards: mode 0 (default) runs the tile math on the
+ * 5th-generation tensor cores (tcgen05.mma with S and O accumulated in tensor memory, one
+ * thread per query row for the softmax); mode 1 runs the warp-level mma.sync kernel. Both
+ * compute pd_prefill's function; results agree within rounding. No reference counterpart. */
+int pd_set_prefill_mode(int32_t mode);
+int pd_get_prefill_mode(void);
+
 /* Time limit, in nanoseconds, of the kernels' waits on a pipeline stage (mbarrier) or on a
  * split item's arrival counter, for launches made afterwards (default 1 s; 0 restores it;
  * at most 10 s). A wait that runs out records PD_DEVERR_WAIT_TIMEOUT in the device error word,

@@ -35,6 +35,7 @@ SOURCES = [
     "pd_decode_mma_bf16.cu",
     "pd_decode_mma_f16.cu",
     "pd_prefill.cu",
+    "pd_prefill_tc.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -37,6 +37,8 @@ std::mutex g_mutex;
 int g_decode_mode = 0;
 int g_cta_stages = 0;
 int g_row_cost = 3;  // column split: virtual columns charged per row start
+// Prefill kernel choice: 0 = tcgen05 / TMEM kernel (default), 1 = mma.sync kernel.
+int g_prefill_mode = 0;
 constexpr int kCtaConsumerWarps = 8;
 
 thread_local char g_last_error[256] = "";
@@ -249,7 +251,7 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
 // piece * box_tokens + token, 16-byte units XOR-permuted by the row index.
 int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_size, int n_kv_head,
                 int head_dim, const int64_t* strides, int dtype, int box_tokens, int box_heads,
-                bool swizzle) {
+                bool swizzle, bool one_piece = false) {
   if (load_encoder() != PD_OK) return PD_ERR_CUDA;
   const int es = elem_size(dtype);
   if (!aligned16(base)) return PD_ERR_INVALID;
@@ -267,7 +269,9 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
     // Byte strides of dims 1..4: token-in-block, head, 128-byte piece, block.
     const cuuint64_t gstr[4] = {cuuint64_t(strides[1] * es), cuuint64_t(strides[2] * es), 128u,
                                 cuuint64_t(strides[0] * es)};
-    const cuuint32_t box[5] = {64u, cuuint32_t(box_tokens), 1u, cuuint32_t(head_dim / 64), 1u};
+    // one_piece: the box is one 128-byte piece of box_tokens rows, so a kernel can place every
+    // piece of a tile where it wants it (the tcgen05 prefill lands tiles piece-major).
+    const cuuint32_t box[5] = {64u, cuuint32_t(box_tokens), 1u, one_piece ? 1u : cuuint32_t(head_dim / 64), 1u};
     const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
     CUresult r = g_encode(map, t, 5, const_cast<void*>(base), dims, gstr, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -624,14 +628,20 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
   if (current_device(&dev) != PD_OK) return PD_ERR_CUDA;
   unsigned* err = error_word(dev);
   if (err == nullptr) return PD_ERR_CUDA;
-  const int tile_tokens = prefill_tile_tokens(head_dim);
+  int mode;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    mode = g_prefill_mode;
+  }
+  const bool tc = mode == 0;
+  const int tile_tokens = tc ? prefill_tc_tile_tokens() : prefill_tile_tokens(head_dim);
   const int box_tokens = block_size < tile_tokens ? block_size : tile_tokens;
   CUtensorMap kmap, vmap;
   int st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype, box_tokens,
-                       1, true);
+                       1, true, tc);
   if (st != PD_OK) return st;
   st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype, box_tokens, 1,
-                   true);
+                   true, tc);
   if (st != PD_OK) return st;
   PrefillParams p{};
   p.q = q;
@@ -651,8 +661,10 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
   p.scale_log2 = scale_log2;
   p.err = err;
   p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
-  const cudaError_t e = launch_prefill(p, kmap, vmap, dtype, head_dim, group, max_seqlen_q, batch, n_kv_head,
-                                       static_cast<cudaStream_t>(stream));
+  const cudaError_t e = tc ? launch_prefill_tc(p, kmap, vmap, dtype, head_dim, group, max_seqlen_q, batch,
+                                               n_kv_head, static_cast<cudaStream_t>(stream))
+                           : launch_prefill(p, kmap, vmap, dtype, head_dim, group, max_seqlen_q, batch,
+                                            n_kv_head, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return PD_OK;
@@ -977,6 +989,18 @@ int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost)
   if (shared_stages) *shared_stages = g_cta_stages;
   if (row_cost) *row_cost = g_row_cost;
   return PD_OK;
+}
+
+int pd_set_prefill_mode(int32_t mode) {
+  if (mode < 0 || mode > 1) return PD_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  g_prefill_mode = mode;
+  return PD_OK;
+}
+
+int pd_get_prefill_mode(void) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  return g_prefill_mode;
 }
 
 int pd_set_wait_limit(uint64_t limit_ns) {

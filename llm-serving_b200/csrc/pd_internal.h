@@ -28,6 +28,13 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& kmap, cons
                            int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,
                            cudaStream_t stream);
 
+// The same prefill on the tcgen05 tensor cores (TMEM accumulators); its pool maps have
+// one-piece boxes of at most prefill_tc_tile_tokens() tokens.
+int prefill_tc_tile_tokens();
+cudaError_t launch_prefill_tc(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype,
+                              int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,
+                              cudaStream_t stream);
+
 // Log-sum-exp merge of n_parts (m, l, acc) triples into the normalised output.
 cudaError_t launch_merge(const MergeParams& p, int dtype, cudaStream_t stream);
 

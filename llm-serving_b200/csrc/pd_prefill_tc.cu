@@ -1,0 +1,488 @@
+// pd_prefill_tc.cu -- block-table-aware chunked-prefill attention on the 5th-generation tensor
+// cores (tcgen05 / TMEM) for sm_100a: bf16 / fp16 pools, head_dim 64, 128 or 256, 1, 2, 4 or 8
+// q heads per kv head, block_size >= 8.
+//
+// What it computes is pd_prefill's contract (pd_prefill.cu has the mma.sync kernel of the same
+// function): row b's chunk of Sq query tokens, packed in q[cu_q[b] .. cu_q[b+1]), attends
+// causally -- bottom-right aligned, query token i at position Lk - Sq + i -- to the row's Lk =
+// seqlen_k[b] keys in the paged pool, softmax(q k^T * scale) in fp32 and P.V with fp32
+// accumulation (P carried as a hi + lo pair of 16-bit operands, about 2^-17 relative).
+//
+// How (one CTA = 128 query rows of one row's chunk and one kv head; a query row is a
+// (token, q head) pair of the kv head's group, token-major, so the group's heads share every
+// K/V tile):
+//  * warp 4, lane 0 streams K and V tiles of 64 keys into 2-3 shared-memory stages by TMA from
+//    the pool's 128-byte-swizzled map, one copy per (block part, 64-element piece), so a tile
+//    lands piece-major -- the K-major (K) and MN-major (V) operand layouts of the MMA;
+//  * warp 5, lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K head_dim) into one of two
+//    TMEM buffers, and O += P_hi V_j + P_lo V_j (M 128, N head_dim, K 64) into the TMEM O
+//    accumulator, with S_{j+1} issued before waiting for P_j so the tensor cores work while
+//    the softmax runs; completion is signalled with tcgen05.commit on mbarriers;
+//  * warps 0-3 own one query row per thread (TMEM lane = row): they load the Q tile, then per
+//    key tile read their row of S from TMEM, mask (causal and row end), keep the running max
+//    in log2 units, write P as bf16/fp16 hi and lo rows into shared memory for the next MMA,
+//    and accumulate the normaliser. The running max is rescaled lazily: only when a row's tile
+//    max exceeds it by more than 2^8 is O rescaled in TMEM (P then stays below 2^8, which the
+//    hi + lo operands carry exactly as well as smaller values); the final out = O / max(l, 1)
+//    is unchanged by this.
+//  * Key tiles past the CTA's last query position are never loaded. V rows past the row end
+//    are zeroed in shared memory before use, so stale or NaN pool bytes never reach O.
+//  * Every wait is bounded (the launch's wait limit). A role whose wait runs out records
+//    DEVERR_WAIT_TIMEOUT and raises the CTA's abort flag; every role then stops, the TMA lane
+//    waits for its copies in flight and the MMA lane for its MMAs (fixed 0.1 s limits), and
+//    the CTA frees its TMEM and returns. TMEM allocation itself cannot wait: at most one CTA of
+//    this kernel fits on an SM (shared memory) and it takes at most 512 columns.
+#include "paged_decode.h"
+#include "pd_common.cuh"
+#include "pd_internal.h"
+#include "pd_tcgen05.cuh"
+
+#include <type_traits>
+
+namespace pd {
+
+namespace {
+
+constexpr int TC_ROWS = 128;    // query rows per CTA (the MMA's M)
+constexpr int TC_KT = 64;       // keys per tile (the S MMA's N)
+constexpr int TC_THREADS = 192; // softmax warps 0-3, TMA warp 4, MMA warp 5
+constexpr float TC_RESCALE = 8.f;  // log2 headroom before the running max is moved
+
+template <int D>
+struct TcCfg {
+  static_assert(D == 64 || D == 128 || D == 256, "head_dim 64, 128 or 256");
+  static constexpr int PIECES = D / 64;                 // 128-byte pieces of a row
+  static constexpr int STAGES = D == 64 ? 3 : 2;        // K/V stages
+  static constexpr int PBUF = D == 256 ? 1 : 2;         // P buffers (each a hi and a lo tile)
+  static constexpr int Q_BYTES = TC_ROWS * D * 2;
+  static constexpr int KV_BYTES = TC_KT * D * 2;        // one K (or V) tile
+  static constexpr int P_BYTES = TC_ROWS * TC_KT * 2;   // one P_hi (or P_lo) tile
+  static constexpr int TMEM_COLS = 2 * TC_KT + D <= 256 ? 256 : 512;
+  static constexpr int O_COL = 2 * TC_KT;               // S buffers at columns 0 and 64
+  // shared memory: [barriers and flags, 1 KB | Q | STAGES x (K, V) | PBUF x (P_hi, P_lo)]
+  static constexpr int OFF_Q = 1024;
+  static constexpr int OFF_KV = OFF_Q + Q_BYTES;
+  static constexpr int OFF_P = OFF_KV + STAGES * 2 * KV_BYTES;
+  static constexpr int SMEM = OFF_P + PBUF * 2 * P_BYTES + 1024;  // + run-time 1 KB alignment
+};
+
+// Barrier slots (8 bytes each) in the first KB of shared memory.
+struct TcBars {
+  static constexpr int K_FULL = 0;    // [3] K tile landed (TMA transaction bytes)
+  static constexpr int V_FULL = 3;    // [3] V tile landed
+  static constexpr int KV_EMPTY = 6;  // [3] the stage's MMAs completed (commit)
+  static constexpr int S_FULL = 9;    // [2] S buffer written (commit)
+  static constexpr int S_FREE = 11;   // [2] S buffer read by the 128 softmax threads
+  static constexpr int P_FULL = 13;   // [2] P buffer written (and O rescaled) by the softmax threads
+  static constexpr int O_DONE = 15;   // [2] P.V of the tile that read P buffer i completed (commit)
+  static constexpr int Q_FULL = 17;   // Q tile written by the softmax threads
+  static constexpr int DRAIN = 18;    // every MMA of the CTA completed (commit at exit)
+  static constexpr int TMEM_SLOT = 512;  // byte offset: TMEM base address written by tcgen05.alloc
+  static constexpr int ABORT = 520;      // byte offset: a role's wait ran out
+};
+
+// Single-thread bounded mbarrier wait (the TMA and MMA lanes run alone in their warps).
+__device__ __forceinline__ bool thread_wait_phase(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+  if (limit_ns < TEST_LIMIT_NS) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Offset of 16-byte unit u of row r in a 128-byte-swizzled piece (rows of 128 bytes).
+__device__ __forceinline__ uint32_t sw128(int r, int u) { return uint32_t(r * 128 + ((u ^ (r & 7)) << 4)); }
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    pd_prefill_tc_kernel(const __grid_constant__ PrefillParams p, const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap) {
+  using C = TcCfg<D>;
+  using E = Elem<T>;
+  constexpr int TQ = TC_ROWS / G;  // query tokens per CTA
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.y;
+  const int h = blockIdx.z;
+  const int qtile = int(gridDim.x) - 1 - int(blockIdx.x);  // heaviest (latest) query tiles first
+  const int q_begin = __ldg(p.cu_q + b);
+  const int sq = __ldg(p.cu_q + b + 1) - q_begin;
+  int lk = __ldg(p.seqlen_k + b);
+  lk = lk < 0 ? 0 : (lk > p.capacity ? p.capacity : lk);
+  const int tok0 = qtile * TQ;
+  if (sq <= 0 || tok0 >= sq) return;
+  const int ntok = sq - tok0 < TQ ? sq - tok0 : TQ;
+  const int ctx = lk - sq;
+  int kend = ctx + tok0 + ntok;  // keys this CTA needs: 0 .. kend - 1
+  if (kend > lk) kend = lk;
+  if (kend < 0) kend = 0;
+  const int ntiles = (kend + TC_KT - 1) / TC_KT;
+  T* og = reinterpret_cast<T*>(p.out);
+
+  if (ntiles == 0) {  // no visible key for any row of the CTA: exact zeros
+    if (tid < TC_ROWS && tid / G < ntok) {
+      T* dst = og + int64_t(q_begin + tok0 + tid / G) * p.o_st + int64_t(h * G + tid % G) * p.o_sh;
+      for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst)[u] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+
+  const uint32_t raw = smem_addr(smem_raw);
+  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const uint32_t sbase = smem_addr(smem);
+  auto bar = [&](int slot) -> uint32_t { return sbase + uint32_t(slot) * 8u; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcBars::ABORT);
+  const unsigned long long wait_ns = p.wait_ns;
+
+  if (tid == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(TcBars::K_FULL + s), 1);
+      mbar_init(bar(TcBars::V_FULL + s), 1);
+      mbar_init(bar(TcBars::KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(TcBars::S_FULL + i), 1);
+      mbar_init(bar(TcBars::S_FREE + i), TC_ROWS);
+      mbar_init(bar(TcBars::P_FULL + i), TC_ROWS);
+      mbar_init(bar(TcBars::O_DONE + i), 1);
+    }
+    mbar_init(bar(TcBars::Q_FULL), TC_ROWS);
+    mbar_init(bar(TcBars::DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(sbase + TcBars::TMEM_SLOT, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + TcBars::TMEM_SLOT);
+
+  const uint32_t q_addr = sbase + C::OFF_Q;
+  auto k_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_KV + s * 2 * C::KV_BYTES); };
+  auto v_addr = [&](int s) -> uint32_t { return k_addr(s) + uint32_t(C::KV_BYTES); };
+  auto p_addr = [&](int pb, int lo) -> uint32_t {
+    return sbase + uint32_t(C::OFF_P + (pb * 2 + lo) * C::P_BYTES);
+  };
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
+  };
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      const int bs = p.block_size;
+      const int bt = p.box_tokens;  // tokens per copy: min(block_size, 64)
+      const int npages = (lk + bs - 1) / bs;
+      const uint32_t box_bytes = uint32_t(bt) * 128u;  // one piece of one box
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        if (*abort_flag) break;
+        const int s = j % C::STAGES;
+        if (j >= C::STAGES &&
+            !thread_wait_phase(bar(TcBars::KV_EMPTY + s), uint32_t((j / C::STAGES - 1) & 1), wait_ns)) {
+          fail();
+          break;
+        }
+        const int t0 = j * TC_KT;
+        const int covered = kend - t0 < TC_KT ? kend - t0 : TC_KT;
+        const int boxes = (covered + bt - 1) / bt;
+        const uint32_t tx = uint32_t(boxes) * box_bytes * C::PIECES;
+        mbar_arrive_expect_tx(bar(TcBars::K_FULL + s), tx);
+        mbar_arrive_expect_tx(bar(TcBars::V_FULL + s), tx);
+        for (int jb = 0; jb < boxes; ++jb) {
+          const int tok = t0 + jb * bt;
+          const int page = tok / bs;
+          const int off = tok - page * bs;
+          const int blk = page < npages && page < p.max_blocks ? __ldg(p.table + int64_t(b) * p.bt_stride + page) : 0;
+          for (int pc = 0; pc < C::PIECES; ++pc) {
+            const uint32_t dst = uint32_t(pc * TC_KT * 128 + jb * bt * 128);
+            tma_load_5d(k_addr(s) + dst, &kmap, bar(TcBars::K_FULL + s), 0, off, h, pc, blk);
+            tma_load_5d(v_addr(s) + dst, &vmap, bar(TcBars::V_FULL + s), 0, off, h, pc, blk);
+          }
+        }
+        issued = j + 1;
+      }
+      // never leave with a copy in flight: the last STAGES tiles' copies must have landed
+      for (int j = issued > C::STAGES ? issued - C::STAGES : 0; j < issued; ++j) {
+        const uint32_t par = uint32_t((j / C::STAGES) & 1);
+        thread_wait_phase(bar(TcBars::K_FULL + j % C::STAGES), par, DRAIN_LIMIT_NS);
+        thread_wait_phase(bar(TcBars::V_FULL + j % C::STAGES), par, DRAIN_LIMIT_NS);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = tc::instr_desc_f16(BF16, TC_ROWS, TC_KT, false, false);
+      constexpr uint32_t IDESC_PV = tc::instr_desc_f16(BF16, TC_ROWS, D, false, true);
+      const uint32_t o_tmem = tmem + C::O_COL;
+      bool ok = thread_wait_phase(bar(TcBars::Q_FULL), 0u, wait_ns);
+      // S_t = Q K_t^T into S buffer t % 2: head_dim / 16 steps of K = 16 (32 bytes of a row)
+      auto issue_s = [&](int t) -> bool {
+        const int s = t % C::STAGES;
+        if (!thread_wait_phase(bar(TcBars::K_FULL + s), uint32_t((t / C::STAGES) & 1), wait_ns)) return false;
+        if (t >= 2 && !thread_wait_phase(bar(TcBars::S_FREE + (t & 1)), uint32_t(((t >> 1) - 1) & 1), wait_ns))
+          return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t koff = uint32_t((ks >> 2) * 16384 + (ks & 3) * 32);  // Q piece = 128 rows x 128 B
+          const uint64_t a = tc::smem_desc(q_addr + koff, 16u, 1024u);
+          const uint64_t bd = tc::smem_desc(k_addr(s) + uint32_t((ks >> 2) * TC_KT * 128 + (ks & 3) * 32), 16u, 1024u);
+          tc::mma_f16_ss(tmem + uint32_t((t & 1) * TC_KT), a, bd, IDESC_S, ks > 0);
+        }
+        tc::commit(bar(TcBars::S_FULL + (t & 1)));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (*abort_flag) break;
+        if (j + 1 < ntiles && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        const int pb = j % C::PBUF;
+        const int s = j % C::STAGES;
+        if (!thread_wait_phase(bar(TcBars::P_FULL + pb), uint32_t((j / C::PBUF) & 1), wait_ns) ||
+            !thread_wait_phase(bar(TcBars::V_FULL + s), uint32_t((j / C::STAGES) & 1), wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        // O += P_hi V + P_lo V: 64 keys in 4 steps of K = 16 (32 bytes of a P row, 16 V rows)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int kk = 0; kk < TC_KT / 16; ++kk) {
+            const uint64_t a = tc::smem_desc(p_addr(pb, half) + uint32_t(kk * 32), 16u, 1024u);
+            const uint64_t bd = tc::smem_desc(v_addr(s) + uint32_t(kk * 2048), uint32_t(TC_KT * 128), 1024u);
+            tc::mma_f16_ss(o_tmem, a, bd, IDESC_PV, j > 0 || half > 0 || kk > 0);
+          }
+        }
+        tc::commit(bar(TcBars::O_DONE + pb));
+        tc::commit(bar(TcBars::KV_EMPTY + s));
+      }
+      if (!ok) fail();
+      // never leave with an MMA in flight (TMEM is freed and shared memory reused after exit)
+      tc::commit(bar(TcBars::DRAIN));
+      thread_wait_phase(bar(TcBars::DRAIN), 0u, DRAIN_LIMIT_NS);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps 0-3
+    const int r = tid;  // query row = TMEM lane
+    const int i = r / G;
+    const int hq = h * G + r % G;
+    {  // Q row -> the swizzled K-major Q tile (zeros past the chunk)
+      const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st + int64_t(hq) * p.q_sh;
+#pragma unroll
+      for (int u = 0; u < D / 8; ++u) {
+        const uint4 v = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(smem + C::OFF_Q + (u >> 3) * 16384 + sw128(r, u & 7)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(TcBars::Q_FULL));
+    }
+    const int row_last = i < ntok ? ctx + tok0 + i : kend - 1;  // padding rows: any finite row
+    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    // P.V of tile t has completed. Tile t's phase on its buffer's barrier is t / PBUF; the
+    // barrier cannot pass it before this thread writes that buffer again, and the phase before
+    // it was observed one buffer turn earlier, so the parity test is unambiguous.
+    auto wait_pv = [&](int t) -> bool {
+      return warp_wait_phase(bar(TcBars::O_DONE + t % C::PBUF), uint32_t((t / C::PBUF) & 1), wait_ns);
+    };
+    for (int j = 0; j < ntiles; ++j) {
+      if (__any_sync(FULL_MASK, *abort_flag != 0)) {
+        ok = false;
+        break;
+      }
+      const int sb = j & 1;
+      if (!warp_wait_phase(bar(TcBars::S_FULL + sb), uint32_t((j >> 1) & 1), wait_ns)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      uint32_t raw_s[TC_KT];
+      tc::ld_32x32b_x32(lane_base + uint32_t(sb * TC_KT), *reinterpret_cast<uint32_t(*)[32]>(raw_s));
+      tc::ld_32x32b_x32(lane_base + uint32_t(sb * TC_KT + 32), *reinterpret_cast<uint32_t(*)[32]>(raw_s + 32));
+      tc::wait_ld();
+      tc::fence_before_sync();
+      mbar_arrive(bar(TcBars::S_FREE + sb));
+
+      const int t0 = j * TC_KT;
+      float s[TC_KT];
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TC_KT; ++c) {
+        const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
+        s[c] = t0 + c <= row_last ? x : -INFINITY;
+        tmax = fmaxf(tmax, s[c]);
+      }
+      const bool move = tmax > m_run + TC_RESCALE || (m_run == -INFINITY && tmax > -INFINITY);
+      const float alpha = !move ? 1.f : (m_run == -INFINITY ? 0.f : exp2f(m_run - tmax));
+      // The P buffer of this tile was last read by P.V of tile j - PBUF.
+      if (j >= C::PBUF && !wait_pv(j - C::PBUF)) {
+        ok = false;
+        break;
+      }
+      const bool rescale = j > 0 && __any_sync(FULL_MASK, move);
+      if (rescale) {  // O *= alpha per row, once P.V of tile j - 1 has landed in O
+        if (!wait_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
+          tc::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tc::st_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
+        }
+        tc::wait_st();
+      }
+      if (move) m_run = tmax;
+      l_run *= alpha;
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      // P = 2^(s - m) as hi + lo 16-bit pairs, written as this row of the two K-major P tiles
+      const int pb = j % C::PBUF;
+      unsigned char* phi = smem + C::OFF_P + (pb * 2) * C::P_BYTES;
+      unsigned char* plo = phi + C::P_BYTES;
+#pragma unroll
+      for (int u = 0; u < TC_KT / 8; ++u) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2f(s[u * 8 + 2 * e] - m_use);
+          const float p1 = exp2f(s[u * 8 + 2 * e + 1] - m_use);
+          l_run += p0 + p1;
+          hw[e] = E::pack2(p0, p1);
+          float hf[2];
+          E::unpack2(hw[e], hf);
+          lw[e] = E::pack2(p0 - hf[0], p1 - hf[1]);
+        }
+        *reinterpret_cast<uint4*>(phi + sw128(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(plo + sw128(r, u)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+      // The last tile: V rows past the row end must be zero (P is 0 there, but 0 * NaN is not).
+      const int valid = kend - t0;
+      if (valid < TC_KT) {
+        const int s_st = j % C::STAGES;
+        if (!warp_wait_phase(bar(TcBars::V_FULL + s_st), uint32_t((j / C::STAGES) & 1), wait_ns)) {
+          ok = false;
+          break;
+        }
+        unsigned char* vs = smem + C::OFF_KV + s_st * 2 * C::KV_BYTES + C::KV_BYTES;
+        const int zrows = TC_KT - valid;
+        for (int idx = r; idx < zrows * 8 * C::PIECES; idx += TC_ROWS) {
+          const int pc = idx / (zrows * 8);
+          const int rem = idx - pc * zrows * 8;
+          const int row = valid + rem / 8;
+          *reinterpret_cast<uint4*>(vs + pc * TC_KT * 128 + row * 128 + ((rem & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      mbar_arrive(bar(TcBars::P_FULL + pb));
+    }
+    if (!ok) fail();
+    // ---- epilogue: out = O / max(l, 1) for the rows of the chunk
+    if (ok && wait_pv(ntiles - 1)) {
+      tc::fence_after_sync();
+      const float inv = 1.f / fmaxf(l_run, 1.f);
+      T* dst = og + int64_t(q_begin + tok0 + i) * p.o_st + int64_t(hq) * p.o_sh;
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
+        tc::wait_ld();
+        if (i < ntok) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = E::pack2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            w.y = E::pack2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            w.z = E::pack2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            w.w = E::pack2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c0 + 8 * u) = w;
+          }
+        }
+      }
+    } else if (ok) {
+      fail();
+    }
+  }
+
+  // ---- every role is done with TMEM and shared memory: free the TMEM columns
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <typename T, int D, int G>
+cudaError_t launch_tc_t(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int max_seqlen_q,
+                        int batch, int n_kv_head, cudaStream_t stream) {
+  using C = TcCfg<D>;
+  auto fn = pd_prefill_tc_kernel<T, D, G>;
+  static int attr_smem[64] = {0};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 64 && attr_smem[dev] < C::SMEM) {
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (err != cudaSuccess) return err;
+    attr_smem[dev] = C::SMEM;
+  }
+  constexpr int TQ = TC_ROWS / G;
+  const dim3 grid((max_seqlen_q + TQ - 1) / TQ, batch, n_kv_head);
+  fn<<<grid, TC_THREADS, C::SMEM, stream>>>(p, kmap, vmap);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_tc_g(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int group,
+                        int max_seqlen_q, int batch, int n_kv_head, cudaStream_t stream) {
+  switch (group) {
+    case 1: return launch_tc_t<T, D, 1>(p, kmap, vmap, max_seqlen_q, batch, n_kv_head, stream);
+    case 2: return launch_tc_t<T, D, 2>(p, kmap, vmap, max_seqlen_q, batch, n_kv_head, stream);
+    case 4: return launch_tc_t<T, D, 4>(p, kmap, vmap, max_seqlen_q, batch, n_kv_head, stream);
+    case 8: return launch_tc_t<T, D, 8>(p, kmap, vmap, max_seqlen_q, batch, n_kv_head, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int prefill_tc_tile_tokens() { return TC_KT; }
+
+cudaError_t launch_prefill_tc(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype,
+                              int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,
+                              cudaStream_t stream) {
+  if (dtype == PD_BF16) {
+    if (head_dim == 64)
+      return launch_tc_g<__nv_bfloat16, 64>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+    if (head_dim == 256)
+      return launch_tc_g<__nv_bfloat16, 256>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+    return launch_tc_g<__nv_bfloat16, 128>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+  }
+  if (head_dim == 64) return launch_tc_g<__half, 64>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+  if (head_dim == 256) return launch_tc_g<__half, 256>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+  return launch_tc_g<__half, 128>(p, kmap, vmap, group, max_seqlen_q, batch, n_kv_head, stream);
+}
+
+}  // namespace pd

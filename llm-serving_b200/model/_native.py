@@ -111,6 +111,8 @@ _SIGNATURES = {
     "pd_get_decode_tuning": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 4),
     "pd_set_decode_mode": (ctypes.c_int, [_c_i32, _c_i32, _c_i32]),
     "pd_get_decode_mode": (ctypes.c_int, [ctypes.POINTER(_c_i32)] * 3),
+    "pd_set_prefill_mode": (ctypes.c_int, [_c_i32]),
+    "pd_get_prefill_mode": (ctypes.c_int, []),
     "pd_set_wait_limit": (ctypes.c_int, [ctypes.c_uint64]),
     "pd_get_wait_limit": (ctypes.c_uint64, []),
 }
@@ -218,6 +220,15 @@ def get_decode_mode() -> tuple[int, int, int]:
     vals = [_c_i32(0) for _ in range(3)]
     check(require().pd_get_decode_mode(*[ctypes.byref(v) for v in vals]), "pd_get_decode_mode")
     return tuple(int(v.value) for v in vals)
+
+
+def set_prefill_mode(mode: int) -> None:
+    """0: tcgen05 / TMEM prefill kernel (default); 1: mma.sync prefill kernel."""
+    check(require().pd_set_prefill_mode(int(mode)), "pd_set_prefill_mode")
+
+
+def get_prefill_mode() -> int:
+    return int(require().pd_get_prefill_mode())
 
 
 def set_wait_limit(limit_ns: int) -> None:

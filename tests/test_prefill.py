@@ -93,6 +93,21 @@ def test_entry_point_refuses_unsupported_shapes_without_touching_memory():
 
 # ------------------------------------------------------------------ kernel (GPU)
 
+
+@pytest.fixture(params=[0, 1], ids=["tcgen05", "mma_sync"])
+def kernel(request):
+    """Runs the test with the tcgen05 / TMEM prefill kernel (mode 0, the default) and with the
+    mma.sync kernel (mode 1); both compute the same function."""
+    from model import _native
+
+    before = _native.get_prefill_mode()
+    _native.set_prefill_mode(request.param)
+    try:
+        yield request.param
+    finally:
+        _native.set_prefill_mode(before)
+
+
 CASES = [
     # H, Hkv, D, bs, ctx, chunks
     pytest.param(16, 8, 128, 16, [0, 100, 1000], [64, 7, 129], id="qwen3-g2-d128-bs16"),
@@ -109,7 +124,7 @@ CASES = [
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("H,Hkv,D,bs,ctx,chunks", CASES)
-def test_prefill_matches_the_oracle(cuda_device, H, Hkv, D, bs, ctx, chunks, dtype):
+def test_prefill_matches_the_oracle(cuda_device, kernel, H, Hkv, D, bs, ctx, chunks, dtype):
     from model import _native
     from model.triton_decode import paged_prefill
 
@@ -124,7 +139,7 @@ def test_prefill_matches_the_oracle(cuda_device, H, Hkv, D, bs, ctx, chunks, dty
 
 
 @pytest.mark.gpu
-def test_prefill_ignores_nan_in_slots_no_row_reads(cuda_device):
+def test_prefill_ignores_nan_in_slots_no_row_reads(cuda_device, kernel):
     from model import _native
     from model.triton_decode import paged_prefill
 
@@ -137,7 +152,7 @@ def test_prefill_ignores_nan_in_slots_no_row_reads(cuda_device):
 
 
 @pytest.mark.gpu
-def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device):
+def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device, kernel):
     """Engines pass a bucketed bound; the extra query tiles of the grid have no tokens."""
     from model import _native
     from model.triton_decode import paged_prefill
@@ -154,7 +169,7 @@ def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device):
 
 
 @pytest.mark.gpu
-def test_one_token_chunks_agree_with_the_decode_kernel(cuda_device):
+def test_one_token_chunks_agree_with_the_decode_kernel(cuda_device, kernel):
     from model.triton_decode import paged_decode, paged_prefill
 
     q, k, v, table, cu, sk = prefill_case(16, 8, 128, 16, [31, 600, 2047, 0], [1, 1, 1, 1], seed=6)
@@ -169,7 +184,7 @@ def test_one_token_chunks_agree_with_the_decode_kernel(cuda_device):
 
 
 @pytest.mark.gpu
-def test_long_chunk_over_a_long_context(cuda_device):
+def test_long_chunk_over_a_long_context(cuda_device, kernel):
     """A 1,000-token chunk after 3,000 cached tokens: many query tiles and key tiles per CTA."""
     from model import _native
     from model.triton_decode import paged_prefill
@@ -184,7 +199,7 @@ def test_long_chunk_over_a_long_context(cuda_device):
 
 
 @pytest.mark.gpu
-def test_chunked_prefill_through_the_engine_pool(cuda_device):
+def test_chunked_prefill_through_the_engine_pool(cuda_device, kernel):
     """The engine's flow: a request's prompt K/V go into the pool with
     ``PagedPool.write_prefill`` chunk by chunk, and each chunk's queries attend over the pool
     with ``paged_prefill`` (earlier chunks included)."""

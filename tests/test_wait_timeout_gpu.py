@@ -72,9 +72,21 @@ def test_decode_wait_runs_out_and_the_next_launch_is_correct(cuda_device, short_
         assert_output_close(out, ref_f32, torch.bfloat16)
 
 
-def test_prefill_wait_runs_out_and_the_next_launch_is_correct(cuda_device, short_waits):
+@pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
+def test_prefill_wait_runs_out_and_the_next_launch_is_correct(cuda_device, short_waits, kernel):
     from model import _native
     from model.triton_decode import paged_prefill
+
+    before = _native.get_prefill_mode()
+    _native.set_prefill_mode(kernel)
+    try:
+        _prefill_case(cuda_device, paged_prefill)
+    finally:
+        _native.set_prefill_mode(before)
+
+
+def _prefill_case(cuda_device, paged_prefill):
+    from model import _native
 
     from test_prefill import prefill_case
 
