@@ -466,6 +466,10 @@ struct PrefillParams {
   float scale_log2;
   unsigned* err;
   unsigned long long wait_ns;  // limit of the stage waits
+  // Filled by the tcgen05 launcher (its grid is 1-D: query tile, kv head, row).
+  int32_t batch;
+  int32_t n_kv_head;
+  int32_t q_tiles;
 };
 
 struct MergeParams {

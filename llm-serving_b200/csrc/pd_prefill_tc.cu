@@ -11,9 +11,11 @@
 // How (one CTA = 128 query rows of one row's chunk and one kv head; a query row is a
 // (token, q head) pair of the kv head's group, token-major, so the group's heads share every
 // K/V tile):
-//  * warp 4, lane 0 streams K and V tiles of 64 keys into 2-3 shared-memory stages by TMA from
-//    the pool's 128-byte-swizzled map, one copy per (block part, 64-element piece), so a tile
-//    lands piece-major -- the K-major (K) and MN-major (V) operand layouts of the MMA;
+//  * warp 4 streams K and V tiles of 64 keys by TMA from the pool's 128-byte-swizzled map into
+//    two rings of shared-memory stages (6 / 4 / 2 each at head_dim 64 / 128 / 256), one copy
+//    per (block part, 64-element piece), so a tile lands piece-major -- the K-major (K) and
+//    MN-major (V) operand layouts of the MMA. A K stage is refilled as soon as its S MMA has
+//    read it, a V stage once its P.V has; the block table is read 32 entries at a time;
 //  * warp 5, lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K head_dim) into one of two
 //    TMEM buffers, and O += P_hi V_j + P_lo V_j (M 128, N head_dim, K 64) into the TMEM O
 //    accumulator, with S_{j+1} issued before waiting for P_j so the tensor cores work while
@@ -52,31 +54,33 @@ template <int D>
 struct TcCfg {
   static_assert(D == 64 || D == 128 || D == 256, "head_dim 64, 128 or 256");
   static constexpr int PIECES = D / 64;                 // 128-byte pieces of a row
-  static constexpr int STAGES = D == 64 ? 3 : 2;        // K/V stages
+  static constexpr int STAGES = D == 64 ? 6 : (D == 128 ? 4 : 2);  // stages of each of the K and V rings
   static constexpr int PBUF = D == 256 ? 1 : 2;         // P buffers (each a hi and a lo tile)
   static constexpr int Q_BYTES = TC_ROWS * D * 2;
   static constexpr int KV_BYTES = TC_KT * D * 2;        // one K (or V) tile
   static constexpr int P_BYTES = TC_ROWS * TC_KT * 2;   // one P_hi (or P_lo) tile
   static constexpr int TMEM_COLS = 2 * TC_KT + D <= 256 ? 256 : 512;
   static constexpr int O_COL = 2 * TC_KT;               // S buffers at columns 0 and 64
-  // shared memory: [barriers and flags, 1 KB | Q | STAGES x (K, V) | PBUF x (P_hi, P_lo)]
+  // shared memory: [barriers and flags, 1 KB | Q | STAGES x K | STAGES x V | PBUF x (P_hi, P_lo)]
   static constexpr int OFF_Q = 1024;
-  static constexpr int OFF_KV = OFF_Q + Q_BYTES;
-  static constexpr int OFF_P = OFF_KV + STAGES * 2 * KV_BYTES;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
   static constexpr int SMEM = OFF_P + PBUF * 2 * P_BYTES + 1024;  // + run-time 1 KB alignment
 };
 
 // Barrier slots (8 bytes each) in the first KB of shared memory.
 struct TcBars {
-  static constexpr int K_FULL = 0;    // [3] K tile landed (TMA transaction bytes)
-  static constexpr int V_FULL = 3;    // [3] V tile landed
-  static constexpr int KV_EMPTY = 6;  // [3] the stage's MMAs completed (commit)
-  static constexpr int S_FULL = 9;    // [2] S buffer written (commit)
-  static constexpr int S_FREE = 11;   // [2] S buffer read by the 128 softmax threads
-  static constexpr int P_FULL = 13;   // [2] P buffer written (and O rescaled) by the softmax threads
-  static constexpr int O_DONE = 15;   // [2] P.V of the tile that read P buffer i completed (commit)
-  static constexpr int Q_FULL = 17;   // Q tile written by the softmax threads
-  static constexpr int DRAIN = 18;    // every MMA of the CTA completed (commit at exit)
+  static constexpr int K_FULL = 0;    // [6] K tile landed (TMA transaction bytes)
+  static constexpr int V_FULL = 6;    // [6] V tile landed
+  static constexpr int K_EMPTY = 12;  // [6] S = Q K^T of the stage's tile completed (commit)
+  static constexpr int V_EMPTY = 18;  // [6] P.V of the stage's tile completed (commit)
+  static constexpr int S_FULL = 24;   // [2] S buffer written (commit)
+  static constexpr int S_FREE = 26;   // [2] S buffer read by the 128 softmax threads
+  static constexpr int P_FULL = 28;   // [2] P buffer written (and O rescaled) by the softmax threads
+  static constexpr int O_DONE = 30;   // [2] P.V of the tile that read P buffer i completed (commit)
+  static constexpr int Q_FULL = 32;   // Q tile written by the softmax threads
+  static constexpr int DRAIN = 33;    // every MMA of the CTA completed (commit at exit)
   static constexpr int TMEM_SLOT = 512;  // byte offset: TMEM base address written by tcgen05.alloc
   static constexpr int ABORT = 520;      // byte offset: a role's wait ran out
 };
@@ -92,6 +96,14 @@ __device__ __forceinline__ bool thread_wait_phase(uint32_t bar, uint32_t parity,
   }
 }
 
+// 2^x by the hardware approximation (ex2.approx, subnormal results flushed to zero). Here x <= 8
+// (the running max's headroom), and a probability below 2^-126 changes no fp32 sum it joins.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Offset of 16-byte unit u of row r in a 128-byte-swizzled piece (rows of 128 bytes).
 __device__ __forceinline__ uint32_t sw128(int r, int u) { return uint32_t(r * 128 + ((u ^ (r & 7)) << 4)); }
 
@@ -105,9 +117,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int b = blockIdx.y;
-  const int h = blockIdx.z;
-  const int qtile = int(gridDim.x) - 1 - int(blockIdx.x);  // heaviest (latest) query tiles first
+  // 1-D grid, query tile slowest: the CTAs of the last (heaviest, causal) query tiles of every
+  // (row, kv head) are launched first, so the lighter ones fill the later waves.
+  const int pairs = p.batch * p.n_kv_head;
+  const int b = int(blockIdx.x) % p.batch;
+  const int h = (int(blockIdx.x) / p.batch) % p.n_kv_head;
+  const int qtile = p.q_tiles - 1 - int(blockIdx.x) / pairs;
   const int q_begin = __ldg(p.cu_q + b);
   const int sq = __ldg(p.cu_q + b + 1) - q_begin;
   int lk = __ldg(p.seqlen_k + b);
@@ -143,7 +158,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(TcBars::K_FULL + s), 1);
       mbar_init(bar(TcBars::V_FULL + s), 1);
-      mbar_init(bar(TcBars::KV_EMPTY + s), 1);
+      mbar_init(bar(TcBars::K_EMPTY + s), 1);
+      mbar_init(bar(TcBars::V_EMPTY + s), 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(TcBars::S_FULL + i), 1);
@@ -166,8 +182,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + TcBars::TMEM_SLOT);
 
   const uint32_t q_addr = sbase + C::OFF_Q;
-  auto k_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_KV + s * 2 * C::KV_BYTES); };
-  auto v_addr = [&](int s) -> uint32_t { return k_addr(s) + uint32_t(C::KV_BYTES); };
+  auto k_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_K + s * C::KV_BYTES); };
+  auto v_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_V + s * C::KV_BYTES); };
   auto p_addr = [&](int pb, int lo) -> uint32_t {
     return sbase + uint32_t(C::OFF_P + (pb * 2 + lo) * C::P_BYTES);
   };
@@ -178,46 +194,82 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      const int bs = p.block_size;
-      const int bt = p.box_tokens;  // tokens per copy: min(block_size, 64)
-      const int npages = (lk + bs - 1) / bs;
-      const uint32_t box_bytes = uint32_t(bt) * 128u;  // one piece of one box
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        if (*abort_flag) break;
-        const int s = j % C::STAGES;
-        if (j >= C::STAGES &&
-            !thread_wait_phase(bar(TcBars::KV_EMPTY + s), uint32_t((j / C::STAGES - 1) & 1), wait_ns)) {
-          fail();
-          break;
-        }
-        const int t0 = j * TC_KT;
-        const int covered = kend - t0 < TC_KT ? kend - t0 : TC_KT;
-        const int boxes = (covered + bt - 1) / bt;
-        const uint32_t tx = uint32_t(boxes) * box_bytes * C::PIECES;
-        mbar_arrive_expect_tx(bar(TcBars::K_FULL + s), tx);
-        mbar_arrive_expect_tx(bar(TcBars::V_FULL + s), tx);
-        for (int jb = 0; jb < boxes; ++jb) {
-          const int tok = t0 + jb * bt;
-          const int page = tok / bs;
-          const int off = tok - page * bs;
-          const int blk = page < npages && page < p.max_blocks ? __ldg(p.table + int64_t(b) * p.bt_stride + page) : 0;
-          for (int pc = 0; pc < C::PIECES; ++pc) {
-            const uint32_t dst = uint32_t(pc * TC_KT * 128 + jb * bt * 128);
-            tma_load_5d(k_addr(s) + dst, &kmap, bar(TcBars::K_FULL + s), 0, off, h, pc, blk);
-            tma_load_5d(v_addr(s) + dst, &vmap, bar(TcBars::V_FULL + s), 0, off, h, pc, blk);
-          }
-        }
-        issued = j + 1;
+    // The whole warp runs the loop (its waits are warp-collective) and keeps the row's block
+    // table in a 32-entry register window, the next window prefetched, so no copy waits on a
+    // dependent table load; lane 0 issues the copies. K tile j is issued once the S MMA of tile
+    // j - STAGES has read its stage, V tile j once the P.V of tile j - STAGES has.
+    const int bs = p.block_size;
+    const int bt = p.box_tokens;  // tokens per copy: min(block_size, 64)
+    const int npages = (lk + bs - 1) / bs;
+    const uint32_t box_bytes = uint32_t(bt) * 128u;  // one piece of one box
+    const int32_t* trow = p.table + int64_t(b) * p.bt_stride;
+    auto entry = [&](int page) -> int {
+      return page >= 0 && page < npages && page < p.max_blocks ? __ldg(trow + page) : 0;
+    };
+    // 64-entry window [win_base, win_base + 64): lane l holds entries win_base + l and + 32 + l.
+    // A tile spans at most 64 / block_size + 1 <= 9 pages, so once the window starts at or
+    // below the tile's first page and within 32 of it, every page of the tile is inside.
+    int win_base = 0, win_cur = entry(lane), win_nxt = entry(32 + lane);
+    auto advance_window = [&](int first_page) {  // warp-collective
+      while (first_page >= win_base + 32) {
+        win_base += 32;
+        win_cur = win_nxt;
+        win_nxt = entry(win_base + 32 + lane);
       }
-      // never leave with a copy in flight: the last STAGES tiles' copies must have landed
-      for (int j = issued > C::STAGES ? issued - C::STAGES : 0; j < issued; ++j) {
-        const uint32_t par = uint32_t((j / C::STAGES) & 1);
-        thread_wait_phase(bar(TcBars::K_FULL + j % C::STAGES), par, DRAIN_LIMIT_NS);
-        thread_wait_phase(bar(TcBars::V_FULL + j % C::STAGES), par, DRAIN_LIMIT_NS);
+    };
+    auto block_of = [&](int page) -> int {  // per-lane page inside the window
+      const int i = page - win_base;
+      const int lo = __shfl_sync(FULL_MASK, win_cur, i & 31);
+      const int hi = __shfl_sync(FULL_MASK, win_nxt, i & 31);
+      return i < 32 ? lo : hi;
+    };
+    // The copies of one K (or V) tile, one per (box, piece), issued in parallel: lane c issues
+    // copy c; boxes * PIECES <= (64 / 8) * 4 = 32 (box_tokens >= 8, head_dim <= 256).
+    auto issue_tile = [&](int t0, int boxes, uint32_t dst0, const CUtensorMap* map, uint32_t full_bar) {
+      const int c = lane;
+      const int jb = c / C::PIECES, pc = c - jb * C::PIECES;
+      const int tok = t0 + jb * bt;
+      const int page = tok / bs;
+      const int blk = block_of(page);
+      if (jb < boxes)
+        tma_load_5d(dst0 + uint32_t(pc * TC_KT * 128 + jb * bt * 128), map, full_bar, 0, tok - page * bs, h, pc, blk);
+    };
+    int issued = 0;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (__any_sync(FULL_MASK, *abort_flag != 0)) break;
+      const int s = j % C::STAGES;
+      const uint32_t par = uint32_t((j / C::STAGES - 1) & 1);
+      if (j >= C::STAGES && !warp_wait_phase(bar(TcBars::K_EMPTY + s), par, wait_ns)) {
+        ok = false;
+        break;
       }
+      const int t0 = j * TC_KT;
+      const int covered = kend - t0 < TC_KT ? kend - t0 : TC_KT;
+      const int boxes = (covered + bt - 1) / bt;
+      const uint32_t tx = uint32_t(boxes) * box_bytes * C::PIECES;
+      advance_window(t0 / bs);
+      if (lane == 0) mbar_arrive_expect_tx(bar(TcBars::K_FULL + s), tx);
+      __syncwarp();
+      issue_tile(t0, boxes, k_addr(s), &kmap, bar(TcBars::K_FULL + s));
+      if (j >= C::STAGES && !warp_wait_phase(bar(TcBars::V_EMPTY + s), par, wait_ns)) {
+        ok = false;
+        issued = -(j + 1);  // K of tile j is in flight, V is not
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(bar(TcBars::V_FULL + s), tx);
+      __syncwarp();
+      issue_tile(t0, boxes, v_addr(s), &vmap, bar(TcBars::V_FULL + s));
+      issued = j + 1;
     }
+    if (!ok && lane == 0) fail();
+    // never leave with a copy in flight: the last STAGES tiles' copies must have landed
+    const int k_issued = issued < 0 ? -issued : issued;
+    const int v_issued = issued < 0 ? -issued - 1 : issued;
+    for (int j = k_issued > C::STAGES ? k_issued - C::STAGES : 0; j < k_issued; ++j)
+      warp_wait_phase(bar(TcBars::K_FULL + j % C::STAGES), uint32_t((j / C::STAGES) & 1), DRAIN_LIMIT_NS);
+    for (int j = v_issued > C::STAGES ? v_issued - C::STAGES : 0; j < v_issued; ++j)
+      warp_wait_phase(bar(TcBars::V_FULL + j % C::STAGES), uint32_t((j / C::STAGES) & 1), DRAIN_LIMIT_NS);
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -240,6 +292,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc::mma_f16_ss(tmem + uint32_t((t & 1) * TC_KT), a, bd, IDESC_S, ks > 0);
         }
         tc::commit(bar(TcBars::S_FULL + (t & 1)));
+        tc::commit(bar(TcBars::K_EMPTY + s));
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -268,7 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         tc::commit(bar(TcBars::O_DONE + pb));
-        tc::commit(bar(TcBars::KV_EMPTY + s));
+        tc::commit(bar(TcBars::V_EMPTY + s));
       }
       if (!ok) fail();
       // never leave with an MMA in flight (TMEM is freed and shared memory reused after exit)
@@ -320,13 +373,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
       const int t0 = j * TC_KT;
       float s[TC_KT];
-      float tmax = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+      if (t0 + TC_KT - 1 <= row_last) {  // the whole tile is visible to this row
 #pragma unroll
-      for (int c = 0; c < TC_KT; ++c) {
-        const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
-        s[c] = t0 + c <= row_last ? x : -INFINITY;
-        tmax = fmaxf(tmax, s[c]);
+        for (int c = 0; c < TC_KT; ++c) {
+          s[c] = __uint_as_float(raw_s[c]) * p.scale_log2;
+          mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+        }
+      } else {  // the causal edge (or the row end) crosses the tile
+#pragma unroll
+        for (int c = 0; c < TC_KT; ++c) {
+          const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
+          s[c] = t0 + c <= row_last ? x : -INFINITY;
+          mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+        }
       }
+      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const bool move = tmax > m_run + TC_RESCALE || (m_run == -INFINITY && tmax > -INFINITY);
       const float alpha = !move ? 1.f : (m_run == -INFINITY ? 0.f : exp2f(m_run - tmax));
       // The P buffer of this tile was last read by P.V of tile j - PBUF.
@@ -359,14 +421,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int pb = j % C::PBUF;
       unsigned char* phi = smem + C::OFF_P + (pb * 2) * C::P_BYTES;
       unsigned char* plo = phi + C::P_BYTES;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int u = 0; u < TC_KT / 8; ++u) {
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(s[u * 8 + 2 * e] - m_use);
-          const float p1 = exp2f(s[u * 8 + 2 * e + 1] - m_use);
-          l_run += p0 + p1;
+          const float p0 = ex2_ftz(s[u * 8 + 2 * e] - m_use);
+          const float p1 = ex2_ftz(s[u * 8 + 2 * e + 1] - m_use);
+          ls[e] += p0 + p1;
           hw[e] = E::pack2(p0, p1);
           float hf[2];
           E::unpack2(hw[e], hf);
@@ -375,6 +438,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         *reinterpret_cast<uint4*>(phi + sw128(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4*>(plo + sw128(r, u)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // The last tile: V rows past the row end must be zero (P is 0 there, but 0 * NaN is not).
       const int valid = kend - t0;
       if (valid < TC_KT) {
@@ -383,7 +447,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           ok = false;
           break;
         }
-        unsigned char* vs = smem + C::OFF_KV + s_st * 2 * C::KV_BYTES + C::KV_BYTES;
+        unsigned char* vs = smem + C::OFF_V + s_st * C::KV_BYTES;
         const int zrows = TC_KT - valid;
         for (int idx = r; idx < zrows * 8 * C::PIECES; idx += TC_ROWS) {
           const int pc = idx / (zrows * 8);
@@ -449,8 +513,13 @@ cudaError_t launch_tc_t(const PrefillParams& p, const CUtensorMap& kmap, const C
     attr_smem[dev] = C::SMEM;
   }
   constexpr int TQ = TC_ROWS / G;
-  const dim3 grid((max_seqlen_q + TQ - 1) / TQ, batch, n_kv_head);
-  fn<<<grid, TC_THREADS, C::SMEM, stream>>>(p, kmap, vmap);
+  PrefillParams q = p;
+  q.batch = batch;
+  q.n_kv_head = n_kv_head;
+  q.q_tiles = (max_seqlen_q + TQ - 1) / TQ;
+  const int64_t ctas = int64_t(q.q_tiles) * batch * n_kv_head;
+  if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
+  fn<<<dim3(unsigned(ctas)), TC_THREADS, C::SMEM, stream>>>(q, kmap, vmap);
   return cudaGetLastError();
 }
 
