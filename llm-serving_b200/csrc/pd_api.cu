@@ -634,7 +634,7 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
     mode = g_prefill_mode;
   }
   const bool tc = mode == 0;
-  const int tile_tokens = tc ? prefill_tc_tile_tokens() : prefill_tile_tokens(head_dim);
+  const int tile_tokens = tc ? prefill_tc_tile_tokens(head_dim) : prefill_tile_tokens(head_dim);
   const int box_tokens = block_size < tile_tokens ? block_size : tile_tokens;
   CUtensorMap kmap, vmap;
   int st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype, box_tokens,

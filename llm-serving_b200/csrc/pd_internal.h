@@ -30,7 +30,7 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& kmap, cons
 
 // The same prefill on the tcgen05 tensor cores (TMEM accumulators); its pool maps have
 // one-piece boxes of at most prefill_tc_tile_tokens() tokens.
-int prefill_tc_tile_tokens();
+int prefill_tc_tile_tokens(int head_dim);
 cudaError_t launch_prefill_tc(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype,
                               int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,
                               cudaStream_t stream);

@@ -46,27 +46,35 @@ namespace pd {
 namespace {
 
 constexpr int TC_ROWS = 128;    // query rows per CTA (the MMA's M)
-constexpr int TC_KT = 64;       // keys per tile (the S MMA's N)
-constexpr int TC_THREADS = 192; // softmax warps 0-3, TMA warp 4, MMA warp 5
+constexpr int TC_SOFTMAX = 256; // softmax warps 0-7: two threads per query row, half a tile each
+constexpr int TC_THREADS = 320; // + TMA warp 8, MMA warp 9
+constexpr int TC_TMA_WARP = 8;
+constexpr int TC_MMA_WARP = 9;
 constexpr float TC_RESCALE = 8.f;  // log2 headroom before the running max is moved
 
 template <int D>
 struct TcCfg {
   static_assert(D == 64 || D == 128 || D == 256, "head_dim 64, 128 or 256");
-  static constexpr int PIECES = D / 64;                 // 128-byte pieces of a row
-  static constexpr int STAGES = D == 64 ? 6 : (D == 128 ? 4 : 2);  // stages of each of the K and V rings
-  static constexpr int PBUF = D == 256 ? 1 : 2;         // P buffers (each a hi and a lo tile)
+  // Keys per tile (the S MMA's N): 128 up to head_dim 128 -- fewer, larger MMAs, since the
+  // issuing lane, not the tensor pipe, bounds a CTA -- and 64 at head_dim 256 (shared memory).
+  static constexpr int KT = D <= 128 ? 128 : 64;
+  static constexpr int HK = KT / 2;                     // keys per softmax thread
+  static constexpr int PIECES = D / 64;                 // 128-byte pieces of a K/V/Q row
+  static constexpr int STAGES = 2;                      // stages of each of the K and V rings
+  static constexpr int PBUF = D == 64 ? 2 : 1;          // P buffers (each a hi and a lo tile)
   static constexpr int Q_BYTES = TC_ROWS * D * 2;
-  static constexpr int KV_BYTES = TC_KT * D * 2;        // one K (or V) tile
-  static constexpr int P_BYTES = TC_ROWS * TC_KT * 2;   // one P_hi (or P_lo) tile
-  static constexpr int TMEM_COLS = 2 * TC_KT + D <= 256 ? 256 : 512;
-  static constexpr int O_COL = 2 * TC_KT;               // S buffers at columns 0 and 64
-  // shared memory: [barriers and flags, 1 KB | Q | STAGES x K | STAGES x V | PBUF x (P_hi, P_lo)]
-  static constexpr int OFF_Q = 1024;
+  static constexpr int KV_BYTES = KT * D * 2;           // one K (or V) tile
+  static constexpr int P_BYTES = TC_ROWS * KT * 2;      // one P_hi (or P_lo) tile, KT / 64 pieces
+  static constexpr int TMEM_COLS = 2 * KT + D <= 256 ? 256 : 512;
+  static constexpr int O_COL = 2 * KT;                  // S buffers at columns 0 and KT
+  // shared memory: [barriers, flags, the pair exchange: 2 KB | Q | STAGES x K | STAGES x V |
+  // PBUF x (P_hi, P_lo)]
+  static constexpr int OFF_Q = 2048;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
   static constexpr int SMEM = OFF_P + PBUF * 2 * P_BYTES + 1024;  // + run-time 1 KB alignment
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 // Barrier slots (8 bytes each) in the first KB of shared memory.
@@ -81,8 +89,10 @@ struct TcBars {
   static constexpr int O_DONE = 30;   // [2] P.V of the tile that read P buffer i completed (commit)
   static constexpr int Q_FULL = 32;   // Q tile written by the softmax threads
   static constexpr int DRAIN = 33;    // every MMA of the CTA completed (commit at exit)
-  static constexpr int TMEM_SLOT = 512;  // byte offset: TMEM base address written by tcgen05.alloc
-  static constexpr int ABORT = 520;      // byte offset: a role's wait ran out
+  static constexpr int XCHG = 34;     // [4 warp pairs x 2 parities] the pair's maxima are posted
+  static constexpr int TMEM_SLOT = 344;  // byte offset: TMEM base address written by tcgen05.alloc
+  static constexpr int ABORT = 352;      // byte offset: a role's wait ran out
+  static constexpr int MAXES = 1024;     // byte offset: bf16 [2 parities][2 halves][128 rows]
 };
 
 // Single-thread bounded mbarrier wait (the TMA and MMA lanes run alone in their warps).
@@ -134,7 +144,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int kend = ctx + tok0 + ntok;  // keys this CTA needs: 0 .. kend - 1
   if (kend > lk) kend = lk;
   if (kend < 0) kend = 0;
-  const int ntiles = (kend + TC_KT - 1) / TC_KT;
+  const int ntiles = (kend + C::KT - 1) / C::KT;
   T* og = reinterpret_cast<T*>(p.out);
 
   if (ntiles == 0) {  // no visible key for any row of the CTA: exact zeros
@@ -163,16 +173,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(TcBars::S_FULL + i), 1);
-      mbar_init(bar(TcBars::S_FREE + i), TC_ROWS);
-      mbar_init(bar(TcBars::P_FULL + i), TC_ROWS);
+      mbar_init(bar(TcBars::S_FREE + i), TC_SOFTMAX);
+      mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX);
       mbar_init(bar(TcBars::O_DONE + i), 1);
     }
-    mbar_init(bar(TcBars::Q_FULL), TC_ROWS);
+    mbar_init(bar(TcBars::Q_FULL), TC_SOFTMAX);
+    for (int i = 0; i < 8; ++i) mbar_init(bar(TcBars::XCHG + i), 64);
     mbar_init(bar(TcBars::DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     tc::tmem_alloc(sbase + TcBars::TMEM_SLOT, C::TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -192,7 +203,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
   };
 
-  if (warp == 4) {
+  if (warp == TC_TMA_WARP) {
     // ---------------------------------------------------------------- TMA producer
     // The whole warp runs the loop (its waits are warp-collective) and keeps the row's block
     // table in a 32-entry register window, the next window prefetched, so no copy waits on a
@@ -207,7 +218,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       return page >= 0 && page < npages && page < p.max_blocks ? __ldg(trow + page) : 0;
     };
     // 64-entry window [win_base, win_base + 64): lane l holds entries win_base + l and + 32 + l.
-    // A tile spans at most 64 / block_size + 1 <= 9 pages, so once the window starts at or
+    // A tile spans at most KT / block_size + 1 <= 17 pages, so once the window starts at or
     // below the tile's first page and within 32 of it, every page of the tile is inside.
     int win_base = 0, win_cur = entry(lane), win_nxt = entry(32 + lane);
     auto advance_window = [&](int first_page) {  // warp-collective
@@ -224,7 +235,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       return i < 32 ? lo : hi;
     };
     // The copies of one K (or V) tile, one per (box, piece), issued in parallel: lane c issues
-    // copy c; boxes * PIECES <= (64 / 8) * 4 = 32 (box_tokens >= 8, head_dim <= 256).
+    // copy c; boxes * PIECES <= 32 (KT / 8 boxes of >= 8 tokens: 16 x 2 pieces up to head_dim
+    // 128, 8 x 4 at 256).
     auto issue_tile = [&](int t0, int boxes, uint32_t dst0, const CUtensorMap* map, uint32_t full_bar) {
       const int c = lane;
       const int jb = c / C::PIECES, pc = c - jb * C::PIECES;
@@ -232,7 +244,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int page = tok / bs;
       const int blk = block_of(page);
       if (jb < boxes)
-        tma_load_5d(dst0 + uint32_t(pc * TC_KT * 128 + jb * bt * 128), map, full_bar, 0, tok - page * bs, h, pc, blk);
+        tma_load_5d(dst0 + uint32_t(pc * C::KT * 128 + jb * bt * 128), map, full_bar, 0, tok - page * bs, h, pc, blk);
     };
     int issued = 0;
     bool ok = true;
@@ -244,8 +256,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = false;
         break;
       }
-      const int t0 = j * TC_KT;
-      const int covered = kend - t0 < TC_KT ? kend - t0 : TC_KT;
+      const int t0 = j * C::KT;
+      const int covered = kend - t0 < C::KT ? kend - t0 : C::KT;
       const int boxes = (covered + bt - 1) / bt;
       const uint32_t tx = uint32_t(boxes) * box_bytes * C::PIECES;
       advance_window(t0 / bs);
@@ -270,13 +282,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       warp_wait_phase(bar(TcBars::K_FULL + j % C::STAGES), uint32_t((j / C::STAGES) & 1), DRAIN_LIMIT_NS);
     for (int j = v_issued > C::STAGES ? v_issued - C::STAGES : 0; j < v_issued; ++j)
       warp_wait_phase(bar(TcBars::V_FULL + j % C::STAGES), uint32_t((j / C::STAGES) & 1), DRAIN_LIMIT_NS);
-  } else if (warp == 5) {
+  } else if (warp == TC_MMA_WARP) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = tc::instr_desc_f16(BF16, TC_ROWS, TC_KT, false, false);
+      constexpr uint32_t IDESC_S = tc::instr_desc_f16(BF16, TC_ROWS, C::KT, false, false);
       constexpr uint32_t IDESC_PV = tc::instr_desc_f16(BF16, TC_ROWS, D, false, true);
       const uint32_t o_tmem = tmem + C::O_COL;
       bool ok = thread_wait_phase(bar(TcBars::Q_FULL), 0u, wait_ns);
+      // Descriptors are built once; a step's operand is the base descriptor plus the step's byte
+      // offset >> 4 in the start-address field (every operand lies below 256 KB of shared
+      // memory, so the 14-bit field never carries into the next one).
+      const uint64_t q_desc = tc::smem_desc(q_addr, 16u, 1024u);
+      const uint64_t k_desc0 = tc::smem_desc(k_addr(0), 16u, 1024u);
+      const uint64_t v_desc0 = tc::smem_desc(v_addr(0), uint32_t(C::KT * 128), 1024u);
+      const uint64_t p_desc0 = tc::smem_desc(p_addr(0, 0), 16u, 1024u);
       // S_t = Q K_t^T into S buffer t % 2: head_dim / 16 steps of K = 16 (32 bytes of a row)
       auto issue_s = [&](int t) -> bool {
         const int s = t % C::STAGES;
@@ -284,12 +303,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (t >= 2 && !thread_wait_phase(bar(TcBars::S_FREE + (t & 1)), uint32_t(((t >> 1) - 1) & 1), wait_ns))
           return false;
         tc::fence_after_sync();
+        const uint64_t k_desc = k_desc0 + uint64_t((s * C::KV_BYTES) >> 4);
+        const uint32_t d_tmem = tmem + uint32_t((t & 1) * C::KT);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t koff = uint32_t((ks >> 2) * 16384 + (ks & 3) * 32);  // Q piece = 128 rows x 128 B
-          const uint64_t a = tc::smem_desc(q_addr + koff, 16u, 1024u);
-          const uint64_t bd = tc::smem_desc(k_addr(s) + uint32_t((ks >> 2) * TC_KT * 128 + (ks & 3) * 32), 16u, 1024u);
-          tc::mma_f16_ss(tmem + uint32_t((t & 1) * TC_KT), a, bd, IDESC_S, ks > 0);
+          const uint64_t a = q_desc + uint64_t(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4);  // Q piece: 128 x 128 B
+          const uint64_t bd = k_desc + uint64_t(((ks >> 2) * C::KT * 128 + (ks & 3) * 32) >> 4);
+          tc::mma_f16_ss(d_tmem, a, bd, IDESC_S, ks > 0);
         }
         tc::commit(bar(TcBars::S_FULL + (t & 1)));
         tc::commit(bar(TcBars::K_EMPTY + s));
@@ -310,15 +330,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         }
         tc::fence_after_sync();
-        // O += P_hi V + P_lo V: 64 keys in 4 steps of K = 16 (32 bytes of a P row, 16 V rows)
+        // O += P_hi V + P_lo V in steps of K = 16 keys (32 bytes of a P row, 16 V rows)
+        const uint64_t v_desc = v_desc0 + uint64_t((s * C::KV_BYTES) >> 4);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int part = 0; part < 2; ++part) {  // P_hi, then P_lo
+          const uint64_t p_desc = p_desc0 + uint64_t(((pb * 2 + part) * C::P_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < TC_KT / 16; ++kk) {
-            const uint64_t a = tc::smem_desc(p_addr(pb, half) + uint32_t(kk * 32), 16u, 1024u);
-            const uint64_t bd = tc::smem_desc(v_addr(s) + uint32_t(kk * 2048), uint32_t(TC_KT * 128), 1024u);
-            tc::mma_f16_ss(o_tmem, a, bd, IDESC_PV, j > 0 || half > 0 || kk > 0);
-          }
+          for (int kk = 0; kk < C::KT / 16; ++kk)  // P piece kk / 4 (128 rows x 128 B), 32 B per step
+            tc::mma_f16_ss(o_tmem, p_desc + uint64_t(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                           v_desc + uint64_t(kk * 128), IDESC_PV, j > 0 || part > 0 || kk > 0);
         }
         tc::commit(bar(TcBars::O_DONE + pb));
         tc::commit(bar(TcBars::V_EMPTY + s));
@@ -329,14 +349,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       thread_wait_phase(bar(TcBars::DRAIN), 0u, DRAIN_LIMIT_NS);
     }
   } else {
-    // ---------------------------------------------------------------- softmax warps 0-3
-    const int r = tid;  // query row = TMEM lane
+    // ---------------------------------------------------------------- softmax warps 0-7
+    // Warps w and w + 4 share the query rows of TMEM lanes 32 (w % 4) .. + 31: half = w / 4 takes
+    // keys HK half .. + HK - 1 of every tile (and columns D/2 half .. of O for rescales and output).
+    // Per tile the pair posts its halves' maxima, rounded down to bf16, and waits for the other's
+    // (an mbarrier of 64 arrivals, bounded): both threads of a row then take the same running max.
+    // Rounding down keeps the running max at or below the row's true maximum, so the largest
+    // probability is at least 1 and l >= 1 for every row with a visible key -- the reference's
+    // out = acc / max(l, 1) (model/triton_decode.py:639) then divides by l itself.
+    const int half = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // query row = TMEM lane
     const int i = r / G;
     const int hq = h * G + r % G;
-    {  // Q row -> the swizzled K-major Q tile (zeros past the chunk)
+    {  // this thread's half of the Q row -> the swizzled K-major Q tile (zeros past the chunk)
       const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st + int64_t(hq) * p.q_sh;
 #pragma unroll
-      for (int u = 0; u < D / 8; ++u) {
+      for (int uu = 0; uu < D / 16; ++uu) {
+        const int u = half * (D / 16) + uu;
         const uint4 v = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4*>(smem + C::OFF_Q + (u >> 3) * 16384 + sw128(r, u & 7)) = v;
       }
@@ -344,7 +373,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_arrive(bar(TcBars::Q_FULL));
     }
     const int row_last = i < ntok ? ctx + tok0 + i : kend - 1;  // padding rows: any finite row
-    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    __nv_bfloat16* maxes = reinterpret_cast<__nv_bfloat16*>(smem + TcBars::MAXES);
+    const uint32_t xbar = bar(TcBars::XCHG + (warp & 3) * 2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     // P.V of tile t has completed. Tile t's phase on its buffer's barrier is t / PBUF; the
@@ -352,6 +383,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // it was observed one buffer turn earlier, so the parity test is unambiguous.
     auto wait_pv = [&](int t) -> bool {
       return warp_wait_phase(bar(TcBars::O_DONE + t % C::PBUF), uint32_t((t / C::PBUF) & 1), wait_ns);
+    };
+    // The pair's rendezvous for tile t (barrier t & 1 of the pair, phase t / 2: the partner
+    // cannot post tile t + 2 before this thread has passed tile t + 1).
+    auto rendezvous = [&](int t) -> bool {
+      mbar_arrive(xbar + uint32_t((t & 1) * 8));
+      return warp_wait_phase(xbar + uint32_t((t & 1) * 8), uint32_t((t >> 1) & 1), wait_ns);
     };
     for (int j = 0; j < ntiles; ++j) {
       if (__any_sync(FULL_MASK, *abort_flag != 0)) {
@@ -364,31 +401,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         break;
       }
       tc::fence_after_sync();
-      uint32_t raw_s[TC_KT];
-      tc::ld_32x32b_x32(lane_base + uint32_t(sb * TC_KT), *reinterpret_cast<uint32_t(*)[32]>(raw_s));
-      tc::ld_32x32b_x32(lane_base + uint32_t(sb * TC_KT + 32), *reinterpret_cast<uint32_t(*)[32]>(raw_s + 32));
+      uint32_t raw_s[C::HK];
+#pragma unroll
+      for (int c = 0; c < C::HK; c += 32)
+        tc::ld_32x32b_x32(lane_base + uint32_t(sb * C::KT + half * C::HK + c),
+                          *reinterpret_cast<uint32_t(*)[32]>(raw_s + c));
       tc::wait_ld();
       tc::fence_before_sync();
       mbar_arrive(bar(TcBars::S_FREE + sb));
 
-      const int t0 = j * TC_KT;
-      float s[TC_KT];
+      const int c0 = j * C::KT + half * C::HK;  // key of raw_s[0]
+      float s[C::HK];
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
-      if (t0 + TC_KT - 1 <= row_last) {  // the whole tile is visible to this row
+      if (c0 + C::HK - 1 <= row_last) {  // every key of this half is visible to the row
 #pragma unroll
-        for (int c = 0; c < TC_KT; ++c) {
+        for (int c = 0; c < C::HK; ++c) {
           s[c] = __uint_as_float(raw_s[c]) * p.scale_log2;
           mx[c & 3] = fmaxf(mx[c & 3], s[c]);
         }
-      } else {  // the causal edge (or the row end) crosses the tile
+      } else {  // the causal edge (or the row end) crosses it
 #pragma unroll
-        for (int c = 0; c < TC_KT; ++c) {
+        for (int c = 0; c < C::HK; ++c) {
           const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
-          s[c] = t0 + c <= row_last ? x : -INFINITY;
+          s[c] = c0 + c <= row_last ? x : -INFINITY;
           mx[c & 3] = fmaxf(mx[c & 3], s[c]);
         }
       }
-      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // post this half's maximum (rounded down: never above the true one) and take the pair's
+      const __nv_bfloat16 mine = __float2bfloat16_rd(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+      maxes[((j & 1) * 2 + half) * TC_ROWS + r] = mine;
+      if (!rendezvous(j)) {
+        ok = false;
+        break;
+      }
+      const float tmax = fmaxf(__bfloat162float(mine), __bfloat162float(maxes[((j & 1) * 2 + (half ^ 1)) * TC_ROWS + r]));
       const bool move = tmax > m_run + TC_RESCALE || (m_run == -INFINITY && tmax > -INFINITY);
       const float alpha = !move ? 1.f : (m_run == -INFINITY ? 0.f : exp2f(m_run - tmax));
       // The P buffer of this tile was last read by P.V of tile j - PBUF.
@@ -397,63 +443,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         break;
       }
       const bool rescale = j > 0 && __any_sync(FULL_MASK, move);
-      if (rescale) {  // O *= alpha per row, once P.V of tile j - 1 has landed in O
+      if (rescale) {  // O *= alpha per row (this half's columns), once P.V of tile j - 1 landed
         if (!wait_pv(j - 1)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
           uint32_t o[32];
-          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
+          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
           tc::wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tc::st_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
+          tc::st_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
         }
         tc::wait_st();
       }
       if (move) m_run = tmax;
       l_run *= alpha;
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      // P = 2^(s - m) as hi + lo 16-bit pairs, written as this row of the two K-major P tiles
+      // P = 2^(s - m) as hi + lo 16-bit pairs: this half's 64 bytes of the row of each P tile
       const int pb = j % C::PBUF;
       unsigned char* phi = smem + C::OFF_P + (pb * 2) * C::P_BYTES;
       unsigned char* plo = phi + C::P_BYTES;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
-      for (int u = 0; u < TC_KT / 8; ++u) {
+      for (int uu = 0; uu < C::HK / 8; ++uu) {
+        const int u = half * (C::HK / 8) + uu;  // 16-byte unit of the P row: piece u / 8
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_ftz(s[u * 8 + 2 * e] - m_use);
-          const float p1 = ex2_ftz(s[u * 8 + 2 * e + 1] - m_use);
+          const float p0 = ex2_ftz(s[uu * 8 + 2 * e] - m_use);
+          const float p1 = ex2_ftz(s[uu * 8 + 2 * e + 1] - m_use);
           ls[e] += p0 + p1;
           hw[e] = E::pack2(p0, p1);
           float hf[2];
           E::unpack2(hw[e], hf);
           lw[e] = E::pack2(p0 - hf[0], p1 - hf[1]);
         }
-        *reinterpret_cast<uint4*>(phi + sw128(r, u)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(plo + sw128(r, u)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        const uint32_t at = uint32_t((u >> 3) * 16384) + sw128(r, u & 7);
+        *reinterpret_cast<uint4*>(phi + at) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(plo + at) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
       l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // The last tile: V rows past the row end must be zero (P is 0 there, but 0 * NaN is not).
-      const int valid = kend - t0;
-      if (valid < TC_KT) {
+      const int valid = kend - j * C::KT;
+      if (valid < C::KT) {
         const int s_st = j % C::STAGES;
         if (!warp_wait_phase(bar(TcBars::V_FULL + s_st), uint32_t((j / C::STAGES) & 1), wait_ns)) {
           ok = false;
           break;
         }
         unsigned char* vs = smem + C::OFF_V + s_st * C::KV_BYTES;
-        const int zrows = TC_KT - valid;
-        for (int idx = r; idx < zrows * 8 * C::PIECES; idx += TC_ROWS) {
+        const int zrows = C::KT - valid;
+        for (int idx = half * TC_ROWS + r; idx < zrows * 8 * C::PIECES; idx += TC_SOFTMAX) {
           const int pc = idx / (zrows * 8);
           const int rem = idx - pc * zrows * 8;
           const int row = valid + rem / 8;
-          *reinterpret_cast<uint4*>(vs + pc * TC_KT * 128 + row * 128 + ((rem & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vs + pc * C::KT * 128 + row * 128 + ((rem & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
         }
       }
       fence_proxy_async_smem();
@@ -461,25 +509,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_arrive(bar(TcBars::P_FULL + pb));
     }
     if (!ok) fail();
-    // ---- epilogue: out = O / max(l, 1) for the rows of the chunk
+    // ---- epilogue: out = O / max(l, 1) for the rows of the chunk; l is the sum of the pair's
+    // halves, exchanged through P buffer 0 (free once the last P.V has completed)
     if (ok && wait_pv(ntiles - 1)) {
-      tc::fence_after_sync();
-      const float inv = 1.f / fmaxf(l_run, 1.f);
-      T* dst = og + int64_t(q_begin + tok0 + i) * p.o_st + int64_t(hq) * p.o_sh;
+      float* lsum = reinterpret_cast<float*>(smem + C::OFF_P);
+      lsum[half * TC_ROWS + r] = l_run;
+      if (!rendezvous(ntiles)) {
+        fail();
+      } else {
+        tc::fence_after_sync();
+        const float inv = 1.f / fmaxf(l_run + lsum[(half ^ 1) * TC_ROWS + r], 1.f);
+        T* dst = og + int64_t(q_begin + tok0 + i) * p.o_st + int64_t(hq) * p.o_sh;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + c0), o);
-        tc::wait_ld();
-        if (i < ntok) {
+        for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
+          tc::wait_ld();
+          if (i < ntok) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 w;
-            w.x = E::pack2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-            w.y = E::pack2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-            w.z = E::pack2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-            w.w = E::pack2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + c0 + 8 * u) = w;
+            for (int u = 0; u < 4; ++u) {
+              uint4 w;
+              w.x = E::pack2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+              w.y = E::pack2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+              w.z = E::pack2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+              w.w = E::pack2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + oc + 8 * u) = w;
+            }
           }
         }
       }
@@ -491,7 +546,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // ---- every role is done with TMEM and shared memory: free the TMEM columns
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     __syncwarp();
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, C::TMEM_COLS);
@@ -537,7 +592,7 @@ cudaError_t launch_tc_g(const PrefillParams& p, const CUtensorMap& kmap, const C
 
 }  // namespace
 
-int prefill_tc_tile_tokens() { return TC_KT; }
+int prefill_tc_tile_tokens(int head_dim) { return head_dim <= 128 ? TcCfg<128>::KT : TcCfg<256>::KT; }
 
 cudaError_t launch_prefill_tc(const PrefillParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype,
                               int head_dim, int group, int max_seqlen_q, int batch, int n_kv_head,
