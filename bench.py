@@ -761,6 +761,7 @@ def config_sweep(reps: int = 5) -> None:
                           ("qwen35", 6)):
         wl = getattr(workloads, name)(device, n_layer=n_layer)
         plan = paged_decode_plan(wl.q[0], wl.k_pools, wl.v_pools, wl.block_table, wl.seqlen)
+        plan._native_plan.set_static_table(True)  # the workloads' tables are fixed, as PagedKV's are
         for layer in range(n_layer):
             plan.run(layer, wl.q[layer])
         torch.cuda.synchronize(device)

@@ -222,6 +222,16 @@ int pd_plan_run_append_rope(const pd_plan* plan, int32_t layer, const void* q, v
  * No reference counterpart (the reference launches one Triton kernel per call). */
 int pd_plan_set_overlap(pd_plan* plan, int32_t enable);
 
+/* pd_plan_set_static_table -- declares (fixed = 1) that the plan's block table keeps its
+ * contents for the plan's lifetime (a decode container's table is built once and never
+ * edited). Every plan caches its launches' work split in its workspace, keyed by a hash of the
+ * clamped lengths and the plan's shape, so the layers of one decode step compute the split once
+ * (model/paged.py:454-472 updates seqlen once per step); with a static table the cache also
+ * keeps each warp's first block-table windows, so a layer's first K/V copies need no table
+ * read. fixed = 0 (the default) re-reads the table, for callers that edit it in place between
+ * launches. No reference counterpart. */
+int pd_plan_set_static_table(pd_plan* plan, int32_t fixed);
+
 void pd_plan_destroy(pd_plan* plan);
 
 /* ---------------------------------------------------------------- split-KV partials

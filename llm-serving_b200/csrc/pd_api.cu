@@ -187,7 +187,7 @@ struct Launch {
 // stages with a full and an empty barrier each.
 size_t smem_for(bool cta, int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
   const size_t bars = round_up(size_t(cta ? 2 : warps) * stages * 8, 16);
-  const size_t arrays = round_up(size_t(1 + 32 + 3 * rows + 1) * 4, 16);
+  const size_t arrays = round_up(size_t(1 + 32 + 64 + 3 * rows + 1) * 4, 16);
   *arrays_off = int(bars);
   *stage_off = int(bars + arrays);
   return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(cta ? 1 : warps) * stages * stage_bytes;
@@ -225,12 +225,14 @@ int launch_shape(int dev, int batch, const Geometry& g, Launch* L) {
 }
 
 // Workspace: [header 256 B: epoch word (u32) at 0, exit counter (u64) at 8 | item arrival
-// counters (u64) | partial (m, l) slots | partial accumulator slots]. The header is the
-// kernel's own launch bookkeeping; nothing in the workspace needs to start at zero.
+// counters (u64) | partial (m, l) slots | partial accumulator slots | step records]. The header
+// is the kernel's own launch bookkeeping; nothing in the workspace needs to start at zero. The
+// step records (one per physical warp) cache a plan's work split across the layers of a step.
 struct WorkspaceLayout {
   size_t counters_off;
-  size_t ml_off, acc_off, total;
+  size_t ml_off, acc_off, step_off, total;
 };
+constexpr size_t kStepRecordBytes = 320;  // STEP_REC_BYTES in pd_decode_kernel.cuh
 
 WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, int head_dim,
                                  const Launch& L) {
@@ -240,7 +242,8 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
   const size_t workers = size_t(L.grid) * L.warps;
   w.ml_off = w.counters_off + round_up(size_t(rows < 1 ? 1 : rows) * n_kv_head * g.n_gchunks * 8, 256);
   w.acc_off = w.ml_off + round_up(workers * 2 * 2 * g.gt * 4, 256);
-  w.total = w.acc_off + round_up(workers * 2 * size_t(g.gt) * head_dim * 4, 256);
+  w.step_off = w.acc_off + round_up(workers * 2 * size_t(g.gt) * head_dim * 4, 256);
+  w.total = w.step_off + round_up(workers * kStepRecordBytes, 256);
   return w;
 }
 
@@ -365,6 +368,9 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   p.epoch_word = reinterpret_cast<unsigned*>(ws);
   p.exit_counter = reinterpret_cast<unsigned long long*>(ws + 8);
   p.tag_salt = layout_salt(P->ws, batch, n_kv_head * P->g.n_gchunks, 0);
+  p.step_rec = nullptr;  // plans switch the step cache on (pd_plan_create)
+  p.step_table = 0;
+
   p.counters = reinterpret_cast<unsigned long long*>(ws + P->ws.counters_off);
   p.ws_ml = reinterpret_cast<float*>(ws + P->ws.ml_off);
   p.ws_acc = reinterpret_cast<float*>(ws + P->ws.acc_off);
@@ -389,6 +395,17 @@ int prepare(Prepared* P, int64_t n_blocks, int32_t block_size, const int32_t* bl
   p.smem_arrays_off = P->L.arrays_off;
   p.smem_stage_off = P->L.stage_off;
   p.scale_log2 = scale_log2;
+  {  // everything besides the lengths that the work split depends on
+    uint64_t x = 0x243F6A8885A308D3ull;
+    const int64_t shape[] = {batch, n_head, n_kv_head, head_dim, dtype, block_size, max_blocks,
+                             P->L.grid, P->L.warps, P->L.stages, P->L.min_tiles, P->L.rows_per_launch,
+                             P->g.gt, P->g.mma, P->g.cta, p.row_cost};
+    for (int64_t v : shape) {
+      x = (x ^ uint64_t(v)) * 0x100000001B3ull;
+      x ^= x >> 29;
+    }
+    p.step_salt = x;
+  }
   return PD_OK;
 }
 
@@ -704,6 +721,9 @@ int pd_plan_create(pd_plan** plan, int32_t n_layer, const void* const* k_caches,
   }
   h->n_layer = n_layer;
   h->dtype = dtype;
+  // Step cache of the work split: one batch chunk per launch and the per-warp kernel.
+  if (batch <= h->P.L.rows_per_launch && !h->P.g.cta)
+    h->P.base.step_rec = static_cast<unsigned char*>(workspace) + h->P.ws.step_off;
   h->q_sh = head_dim;
   h->q_sb = int64_t(n_head) * head_dim;
   h->n_blocks = n_blocks;
@@ -739,6 +759,12 @@ int pd_plan_run(const pd_plan* plan, int32_t layer, const void* q, void* out, vo
   return run_prepared(plan->P, plan->kmaps[layer], plan->vmaps[layer], q, plan->q_sb, plan->q_sh, out,
                       plan->q_sb, plan->q_sh, nullptr, nullptr, nullptr, 0, plan->dtype,
                       static_cast<cudaStream_t>(stream), nullptr, plan->overlap != 0, &plan->seq);
+}
+
+int pd_plan_set_static_table(pd_plan* plan, int32_t fixed) {
+  if (plan == nullptr || fixed < 0 || fixed > 1) return PD_ERR_INVALID;
+  plan->P.base.step_table = fixed;
+  return PD_OK;
 }
 
 int pd_plan_set_overlap(pd_plan* plan, int32_t enable) {

@@ -396,6 +396,13 @@ struct DecodeParams {
   unsigned* epoch_word;
   unsigned long long* exit_counter;
   uint32_t tag_salt;  // even; mixed into the counters' tags (counter_tag in pd_decode_kernel.cuh)
+  // Step cache of the work split (nullptr: off). One STEP_REC_BYTES record per physical warp
+  // (blockIdx.x * warps + warp), written by a launch that computed its split and read by later
+  // launches whose lengths hash to the same key (the layers of one decode step): see
+  // StepRecord in pd_decode_kernel.cuh.
+  unsigned char* step_rec;
+  unsigned long long step_salt;  // the plan's geometry and launch shape, mixed into the key
+  int32_t step_table;  // 1: the block table never changes, so cached table windows are valid
   unsigned long long wait_ns;  // limit of mbarrier and arrival-counter waits
   // Fused append (append != 0): before the decode reads them, row b's new K and V rows
   // (app_k/app_v, same dtype as the pool, 16-byte aligned) are stored at logical position

@@ -146,6 +146,37 @@ __device__ __forceinline__ uint32_t counter_tag(uint32_t epoch, uint32_t salt) {
   return ((epoch << 1) | 1u) ^ salt;
 }
 
+// ---- step cache of the work split ------------------------------------------------------
+// A launch's split -- each warp's range of units (or of columns), its starting cursor, and the
+// first two 32-entry windows of that row's block table -- depends only on the clamped lengths
+// and the plan's geometry. The layers of a decode step share both, so the first layer of a
+// step computes the split and records it per warp, and the later layers, whose lengths hash to
+// the recorded key, take it from the record (loaded in the same round trip as the lengths)
+// instead of recomputing it and then waiting on the block table. A record's key is never 0,
+// so zero-filled memory never matches.
+constexpr int STEP_REC_BYTES = 320;
+constexpr int STEP_WIN_OFF = 64;  // 64 int32 table entries (the window and the next one)
+struct StepHeader {               // bytes 0..47 of a record
+  long long u0, u1;
+  int b, item, tile, workers;
+  int win_row, win_base;
+  unsigned long long key;
+};
+
+__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {  // SplitMix64 finaliser
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 // Arrival on the counter shared by the pieces of one split item; returns how many pieces of
 // this launch arrived before. Counters live in workspace memory that is never cleared and hold
 // (tag << 32) | count. Every launch re-tags its item counters with its own tag in the
@@ -204,8 +235,8 @@ __device__ __forceinline__ int worker_of(int64_t u, int64_t units, int workers) 
 
 // One launch's work for this thread's warp. It returns on several paths (no work, a failed
 // wait, the end of the warp's range); pd_decode_kernel then lets the warp leave the launch.
-// The launch's epoch sits in the first word of the shared arrays (written by thread 0 before
-// the body starts, read after the prologue's first block barrier).
+// The launch's epoch sits in the first word of the shared arrays (written by thread 0 in the
+// prologue, read after its block barriers).
 //
 // CTA = false: every warp runs its own TMA pipeline (per-warp stages, unit or column split).
 // CTA = true (used when a row has exactly one item per consumer warp): the CTA shares its
@@ -230,13 +261,16 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   const int row_stride = CTA ? p.n_kv_head * C::ROW_BYTES : C::ROW_BYTES;       // token to token
 
   // Dynamic shared memory:
-  // [mbarriers | epoch | warp_sums[32] | lens[B] | pre[B+1] | apos[B] | pad | stages].
+  // [mbarriers | epoch | warp_sums[32] | key_lo[32] | key_hi[32] | lens[B] | pre[B+1] | apos[B] |
+  //  pad | stages].
   // mbarriers: per-warp mode S per warp; CTA mode full[S] then empty[S].
   // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   const uint32_t* s_epoch = reinterpret_cast<const uint32_t*>(smem + p.smem_arrays_off);
   int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off) + 1;
-  int* lens = warp_sums + 32;
+  unsigned* key_lo = reinterpret_cast<unsigned*>(warp_sums + 32);  // per warp: XOR of its rows' hashes
+  unsigned* key_hi = key_lo + 32;
+  int* lens = reinterpret_cast<int*>(key_hi + 32);
   int* pre = lens + B;  // B + 1 entries: exclusive prefix of tiles per row
   int* apos = pre + B + 1;  // fused append: position to take from the source, or -1
   const uint32_t smem_base = smem_addr(smem);
@@ -246,6 +280,21 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   if (tid == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
+  }
+  // The stage mbarriers are initialised before this thread has any memory operation in
+  // flight: the init fence is a release and would otherwise wait for them (the counter
+  // re-tags below). Shared stages: thread 0, made visible by the prologue's block barriers.
+  if (CTA) {
+    if (tid == 0) {
+      for (int s = 0; s < S; ++s) {
+        mbar_init(smem_addr(bars + s), 1);
+        mbar_init(smem_addr(bars + S + s), nwarps);
+      }
+      fence_barrier_init();
+    }
+  } else if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(smem_addr(bars + warp * S + s), 1);
+    fence_barrier_init();
   }
 
   // ---- fused append: store every row's new K/V rows in the pools (16 B per thread) -----
@@ -295,17 +344,40 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     }
   };
 
+  // ---- this warp's step record, loaded alongside the lengths --------------------------
+  const bool use_step = !CTA && p.step_rec != nullptr;
+  unsigned char* my_rec =
+      use_step ? p.step_rec + (size_t(blockIdx.x) * (blockDim.x >> 5) + warp) * STEP_REC_BYTES : nullptr;
+  uint4 rec_a = make_uint4(0u, 0u, 0u, 0u), rec_b = rec_a, rec_c = rec_a;
+  int rec_win0 = 0, rec_win1 = 0;
+  if (use_step) {
+    if (lane == 0) {
+      rec_a = ld_cg_v4(my_rec);
+      rec_b = ld_cg_v4(my_rec + 16);
+      rec_c = ld_cg_v4(my_rec + 32);
+    }
+    if (p.step_table) {
+      rec_win0 = __ldcg(reinterpret_cast<const int*>(my_rec + STEP_WIN_OFF) + lane);
+      rec_win1 = __ldcg(reinterpret_cast<const int*>(my_rec + STEP_WIN_OFF) + 32 + lane);
+    }
+  }
+
   // ---- prologue: clamp lengths, tiles per row, block-wide exclusive scan -------------
+  unsigned long long launch_key = 0;  // the step key of these lengths (step cache)
   {
+    // The launch's epoch (thread 0) is loaded alongside the lengths, not before them.
+    const unsigned ep = tid == 0 ? *reinterpret_cast<volatile unsigned*>(p.epoch_word) : 0u;
     const int per = (B + blockDim.x - 1) / blockDim.x;
     const int b0 = min(B, tid * per);
     const int b1 = min(B, b0 + per);
     int local = 0;
+    unsigned long long key = 0;
     for (int b = b0; b < b1; ++b) {
       int len = __ldg(p.seqlen + b);
       const int64_t pos = p.append ? __ldg(p.app_pos + b) : -1;
       len = len < 0 ? 0 : (len > p.capacity ? p.capacity : len);
       lens[b] = len;
+      key ^= mix64(p.step_salt ^ ((unsigned long long)(unsigned)b << 32 | (unsigned)len));
       // Fused append: the tile holding the appended token takes it from the source when the
       // row reads that position (a position inside [0, len) is inside the table).
       if (p.append) apos[b] = pos >= 0 && pos < len ? int(pos) : -1;
@@ -318,6 +390,13 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       if (lane >= o) incl += y;
     }
     if (lane == 31) warp_sums[warp] = incl;
+    if (tid == 0) *reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off) = ep;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) key ^= __shfl_xor_sync(FULL_MASK, key, o);
+    if (lane == 0) {
+      key_lo[warp] = unsigned(key);
+      key_hi[warp] = unsigned(key >> 32);
+    }
     __syncthreads();
     if (warp == 0) {
       int v = lane < int(blockDim.x >> 5) ? warp_sums[lane] : 0;  // every warp's share
@@ -337,6 +416,11 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       run += (lens[b] + C::TILE - 1) >> C::LOG_TILE;
     }
     __syncthreads();
+    if (use_step) {
+      for (int i = 0; i < int(blockDim.x >> 5); ++i)
+        launch_key ^= (unsigned long long)key_hi[i] << 32 | key_lo[i];
+      launch_key = mix64(launch_key ^ p.step_salt) | 1ull;
+    }
   }
   const uint32_t epoch = *s_epoch;
 
@@ -420,7 +504,15 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   auto range_start = [&](int c) -> int64_t { return real_col(int64_t(c) * vcols / col_parts); };
   int workers = 0, w = 0;     // unit mode: worker count and this warp's worker id
   int64_t u0 = 0, u1 = 0;     // unit mode: range of units; column mode: range of real columns
-  if (colmode) {
+  // Step cache: this warp's record holds the split of these very lengths.
+  const bool cached =
+      use_step && __shfl_sync(FULL_MASK, lane == 0 && ((unsigned long long)rec_c.w << 32 | rec_c.z) == launch_key, 0);
+  if (!colmode) w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
+  if (cached) {
+    u0 = __shfl_sync(FULL_MASK, (long long)rec_a.y << 32 | rec_a.x, 0);
+    u1 = __shfl_sync(FULL_MASK, (long long)rec_a.w << 32 | rec_a.z, 0);
+    workers = __shfl_sync(FULL_MASK, int(rec_b.w), 0);
+  } else if (colmode) {
     if (int(blockIdx.x) < col_parts) {
       u0 = range_start(int(blockIdx.x));
       u1 = range_start(int(blockIdx.x) + 1);
@@ -445,11 +537,33 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         if (int64_t(aligned) * 20 >= int64_t(workers) * 19) workers = aligned;
       }
     }
-    w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
     u0 = w < workers ? int64_t(w) * units / workers : 0;
     u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
   }
+  // Records this launch's split of its warp (when it computed it): header by lane 0, the
+  // table windows the first copies used by every lane, made visible before the launch lets the
+  // next one start (enter_dependent).
+  auto write_record = [&](int rb, int ritem, int rtile, int wrow, int wbase, int wcur, int wnxt) {
+    if (!use_step || cached) return;
+    if (lane == 0) {
+      StepHeader hd;
+      hd.u0 = u0;
+      hd.u1 = u1;
+      hd.b = rb;
+      hd.item = ritem;
+      hd.tile = rtile;
+      hd.workers = workers;
+      hd.win_row = wrow;
+      hd.win_base = wbase;
+      hd.key = launch_key;
+      *reinterpret_cast<StepHeader*>(my_rec) = hd;
+    }
+    reinterpret_cast<int*>(my_rec + STEP_WIN_OFF)[lane] = wcur;
+    reinterpret_cast<int*>(my_rec + STEP_WIN_OFF)[32 + lane] = wnxt;
+    __threadfence();
+  };
   if (u0 >= u1) {
+    write_record(0, 0, 0, -1, 0, 0, 0);
     enter_dependent();
     store_appended();
     return epoch;
@@ -470,25 +584,22 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   unsigned char* my_stages = CTA ? stage_base : stage_base + size_t(warp) * S * C::STAGE_BYTES;
   const size_t stage_stride = CTA ? size_t(2) * kv_stage_bytes : size_t(C::STAGE_BYTES);
   if (CTA) {
-    if (tid == 0) {
-      for (int s = 0; s < S; ++s) {
-        mbar_init(smem_addr(my_bars + s), 1);
-        mbar_init(smem_addr(empty_bars + s), nwarps);
-      }
-      fence_barrier_init();
-    }
     __syncthreads();  // the CTA's warps share one range: all of them are here
   } else {
-    if (lane == 0) {
-      for (int s = 0; s < S; ++s) mbar_init(smem_addr(my_bars + s), 1);
-      fence_barrier_init();
-    }
     __syncwarp();
   }
 
   // Locate u0: the last row whose first unit (column) is <= u0 (rows with no tiles are skipped).
   Cursor cur;
-  {
+  if (cached) {
+    cur.b = __shfl_sync(FULL_MASK, int(rec_b.x), 0);
+    cur.item = __shfl_sync(FULL_MASK, int(rec_b.y), 0);
+    cur.tile = __shfl_sync(FULL_MASK, int(rec_b.z), 0);
+    cur.ntile = pre[cur.b + 1] - pre[cur.b];
+    cur.len = lens[cur.b];
+    cur.h = cur.item / p.n_gchunks;
+    cur.gc = cur.item - cur.h * p.n_gchunks;
+  } else {
     const int per_row = colmode ? 1 : items_per_row;
     int lo = 0, hi = B;  // find first i with per_row * pre[i] > u0
     while (lo < hi) {
@@ -512,6 +623,15 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   const int nbox = C::TILE >> log2_box;
   const uint32_t box_bytes = uint32_t(box_tokens) * uint32_t(row_stride);  // one copy
   int win_row = -1, win_base = 0, win_cur = 0, win_nxt = 0;
+  if (cached && p.step_table) {  // the recorded windows of this row's table (a fixed table)
+    const int rrow = __shfl_sync(FULL_MASK, int(rec_c.x), 0);
+    if (rrow >= 0) {
+      win_row = rrow;
+      win_base = __shfl_sync(FULL_MASK, int(rec_c.y), 0);
+      win_cur = rec_win0;
+      win_nxt = rec_win1;
+    }
+  }
 
   auto table_entry = [&](int row, int page, int npages) -> int {
     if (page < npages && page < p.max_blocks) return __ldg(p.table + int64_t(row) * p.bt_stride + page);
@@ -608,6 +728,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       advance(pc);
       if (pc.tile == 0 && issued + 1 < nunits) prefetch_q(pc);
     }
+    write_record(cur.b, cur.item, cur.tile, win_row, win_base, win_cur, win_nxt);
   }
   enter_dependent();
   store_appended();
@@ -1218,8 +1339,6 @@ __global__ void __launch_bounds__(CTA ? 288 : 256, 1)
     pd_decode_kernel(const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  if (threadIdx.x == 0) *reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off) =
-      *reinterpret_cast<volatile unsigned*>(p.epoch_word);
   const uint32_t epoch = decode_body<T, D, GT, CTA, MMA>(p, kmap, vmap, smem);
   __syncwarp();
   if ((threadIdx.x & 31) == 0)

@@ -91,6 +91,7 @@ _SIGNATURES = {
     ),
     "pd_plan_destroy": (None, [_c_ptr]),
     "pd_plan_set_overlap": (ctypes.c_int, [_c_ptr, _c_i32]),
+    "pd_plan_set_static_table": (ctypes.c_int, [_c_ptr, _c_i32]),
     "pd_kv_append_slots": (
         ctypes.c_int,
         [_c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64p, _c_i64p, _c_i32, _c_ptr, _c_i32, _c_ptr, _c_i64p,
@@ -384,6 +385,11 @@ class NativePlan:
         if bool(overlap) != self._overlap:
             check(self._lib.pd_plan_set_overlap(self._handle, int(bool(overlap))), "pd_plan_set_overlap")
             self._overlap = bool(overlap)
+
+    def set_static_table(self, fixed: bool) -> None:
+        """The block table keeps its contents for the plan's lifetime: the step cache may keep
+        table windows too (pd_plan_set_static_table)."""
+        check(self._lib.pd_plan_set_static_table(self._handle, int(bool(fixed))), "pd_plan_set_static_table")
 
     def run(self, layer: int, q, out, stream: int, overlap: bool = False) -> None:
         """``overlap``: the launch may start before the previous kernel of the stream ends

@@ -462,6 +462,9 @@ class PagedKV:
                 q3, self.pool._keys, self.pool._values, self._block_table_tensor, self._seqlen,
                 scale=1.0 / (self.head_dim ** 0.5),
             )
+            # The container's padded table is built once and never edited, so the plan's step
+            # cache may keep the table windows of each step's first copies too.
+            self._decode_plan._native_plan.set_static_table(True)
         return self._decode_plan
 
     def attend(self, layer: int, q: torch.Tensor, *, dropout_p: float = 0.0,
