@@ -252,9 +252,22 @@ WorkspaceLayout workspace_layout(int batch, int n_kv_head, const Geometry& g, in
 // 5-D (64 elements, token-in-block, head, 128-byte piece, block) with the 128-byte swizzle and
 // box (64, box_tokens, 1, head_dim / 64, 1), so a box lands piece-major: shared row
 // piece * box_tokens + token, 16-byte units XOR-permuted by the row index.
+// Swizzled pool views (the tensor-core kernels'):
+//  * SW_ROWS: (64 elements, token-in-block, head, 128-byte piece, block), a box = box_tokens rows
+//    of every piece (the decode kernel);
+//  * SW_ONE_PIECE: the same view, a box = one piece of box_tokens rows, so a kernel can place
+//    every piece of a tile where it wants it;
+//  * SW_GROUPED: (64 elements, 8 tokens, 128-byte piece, head, 8-token group of the pool), a box
+//    = box_tokens / 8 groups of every piece. It lands as [group][piece][8 rows of 128 bytes], so
+//    every piece's 8-row groups are evenly spaced (pieces x 1 KB apart) and a box carries all
+//    pieces at once -- 2x-4x larger copies than one-piece boxes. Needs the pool's blocks evenly
+//    spaced at block_size tokens (block stride = block_size x token stride) and block_size a
+//    multiple of 8.
+enum SwizzledView { SW_ROWS = 0, SW_ONE_PIECE = 1, SW_GROUPED = 2 };
+
 int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_size, int n_kv_head,
                 int head_dim, const int64_t* strides, int dtype, int box_tokens, int box_heads,
-                bool swizzle, bool one_piece = false) {
+                bool swizzle, int view = SW_ROWS) {
   if (load_encoder() != PD_OK) return PD_ERR_CUDA;
   const int es = elem_size(dtype);
   if (!aligned16(base)) return PD_ERR_INVALID;
@@ -265,6 +278,22 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
   CUtensorMapDataType t = dtype == PD_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                           : dtype == PD_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (swizzle && view == SW_GROUPED) {
+    if (es != 2 || head_dim % 64 != 0 || box_heads != 1 || block_size % 8 != 0 || box_tokens % 8 != 0 ||
+        strides[0] != int64_t(block_size) * strides[1])
+      return PD_ERR_INVALID;
+    const cuuint64_t dims[5] = {64u, 8u, cuuint64_t(head_dim / 64), cuuint64_t(n_kv_head),
+                                cuuint64_t(n_blocks) * cuuint64_t(block_size / 8)};
+    // Byte strides of dims 1..4: token, 128-byte piece, head, 8-token group.
+    const cuuint64_t gstr[4] = {cuuint64_t(strides[1] * es), 128u, cuuint64_t(strides[2] * es),
+                                cuuint64_t(strides[1] * es) * 8u};
+    const cuuint32_t box[5] = {64u, 8u, cuuint32_t(head_dim / 64), 1u, cuuint32_t(box_tokens / 8)};
+    const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+    CUresult r = g_encode(map, t, 5, const_cast<void*>(base), dims, gstr, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? PD_OK : PD_ERR_INVALID;
+  }
   if (swizzle) {
     if (es != 2 || head_dim % 64 != 0 || box_heads != 1) return PD_ERR_INVALID;
     const cuuint64_t dims[5] = {64u, cuuint64_t(block_size), cuuint64_t(n_kv_head), cuuint64_t(head_dim / 64),
@@ -272,9 +301,8 @@ int encode_pool(CUtensorMap* map, const void* base, int64_t n_blocks, int block_
     // Byte strides of dims 1..4: token-in-block, head, 128-byte piece, block.
     const cuuint64_t gstr[4] = {cuuint64_t(strides[1] * es), cuuint64_t(strides[2] * es), 128u,
                                 cuuint64_t(strides[0] * es)};
-    // one_piece: the box is one 128-byte piece of box_tokens rows, so a kernel can place every
-    // piece of a tile where it wants it (the tcgen05 prefill lands tiles piece-major).
-    const cuuint32_t box[5] = {64u, cuuint32_t(box_tokens), 1u, one_piece ? 1u : cuuint32_t(head_dim / 64), 1u};
+    const cuuint32_t box[5] = {64u, cuuint32_t(box_tokens), 1u,
+                               view == SW_ONE_PIECE ? 1u : cuuint32_t(head_dim / 64), 1u};
     const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
     CUresult r = g_encode(map, t, 5, const_cast<void*>(base), dims, gstr, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -653,14 +681,20 @@ int pd_prefill(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache, c
   const bool tc = mode == 0;
   const int tile_tokens = tc ? prefill_tc_tile_tokens(head_dim) : prefill_tile_tokens(head_dim);
   const int box_tokens = block_size < tile_tokens ? block_size : tile_tokens;
+  // The tcgen05 kernel takes grouped boxes where the pools' blocks are evenly spaced (the
+  // engine's layout), one-piece boxes otherwise.
+  const bool grouped = tc && k_strides[0] == int64_t(block_size) * k_strides[1] &&
+                       v_strides[0] == int64_t(block_size) * v_strides[1];
+  const int view = !tc ? SW_ROWS : (grouped ? SW_GROUPED : SW_ONE_PIECE);
   CUtensorMap kmap, vmap;
   int st = encode_pool(&kmap, k_cache, n_blocks, block_size, n_kv_head, head_dim, k_strides, dtype, box_tokens,
-                       1, true, tc);
+                       1, true, view);
   if (st != PD_OK) return st;
   st = encode_pool(&vmap, v_cache, n_blocks, block_size, n_kv_head, head_dim, v_strides, dtype, box_tokens, 1,
-                   true, tc);
+                   true, view);
   if (st != PD_OK) return st;
   PrefillParams p{};
+  p.grouped = grouped ? 1 : 0;
   p.q = q;
   p.q_st = q_st;
   p.q_sh = q_sh;

@@ -473,6 +473,10 @@ struct PrefillParams {
   float scale_log2;
   unsigned* err;
   unsigned long long wait_ns;  // limit of the stage waits
+  // tcgen05 kernel only: 1 when the pool maps are grouped (one copy per box of box_tokens
+  // tokens and every 128-byte piece, landing as 8-token groups of all pieces), 0 when each copy
+  // is one piece of box_tokens rows.
+  int32_t grouped;
   // Filled by the tcgen05 launcher (its grid is 1-D: query tile, kv head, row).
   int32_t batch;
   int32_t n_kv_head;

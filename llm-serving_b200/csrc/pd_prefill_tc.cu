@@ -11,22 +11,28 @@
 // How (one CTA = 128 query rows of one row's chunk and one kv head; a query row is a
 // (token, q head) pair of the kv head's group, token-major, so the group's heads share every
 // K/V tile):
-//  * warp 4 streams K and V tiles of 64 keys by TMA from the pool's 128-byte-swizzled map into
-//    two rings of shared-memory stages (6 / 4 / 2 each at head_dim 64 / 128 / 256), one copy
-//    per (block part, 64-element piece), so a tile lands piece-major -- the K-major (K) and
-//    MN-major (V) operand layouts of the MMA. A K stage is refilled as soon as its S MMA has
-//    read it, a V stage once its P.V has; the block table is read 32 entries at a time;
-//  * warp 5, lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K head_dim) into one of two
-//    TMEM buffers, and O += P_hi V_j + P_lo V_j (M 128, N head_dim, K 64) into the TMEM O
-//    accumulator, with S_{j+1} issued before waiting for P_j so the tensor cores work while
-//    the softmax runs; completion is signalled with tcgen05.commit on mbarriers;
-//  * warps 0-3 own one query row per thread (TMEM lane = row): they load the Q tile, then per
-//    key tile read their row of S from TMEM, mask (causal and row end), keep the running max
-//    in log2 units, write P as bf16/fp16 hi and lo rows into shared memory for the next MMA,
-//    and accumulate the normaliser. The running max is rescaled lazily: only when a row's tile
-//    max exceeds it by more than 2^8 is O rescaled in TMEM (P then stays below 2^8, which the
-//    hi + lo operands carry exactly as well as smaller values); the final out = O / max(l, 1)
-//    is unchanged by this.
+//  * warp 8 streams K and V tiles of KT keys (128 up to head_dim 128, 64 at 256) by TMA from the
+//    pool's 128-byte-swizzled map into two rings of shared-memory stages. With the engine's pool
+//    layout one copy carries a block part of every 64-element piece and lands as 8-token
+//    groups of all pieces (4 KB per 16 tokens at head_dim 128: a copy costs the TMA unit ~75
+//    cycles whatever its size up to a few KB, so 2 KB copies capped a CTA at ~28 bytes per
+//    cycle); other pool strides take one copy per (block part, piece). Either way every
+//    piece's 8-row groups are evenly spaced -- the K-major (K) and MN-major (V) operand layouts
+//    of the MMA. A K stage is refilled as soon as its S MMA has read it, a V stage once its
+//    P.V has; the block table is read 32 entries at a time;
+//  * warp 9, lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N KT, K head_dim; both operands in
+//    shared memory) into TMEM buffer j % 3, and O += P_hi V_j + P_lo V_j (M 128, N head_dim,
+//    K KT) into the TMEM O accumulator with P read from TMEM -- the softmax writes P over the
+//    S it came from -- and V from shared memory. S_{j+1} is issued before P.V_j, so the tensor
+//    cores work while the softmax runs; a buffer takes S_{j+3} once P.V_j has read its P.
+//    Completion is signalled with tcgen05.commit on mbarriers;
+//  * warps 0-7, two threads per query row (TMEM lane = row; warps w and w + 4 take the two
+//    halves of each key tile): they load the Q tile, then per key tile read their half row of
+//    S from TMEM, mask it (causal and row end), agree on the running max with the partner,
+//    and write P = 2^(s - m) as 16-bit hi and lo halves into the same TMEM columns, summing
+//    the normaliser. The running max is rescaled lazily: only when a row's tile max exceeds it
+//    by more than 2^8 is O rescaled in TMEM (P then stays below 2^8, which the hi + lo operands
+//    carry exactly as well as smaller values); the final out = O / max(l, 1) is unchanged.
 //  * Key tiles past the CTA's last query position are never loaded. V rows past the row end
 //    are zeroed in shared memory before use, so stale or NaN pool bytes never reach O.
 //  * Every wait is bounded (the launch's wait limit). A role whose wait runs out records
@@ -55,25 +61,31 @@ constexpr float TC_RESCALE = 8.f;  // log2 headroom before the running max is mo
 template <int D>
 struct TcCfg {
   static_assert(D == 64 || D == 128 || D == 256, "head_dim 64, 128 or 256");
-  // Keys per tile (the S MMA's N): 128 up to head_dim 128 -- fewer, larger MMAs, since the
-  // issuing lane, not the tensor pipe, bounds a CTA -- and 64 at head_dim 256 (shared memory).
+  // Keys per tile (the S MMA's N): 128 up to head_dim 128 -- fewer, larger MMAs, since every
+  // tcgen05.mma costs at least ~94 cycles to issue whatever its N -- and 64 at head_dim 256
+  // (shared memory).
   static constexpr int KT = D <= 128 ? 128 : 64;
   static constexpr int HK = KT / 2;                     // keys per softmax thread
   static constexpr int PIECES = D / 64;                 // 128-byte pieces of a K/V/Q row
-  static constexpr int STAGES = 2;                      // stages of each of the K and V rings
-  static constexpr int PBUF = D == 64 ? 2 : 1;          // P buffers (each a hi and a lo tile)
+  static constexpr int STAGES = D == 64 ? 4 : (D == 128 ? 3 : 2);  // stages of each K/V ring
+  static constexpr int NSB = 3;                         // TMEM S/P buffers
+  // S_{j+SLEAD} is issued before P.V_j, and K_{j+KLEAD} copied before V_j. Measured on the
+  // bench's prefill cases over (SLEAD, KLEAD) = (1, 0), (1, 1), (2, 0), (2, 1), (2, 2): (1, 0) is
+  // fastest up to head_dim 128, where a K copy ahead of V delays the P.V that waits for V;
+  // (1, 1) at 256.
+  static constexpr int SLEAD = 1;
+  static constexpr int KLEAD = D <= 128 ? 0 : 1;
+  static_assert(SLEAD < NSB && KLEAD <= STAGES && KLEAD <= 2, "lookahead");
   static constexpr int Q_BYTES = TC_ROWS * D * 2;
   static constexpr int KV_BYTES = KT * D * 2;           // one K (or V) tile
-  static constexpr int P_BYTES = TC_ROWS * KT * 2;      // one P_hi (or P_lo) tile, KT / 64 pieces
-  static constexpr int TMEM_COLS = 2 * KT + D <= 256 ? 256 : 512;
-  static constexpr int O_COL = 2 * KT;                  // S buffers at columns 0 and KT
-  // shared memory: [barriers, flags, the pair exchange: 2 KB | Q | STAGES x K | STAGES x V |
-  // PBUF x (P_hi, P_lo)]
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int O_COL = NSB * KT;                // S/P buffers at columns 0, KT, 2 KT
+  static_assert(O_COL + D <= TMEM_COLS, "TMEM columns");
+  // shared memory: [barriers, flags, the pair exchange: 2 KB | Q | STAGES x K | STAGES x V]
   static constexpr int OFF_Q = 2048;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int SMEM = OFF_P + PBUF * 2 * P_BYTES + 1024;  // + run-time 1 KB alignment
+  static constexpr int SMEM = OFF_V + STAGES * KV_BYTES + 1024;  // + run-time 1 KB alignment
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
@@ -83,17 +95,17 @@ struct TcBars {
   static constexpr int V_FULL = 6;    // [6] V tile landed
   static constexpr int K_EMPTY = 12;  // [6] S = Q K^T of the stage's tile completed (commit)
   static constexpr int V_EMPTY = 18;  // [6] P.V of the stage's tile completed (commit)
-  static constexpr int S_FULL = 24;   // [2] S buffer written (commit)
-  static constexpr int S_FREE = 26;   // [2] S buffer read by the 128 softmax threads
-  static constexpr int P_FULL = 28;   // [2] P buffer written (and O rescaled) by the softmax threads
-  static constexpr int O_DONE = 30;   // [2] P.V of the tile that read P buffer i completed (commit)
-  static constexpr int Q_FULL = 32;   // Q tile written by the softmax threads
-  static constexpr int DRAIN = 33;    // every MMA of the CTA completed (commit at exit)
-  static constexpr int XCHG = 34;     // [4 warp pairs x 2 parities] the pair's maxima are posted
+  static constexpr int S_FULL = 24;   // [3] S buffer written (commit)
+  static constexpr int P_FULL = 27;   // [3] P written over the buffer's S (and O rescaled) by the softmax
+  static constexpr int O_DONE = 30;   // [3] P.V of the tile that read buffer i's P completed (commit)
+  static constexpr int Q_FULL = 33;   // Q tile written by the softmax threads
+  static constexpr int DRAIN = 34;    // every MMA of the CTA completed (commit at exit)
+  static constexpr int XCHG = 35;     // [4 warp pairs x 2 parities] the pair's maxima are posted
   static constexpr int TMEM_SLOT = 344;  // byte offset: TMEM base address written by tcgen05.alloc
   static constexpr int ABORT = 352;      // byte offset: a role's wait ran out
   static constexpr int MAXES = 1024;     // byte offset: bf16 [2 parities][2 halves][128 rows]
 };
+static_assert((TcBars::XCHG + 8) * 8 <= TcBars::TMEM_SLOT, "barrier slots");
 
 // Single-thread bounded mbarrier wait (the TMA and MMA lanes run alone in their warps).
 __device__ __forceinline__ bool thread_wait_phase(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
@@ -155,6 +167,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     return;
   }
 
+  // Loads that nothing else waits for are issued before the barrier set-up: the TMA warp's first
+  // block-table window (entries past the row's pages are loaded but never used) and each softmax
+  // thread's half of its Q row (zeros past the chunk).
+  int pre_win0 = 0, pre_win1 = 0;
+  uint4 qv[D / 16];
+  if (warp == TC_TMA_WARP) {
+    const int32_t* trow0 = p.table + int64_t(b) * p.bt_stride;
+    pre_win0 = lane < p.max_blocks ? __ldg(trow0 + lane) : 0;
+    pre_win1 = 32 + lane < p.max_blocks ? __ldg(trow0 + 32 + lane) : 0;
+  } else if (warp < TC_SOFTMAX / 32) {
+    const int r = (warp & 3) * 32 + lane, i = r / G;
+    const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st +
+                   int64_t(h * G + r % G) * p.q_sh;
+#pragma unroll
+    for (int uu = 0; uu < D / 16; ++uu)
+      qv[uu] = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + (warp >> 2) * (D / 16) + uu)
+                        : make_uint4(0u, 0u, 0u, 0u);
+  }
+
   const uint32_t raw = smem_addr(smem_raw);
   unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   const uint32_t sbase = smem_addr(smem);
@@ -171,9 +202,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(bar(TcBars::K_EMPTY + s), 1);
       mbar_init(bar(TcBars::V_EMPTY + s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NSB; ++i) {
       mbar_init(bar(TcBars::S_FULL + i), 1);
-      mbar_init(bar(TcBars::S_FREE + i), TC_SOFTMAX);
       mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX);
       mbar_init(bar(TcBars::O_DONE + i), 1);
     }
@@ -195,13 +225,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t q_addr = sbase + C::OFF_Q;
   auto k_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_K + s * C::KV_BYTES); };
   auto v_addr = [&](int s) -> uint32_t { return sbase + uint32_t(C::OFF_V + s * C::KV_BYTES); };
-  auto p_addr = [&](int pb, int lo) -> uint32_t {
-    return sbase + uint32_t(C::OFF_P + (pb * 2 + lo) * C::P_BYTES);
-  };
   auto fail = [&]() {
     *abort_flag = 1;
     atomicOr(p.err, DEVERR_WAIT_TIMEOUT);
   };
+  // Where row r (a key) of 128-byte piece pc of a K/V tile sits: 8-row groups `gstride` bytes
+  // apart, pieces `pstride` apart. Grouped copies land [group][piece][8 rows]; one-piece copies
+  // land piece-major, [piece][row].
+  const uint32_t gstride = p.grouped ? uint32_t(C::PIECES * 1024) : 1024u;
+  const uint32_t pstride = p.grouped ? 1024u : uint32_t(C::KT * 128);
 
   if (warp == TC_TMA_WARP) {
     // ---------------------------------------------------------------- TMA producer
@@ -218,9 +250,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       return page >= 0 && page < npages && page < p.max_blocks ? __ldg(trow + page) : 0;
     };
     // 64-entry window [win_base, win_base + 64): lane l holds entries win_base + l and + 32 + l.
-    // A tile spans at most KT / block_size + 1 <= 17 pages, so once the window starts at or
-    // below the tile's first page and within 32 of it, every page of the tile is inside.
-    int win_base = 0, win_cur = entry(lane), win_nxt = entry(32 + lane);
+    // Tiles start on KT-token boundaries, so a tile spans at most KT / block_size <= 16 pages (a
+    // block of KT tokens or more holds a whole tile); once the window starts at or below the
+    // tile's first page and within 32 of it, every page of the tile is inside.
+    int win_base = 0, win_cur = pre_win0, win_nxt = pre_win1;
     auto advance_window = [&](int first_page) {  // warp-collective
       while (first_page >= win_base + 32) {
         win_base += 32;
@@ -234,50 +267,85 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int hi = __shfl_sync(FULL_MASK, win_nxt, i & 31);
       return i < 32 ? lo : hi;
     };
-    // The copies of one K (or V) tile, one per (box, piece), issued in parallel: lane c issues
-    // copy c; boxes * PIECES <= 32 (KT / 8 boxes of >= 8 tokens: 16 x 2 pieces up to head_dim
-    // 128, 8 x 4 at 256).
-    auto issue_tile = [&](int t0, int boxes, uint32_t dst0, const CUtensorMap* map, uint32_t full_bar) {
-      const int c = lane;
-      const int jb = c / C::PIECES, pc = c - jb * C::PIECES;
-      const int tok = t0 + jb * bt;
-      const int page = tok / bs;
-      const int blk = block_of(page);
-      if (jb < boxes)
-        tma_load_5d(dst0 + uint32_t(pc * C::KT * 128 + jb * bt * 128), map, full_bar, 0, tok - page * bs, h, pc, blk);
-    };
-    int issued = 0;
-    bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      if (__any_sync(FULL_MASK, *abort_flag != 0)) break;
-      const int s = j % C::STAGES;
-      const uint32_t par = uint32_t((j / C::STAGES - 1) & 1);
-      if (j >= C::STAGES && !warp_wait_phase(bar(TcBars::K_EMPTY + s), par, wait_ns)) {
-        ok = false;
-        break;
-      }
-      const int t0 = j * C::KT;
+    // The copies of one K (or V) tile, issued in parallel: lane c issues copy c. Grouped: one
+    // copy per box of bt tokens and every piece (boxes <= KT / 8 <= 16), at group coordinate
+    // block * bs / 8 + (token in block) / 8. One-piece: one copy per (box, piece) (boxes *
+    // PIECES <= 32: 16 x 2 pieces up to head_dim 128, 8 x 4 at 256). `blk` is the block of this
+    // lane's box.
+    const int my_box = p.grouped ? lane : lane / C::PIECES;
+    const int my_piece = p.grouped ? 0 : lane - my_box * C::PIECES;
+    auto issue_tile = [&](int t, bool is_k, int blk) {
+      const int t0 = t * C::KT;
       const int covered = kend - t0 < C::KT ? kend - t0 : C::KT;
       const int boxes = (covered + bt - 1) / bt;
-      const uint32_t tx = uint32_t(boxes) * box_bytes * C::PIECES;
-      advance_window(t0 / bs);
-      if (lane == 0) mbar_arrive_expect_tx(bar(TcBars::K_FULL + s), tx);
+      const int s = t % C::STAGES;
+      const uint32_t full = bar((is_k ? TcBars::K_FULL : TcBars::V_FULL) + s);
+      const uint32_t dst0 = is_k ? k_addr(s) : v_addr(s);
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
+      if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(boxes) * box_bytes * C::PIECES);
       __syncwarp();
-      issue_tile(t0, boxes, k_addr(s), &kmap, bar(TcBars::K_FULL + s));
-      if (j >= C::STAGES && !warp_wait_phase(bar(TcBars::V_EMPTY + s), par, wait_ns)) {
+      const int tok = t0 + my_box * bt;
+      const int page = tok / bs;
+      if (my_box < boxes) {
+        if (p.grouped)
+          tma_load_5d(dst0 + uint32_t(my_box * bt * 128 * C::PIECES), map, full, 0, 0, 0, h,
+                      blk * (bs >> 3) + ((tok - page * bs) >> 3));
+        else
+          tma_load_5d(dst0 + uint32_t(my_piece * C::KT * 128 + my_box * bt * 128), map, full, 0, tok - page * bs, h,
+                      my_piece, blk);
+      }
+    };
+    // K runs KLEAD tiles ahead of V (the MMA lane consumes S_{j+SLEAD} before P.V_j).
+    // Each K issue looks up its boxes' blocks and keeps them for the tile's V (a 3-entry ring:
+    // K_t is issued after V_{t-3}). K_t goes into its stage once S_{t - STAGES} has read it, V_t
+    // once P.V_{t - STAGES} has.
+    int ring0 = 0, ring1 = 0, ring2 = 0;
+    auto issue_k = [&](int t) -> bool {
+      const int s = t % C::STAGES;
+      if (t >= C::STAGES &&
+          !warp_wait_phase(bar(TcBars::K_EMPTY + s), uint32_t((t / C::STAGES - 1) & 1), wait_ns))
+        return false;
+      advance_window(t * C::KT / bs);
+      const int blk = block_of((t * C::KT + my_box * bt) / bs);
+      const int r3 = t % 3;
+      ring0 = r3 == 0 ? blk : ring0;
+      ring1 = r3 == 1 ? blk : ring1;
+      ring2 = r3 == 2 ? blk : ring2;
+      issue_tile(t, true, blk);
+      return true;
+    };
+    auto issue_v = [&](int t) -> bool {
+      const int s = t % C::STAGES;
+      if (t >= C::STAGES &&
+          !warp_wait_phase(bar(TcBars::V_EMPTY + s), uint32_t((t / C::STAGES - 1) & 1), wait_ns))
+        return false;
+      const int r3 = t % 3;
+      issue_tile(t, false, r3 == 0 ? ring0 : (r3 == 1 ? ring1 : ring2));
+      return true;
+    };
+    int k_issued = 0, v_issued = 0;
+    bool ok = true;
+    for (int t = 0; ok && t < C::KLEAD && t < ntiles; ++t) {
+      ok = issue_k(t);
+      if (ok) k_issued = t + 1;
+    }
+    for (int j = 0; ok && j < ntiles; ++j) {
+      if (__any_sync(FULL_MASK, *abort_flag != 0)) break;
+      if (j + C::KLEAD < ntiles) {
+        if (!issue_k(j + C::KLEAD)) {
+          ok = false;
+          break;
+        }
+        k_issued = j + C::KLEAD + 1;
+      }
+      if (!issue_v(j)) {
         ok = false;
-        issued = -(j + 1);  // K of tile j is in flight, V is not
         break;
       }
-      if (lane == 0) mbar_arrive_expect_tx(bar(TcBars::V_FULL + s), tx);
-      __syncwarp();
-      issue_tile(t0, boxes, v_addr(s), &vmap, bar(TcBars::V_FULL + s));
-      issued = j + 1;
+      v_issued = j + 1;
     }
     if (!ok && lane == 0) fail();
     // never leave with a copy in flight: the last STAGES tiles' copies must have landed
-    const int k_issued = issued < 0 ? -issued : issued;
-    const int v_issued = issued < 0 ? -issued - 1 : issued;
     for (int j = k_issued > C::STAGES ? k_issued - C::STAGES : 0; j < k_issued; ++j)
       warp_wait_phase(bar(TcBars::K_FULL + j % C::STAGES), uint32_t((j / C::STAGES) & 1), DRAIN_LIMIT_NS);
     for (int j = v_issued > C::STAGES ? v_issued - C::STAGES : 0; j < v_issued; ++j)
@@ -293,54 +361,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // offset >> 4 in the start-address field (every operand lies below 256 KB of shared
       // memory, so the 14-bit field never carries into the next one).
       const uint64_t q_desc = tc::smem_desc(q_addr, 16u, 1024u);
-      const uint64_t k_desc0 = tc::smem_desc(k_addr(0), 16u, 1024u);
-      const uint64_t v_desc0 = tc::smem_desc(v_addr(0), uint32_t(C::KT * 128), 1024u);
-      const uint64_t p_desc0 = tc::smem_desc(p_addr(0, 0), 16u, 1024u);
-      // S_t = Q K_t^T into S buffer t % 2: head_dim / 16 steps of K = 16 (32 bytes of a row)
+      // K: K-major B operand (rows = keys), 8-row groups gstride apart, the next 64 elements of
+      // head_dim pstride further. V: MN-major B operand, 64-element head_dim blocks pstride
+      // apart (leading byte offset), 8-key groups gstride apart (stride byte offset).
+      const uint64_t k_desc0 = tc::smem_desc(k_addr(0), 16u, gstride);
+      const uint64_t v_desc0 = tc::smem_desc(v_addr(0), pstride, gstride);
+      // S_t = Q K_t^T into buffer t % 3 (head_dim / 16 steps of K = 16: 32 bytes of a row), once
+      // P.V of tile t - 3 has read the P that buffer held.
       auto issue_s = [&](int t) -> bool {
         const int s = t % C::STAGES;
+        const int sb = t % C::NSB;
         if (!thread_wait_phase(bar(TcBars::K_FULL + s), uint32_t((t / C::STAGES) & 1), wait_ns)) return false;
-        if (t >= 2 && !thread_wait_phase(bar(TcBars::S_FREE + (t & 1)), uint32_t(((t >> 1) - 1) & 1), wait_ns))
+        if (t >= C::NSB && !thread_wait_phase(bar(TcBars::O_DONE + sb), uint32_t((t / C::NSB - 1) & 1), wait_ns))
           return false;
         tc::fence_after_sync();
         const uint64_t k_desc = k_desc0 + uint64_t((s * C::KV_BYTES) >> 4);
-        const uint32_t d_tmem = tmem + uint32_t((t & 1) * C::KT);
+        const uint32_t d_tmem = tmem + uint32_t(sb * C::KT);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint64_t a = q_desc + uint64_t(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4);  // Q piece: 128 x 128 B
-          const uint64_t bd = k_desc + uint64_t(((ks >> 2) * C::KT * 128 + (ks & 3) * 32) >> 4);
+          const uint64_t bd = k_desc + uint64_t(((ks >> 2) * pstride + (ks & 3) * 32) >> 4);
           tc::mma_f16_ss(d_tmem, a, bd, IDESC_S, ks > 0);
         }
-        tc::commit(bar(TcBars::S_FULL + (t & 1)));
+        tc::commit(bar(TcBars::S_FULL + sb));
         tc::commit(bar(TcBars::K_EMPTY + s));
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int t = 0; ok && t < C::SLEAD && t < ntiles; ++t) ok = issue_s(t);
       for (int j = 0; ok && j < ntiles; ++j) {
         if (*abort_flag) break;
-        if (j + 1 < ntiles && !issue_s(j + 1)) {
+        // S_{j+SLEAD} goes ahead of P.V_j, so the tensor pipe has work while the softmax of tile j
+        // runs (S_t reuses the buffer P.V_{t-3} has read).
+        if (j + C::SLEAD < ntiles && !issue_s(j + C::SLEAD)) {
           ok = false;
           break;
         }
-        const int pb = j % C::PBUF;
+        const int sb = j % C::NSB;
         const int s = j % C::STAGES;
-        if (!thread_wait_phase(bar(TcBars::P_FULL + pb), uint32_t((j / C::PBUF) & 1), wait_ns) ||
+        if (!thread_wait_phase(bar(TcBars::P_FULL + sb), uint32_t((j / C::NSB) & 1), wait_ns) ||
             !thread_wait_phase(bar(TcBars::V_FULL + s), uint32_t((j / C::STAGES) & 1), wait_ns)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
-        // O += P_hi V + P_lo V in steps of K = 16 keys (32 bytes of a P row, 16 V rows)
+        // O += P_hi V + P_lo V in steps of K = 16 keys (8 TMEM columns of P, two 8-row groups of
+        // V). Half h of
+        // the buffer (columns h KT/2 ..) holds keys h KT/2 .. of the tile: hi in its first KT/4
+        // columns, lo in the next KT/4.
         const uint64_t v_desc = v_desc0 + uint64_t((s * C::KV_BYTES) >> 4);
+        const uint32_t p_tmem = tmem + uint32_t(sb * C::KT);
 #pragma unroll
         for (int part = 0; part < 2; ++part) {  // P_hi, then P_lo
-          const uint64_t p_desc = p_desc0 + uint64_t(((pb * 2 + part) * C::P_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < C::KT / 16; ++kk)  // P piece kk / 4 (128 rows x 128 B), 32 B per step
-            tc::mma_f16_ss(o_tmem, p_desc + uint64_t(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
-                           v_desc + uint64_t(kk * 128), IDESC_PV, j > 0 || part > 0 || kk > 0);
+          for (int kk = 0; kk < C::KT / 16; ++kk) {
+            const int hh = kk / (C::HK / 16), within = kk % (C::HK / 16);
+            tc::mma_f16_ts(o_tmem, p_tmem + uint32_t(hh * C::HK + part * (C::HK / 2) + within * 8),
+                           v_desc + uint64_t((kk * 2 * gstride) >> 4), IDESC_PV, j > 0 || part > 0 || kk > 0);
+          }
         }
-        tc::commit(bar(TcBars::O_DONE + pb));
+        tc::commit(bar(TcBars::O_DONE + sb));
         tc::commit(bar(TcBars::V_EMPTY + s));
       }
       if (!ok) fail();
@@ -361,13 +440,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int r = (warp & 3) * 32 + lane;  // query row = TMEM lane
     const int i = r / G;
     const int hq = h * G + r % G;
-    {  // this thread's half of the Q row -> the swizzled K-major Q tile (zeros past the chunk)
-      const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st + int64_t(hq) * p.q_sh;
+    {  // this thread's half of the Q row (loaded at entry) -> the swizzled K-major Q tile
 #pragma unroll
       for (int uu = 0; uu < D / 16; ++uu) {
         const int u = half * (D / 16) + uu;
-        const uint4 v = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + u) : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(smem + C::OFF_Q + (u >> 3) * 16384 + sw128(r, u & 7)) = v;
+        *reinterpret_cast<uint4*>(smem + C::OFF_Q + (u >> 3) * 16384 + sw128(r, u & 7)) = qv[uu];
       }
       fence_proxy_async_smem();
       mbar_arrive(bar(TcBars::Q_FULL));
@@ -378,11 +455,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t xbar = bar(TcBars::XCHG + (warp & 3) * 2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    // P.V of tile t has completed. Tile t's phase on its buffer's barrier is t / PBUF; the
-    // barrier cannot pass it before this thread writes that buffer again, and the phase before
-    // it was observed one buffer turn earlier, so the parity test is unambiguous.
+    // P.V of tile t has completed. Tile t's phase on its buffer's barrier is t / 3; the barrier
+    // cannot pass it before this thread writes P_{t+3}, and the phase before it (P.V of tile
+    // t - 3) completed before S_t was issued, which this thread has seen, so the parity test is
+    // unambiguous.
     auto wait_pv = [&](int t) -> bool {
-      return warp_wait_phase(bar(TcBars::O_DONE + t % C::PBUF), uint32_t((t / C::PBUF) & 1), wait_ns);
+      return warp_wait_phase(bar(TcBars::O_DONE + t % C::NSB), uint32_t((t / C::NSB) & 1), wait_ns);
     };
     // The pair's rendezvous for tile t (barrier t & 1 of the pair, phase t / 2: the partner
     // cannot post tile t + 2 before this thread has passed tile t + 1).
@@ -395,20 +473,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = false;
         break;
       }
-      const int sb = j & 1;
-      if (!warp_wait_phase(bar(TcBars::S_FULL + sb), uint32_t((j >> 1) & 1), wait_ns)) {
+      const int sb = j % C::NSB;
+      if (!warp_wait_phase(bar(TcBars::S_FULL + sb), uint32_t((j / C::NSB) & 1), wait_ns)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
+      // this thread's half row of S: columns half KT/2 .. + KT/2 - 1 of the buffer
+      const uint32_t s_tmem = lane_base + uint32_t(sb * C::KT + half * C::HK);
       uint32_t raw_s[C::HK];
 #pragma unroll
       for (int c = 0; c < C::HK; c += 32)
-        tc::ld_32x32b_x32(lane_base + uint32_t(sb * C::KT + half * C::HK + c),
-                          *reinterpret_cast<uint32_t(*)[32]>(raw_s + c));
+        tc::ld_32x32b_x32(s_tmem + uint32_t(c), *reinterpret_cast<uint32_t(*)[32]>(raw_s + c));
       tc::wait_ld();
-      tc::fence_before_sync();
-      mbar_arrive(bar(TcBars::S_FREE + sb));
 
       const int c0 = j * C::KT + half * C::HK;  // key of raw_s[0]
       float s[C::HK];
@@ -437,11 +514,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const float tmax = fmaxf(__bfloat162float(mine), __bfloat162float(maxes[((j & 1) * 2 + (half ^ 1)) * TC_ROWS + r]));
       const bool move = tmax > m_run + TC_RESCALE || (m_run == -INFINITY && tmax > -INFINITY);
       const float alpha = !move ? 1.f : (m_run == -INFINITY ? 0.f : exp2f(m_run - tmax));
-      // The P buffer of this tile was last read by P.V of tile j - PBUF.
-      if (j >= C::PBUF && !wait_pv(j - C::PBUF)) {
-        ok = false;
-        break;
-      }
       const bool rescale = j > 0 && __any_sync(FULL_MASK, move);
       if (rescale) {  // O *= alpha per row (this half's columns), once P.V of tile j - 1 landed
         if (!wait_pv(j - 1)) {
@@ -463,14 +535,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (move) m_run = tmax;
       l_run *= alpha;
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      // P = 2^(s - m) as hi + lo 16-bit pairs: this half's 64 bytes of the row of each P tile
-      const int pb = j % C::PBUF;
-      unsigned char* phi = smem + C::OFF_P + (pb * 2) * C::P_BYTES;
-      unsigned char* plo = phi + C::P_BYTES;
+      // P = 2^(s - m) as hi + lo 16-bit pairs, written over this thread's own S columns (read
+      // above): hi in the first KT/4 columns, lo in the next KT/4, two keys per column, the lower
+      // key in the low half -- the K-major A layout of the P.V MMA.
       float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int uu = 0; uu < C::HK / 8; ++uu) {
-        const int u = half * (C::HK / 8) + uu;  // 16-byte unit of the P row: piece u / 8
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -482,9 +552,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           E::unpack2(hw[e], hf);
           lw[e] = E::pack2(p0 - hf[0], p1 - hf[1]);
         }
-        const uint32_t at = uint32_t((u >> 3) * 16384) + sw128(r, u & 7);
-        *reinterpret_cast<uint4*>(phi + at) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(plo + at) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        tc::st_32x32b_x4(s_tmem + uint32_t(uu * 4), hw[0], hw[1], hw[2], hw[3]);
+        tc::st_32x32b_x4(s_tmem + uint32_t(C::HK / 2 + uu * 4), lw[0], lw[1], lw[2], lw[3]);
       }
       l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // The last tile: V rows past the row end must be zero (P is 0 there, but 0 * NaN is not).
@@ -501,18 +570,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const int pc = idx / (zrows * 8);
           const int rem = idx - pc * zrows * 8;
           const int row = valid + rem / 8;
-          *reinterpret_cast<uint4*>(vs + pc * C::KT * 128 + row * 128 + ((rem & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vs + (row >> 3) * gstride + pc * pstride + (row & 7) * 128 + ((rem & 7) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
         }
       }
       fence_proxy_async_smem();
+      tc::wait_st();
       tc::fence_before_sync();
-      mbar_arrive(bar(TcBars::P_FULL + pb));
+      mbar_arrive(bar(TcBars::P_FULL + sb));
     }
     if (!ok) fail();
     // ---- epilogue: out = O / max(l, 1) for the rows of the chunk; l is the sum of the pair's
-    // halves, exchanged through P buffer 0 (free once the last P.V has completed)
+    // halves, exchanged through K stage 0 (free once the last P.V has completed: every copy has
+    // landed and been read by then)
     if (ok && wait_pv(ntiles - 1)) {
-      float* lsum = reinterpret_cast<float*>(smem + C::OFF_P);
+      float* lsum = reinterpret_cast<float*>(smem + C::OFF_K);
       lsum[half * TC_ROWS + r] = l_run;
       if (!rendezvous(ntiles)) {
         fail();

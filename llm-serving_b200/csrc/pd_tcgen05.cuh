@@ -1,8 +1,9 @@
 // pd_tcgen05.cuh -- 5th-generation tensor-core (tcgen05 / UMMA) helpers for sm_100a.
 //
 // Inline-PTX wrappers for tensor-memory (TMEM) allocation, the single-thread tcgen05.mma of
-// kind::f16 with both operands in shared memory, its commit to an mbarrier, TMEM loads and
-// stores, the tcgen05 ordering fences, and the two 64-bit descriptors the MMA takes:
+// kind::f16 with both operands in shared memory (SS) or A in TMEM (TS), its commit to an
+// mbarrier, TMEM loads and stores, the tcgen05 ordering fences, and the two 64-bit descriptors
+// the MMA takes:
 //
 //  * shared-memory matrix descriptor: start address >> 4 in bits [0,14), leading-dimension
 //    byte offset >> 4 in [16,30), stride-dimension byte offset >> 4 in [32,46), the constant 1
@@ -69,6 +70,19 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// ---- D[tmem] (+)= A[tmem] * B[smem], issued by one thread. A (M = 128 rows, K-major) sits in
+// TMEM lanes 0..127, its K elements packed two 16-bit values per 32-bit column, the lower K
+// index in the low half; one K = 16 step is 8 columns.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
 // The mbarrier receives one arrival once every tcgen05.mma this thread issued before has
 // completed (its TMEM results written, its shared-memory operands read).
 __device__ __forceinline__ void commit(uint32_t bar) {
@@ -98,6 +112,12 @@ __device__ __forceinline__ void st_32x32b_x32(uint32_t taddr, const uint32_t (&r
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
       "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+// 32 lanes x 4 columns (thread t writes lane taddr.lane + t, columns taddr.col .. +3).
+__device__ __forceinline__ void st_32x32b_x4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
 }
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

@@ -152,6 +152,40 @@ def test_prefill_ignores_nan_in_slots_no_row_reads(cuda_device, kernel):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("pad", ["block", "row"])
+@pytest.mark.parametrize("D,bs", [(128, 16), (256, 32), (64, 8)])
+def test_strided_pool_views(cuda_device, kernel, pad, D, bs):
+    """Pools that are views of larger tensors. With padding between blocks (block stride
+    above block_size x token stride) the tcgen05 kernel copies one 128-byte piece per box; with
+    padded rows (token stride above n_kv_head x head_dim) it keeps the grouped boxes. Both
+    layouts must give the oracle's output."""
+    from model import _native
+    from model.triton_decode import paged_prefill
+
+    H, Hkv = 8, 2
+    q, k, v, table, cu, sk = prefill_case(H, Hkv, D, bs, [70, 0, 333], [45, 130, 9], seed=D + bs)
+    ref_f32, _ = oracle.paged_prefill(q, k, v, table, cu, sk)
+
+    def padded(x):
+        n = x.shape[0]
+        if pad == "block":
+            big = torch.full((n, bs + 8, Hkv, D), float("nan"), dtype=x.dtype)
+            big[:, :bs] = x
+            return big.to(cuda_device)[:, :bs]
+        big = torch.full((n, bs, Hkv + 1, D), float("nan"), dtype=x.dtype)
+        big[:, :, :Hkv] = x
+        return big.to(cuda_device)[:, :, :Hkv]
+
+    kp, vp = padded(k), padded(v)
+    assert not kp.is_contiguous()
+    got = paged_prefill(q.to(cuda_device), kp, vp, table.to(cuda_device), cu.to(cuda_device),
+                        sk.to(cuda_device), 130)
+    torch.cuda.synchronize()
+    assert_output_close(got, ref_f32, torch.bfloat16)
+    assert _native.device_error() == 0
+
+
+@pytest.mark.gpu
 def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device, kernel):
     """Engines pass a bucketed bound; the extra query tiles of the grid have no tokens."""
     from model import _native
