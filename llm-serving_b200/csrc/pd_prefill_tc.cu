@@ -96,16 +96,15 @@ struct TcBars {
   static constexpr int K_EMPTY = 12;  // [6] S = Q K^T of the stage's tile completed (commit)
   static constexpr int V_EMPTY = 18;  // [6] P.V of the stage's tile completed (commit)
   static constexpr int S_FULL = 24;   // [3] S buffer written (commit)
-  static constexpr int P_FULL = 27;   // [3] P written over the buffer's S (and O rescaled) by the softmax
+  static constexpr int P_FULL = 27;   // [3] P written over the buffer's S (and O rescaled): one arrival per softmax warp
   static constexpr int O_DONE = 30;   // [3] P.V of the tile that read buffer i's P completed (commit)
-  static constexpr int Q_FULL = 33;   // Q tile written by the softmax threads
+  static constexpr int Q_FULL = 33;   // Q tile written: one arrival per softmax warp
   static constexpr int DRAIN = 34;    // every MMA of the CTA completed (commit at exit)
-  static constexpr int XCHG = 35;     // [4 warp pairs x 2 parities] the pair's maxima are posted
   static constexpr int TMEM_SLOT = 344;  // byte offset: TMEM base address written by tcgen05.alloc
   static constexpr int ABORT = 352;      // byte offset: a role's wait ran out
   static constexpr int MAXES = 1024;     // byte offset: bf16 [2 parities][2 halves][128 rows]
 };
-static_assert((TcBars::XCHG + 8) * 8 <= TcBars::TMEM_SLOT, "barrier slots");
+static_assert((TcBars::DRAIN + 1) * 8 <= TcBars::TMEM_SLOT, "barrier slots");
 
 // Single-thread bounded mbarrier wait (the TMA and MMA lanes run alone in their warps).
 __device__ __forceinline__ bool thread_wait_phase(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
@@ -116,6 +115,21 @@ __device__ __forceinline__ bool thread_wait_phase(uint32_t bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
   }
+}
+
+// Named barrier `id` over `threads` threads (whole warps) with an OR of `pred` over them: every
+// participant gets the same answer, so a failure seen by one warp stops all of them together.
+__device__ __forceinline__ bool bar_any(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
 }
 
 // 2^x by the hardware approximation (ex2.approx, subnormal results flushed to zero). Here x <= 8
@@ -204,11 +218,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < C::NSB; ++i) {
       mbar_init(bar(TcBars::S_FULL + i), 1);
-      mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX);
+      mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX / 32);
       mbar_init(bar(TcBars::O_DONE + i), 1);
     }
-    mbar_init(bar(TcBars::Q_FULL), TC_SOFTMAX);
-    for (int i = 0; i < 8; ++i) mbar_init(bar(TcBars::XCHG + i), 64);
+    mbar_init(bar(TcBars::Q_FULL), TC_SOFTMAX / 32);
     mbar_init(bar(TcBars::DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -447,67 +460,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         *reinterpret_cast<uint4*>(smem + C::OFF_Q + (u >> 3) * 16384 + sw128(r, u & 7)) = qv[uu];
       }
       fence_proxy_async_smem();
-      mbar_arrive(bar(TcBars::Q_FULL));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(TcBars::Q_FULL));
     }
     const int row_last = i < ntok ? ctx + tok0 + i : kend - 1;  // padding rows: any finite row
     const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
     __nv_bfloat16* maxes = reinterpret_cast<__nv_bfloat16*>(smem + TcBars::MAXES);
-    const uint32_t xbar = bar(TcBars::XCHG + (warp & 3) * 2);
+    const int pair_bar = 1 + (warp & 3);  // the warp pair's named barrier (0 is __syncthreads)
     float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
+    bool ok = true;  // this warp's own waits so far (warp-uniform)
     // P.V of tile t has completed. Tile t's phase on its buffer's barrier is t / 3; the barrier
-    // cannot pass it before this thread writes P_{t+3}, and the phase before it (P.V of tile
-    // t - 3) completed before S_t was issued, which this thread has seen, so the parity test is
+    // cannot pass it before this warp writes P_{t+3}, and the phase before it (P.V of tile
+    // t - 3) completed before S_t was issued, which this warp has seen, so the parity test is
     // unambiguous.
     auto wait_pv = [&](int t) -> bool {
       return warp_wait_phase(bar(TcBars::O_DONE + t % C::NSB), uint32_t((t / C::NSB) & 1), wait_ns);
     };
-    // The pair's rendezvous for tile t (barrier t & 1 of the pair, phase t / 2: the partner
-    // cannot post tile t + 2 before this thread has passed tile t + 1).
-    auto rendezvous = [&](int t) -> bool {
-      mbar_arrive(xbar + uint32_t((t & 1) * 8));
-      return warp_wait_phase(xbar + uint32_t((t & 1) * 8), uint32_t((t >> 1) & 1), wait_ns);
-    };
+    // Every exit from the loop is taken by both warps of a pair at the same pair barrier (a wait
+    // that runs out later in a tile only skips that tile's work, and the next barrier stops
+    // both), so neither warp is ever left waiting for the other.
     for (int j = 0; j < ntiles; ++j) {
-      if (__any_sync(FULL_MASK, *abort_flag != 0)) {
-        ok = false;
-        break;
-      }
       const int sb = j % C::NSB;
-      if (!warp_wait_phase(bar(TcBars::S_FULL + sb), uint32_t((j / C::NSB) & 1), wait_ns)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
+      bool bad = __any_sync(FULL_MASK, !ok || *abort_flag != 0);
+      if (!bad && !warp_wait_phase(bar(TcBars::S_FULL + sb), uint32_t((j / C::NSB) & 1), wait_ns)) bad = true;
       // this thread's half row of S: columns half KT/2 .. + KT/2 - 1 of the buffer
       const uint32_t s_tmem = lane_base + uint32_t(sb * C::KT + half * C::HK);
-      uint32_t raw_s[C::HK];
-#pragma unroll
-      for (int c = 0; c < C::HK; c += 32)
-        tc::ld_32x32b_x32(s_tmem + uint32_t(c), *reinterpret_cast<uint32_t(*)[32]>(raw_s + c));
-      tc::wait_ld();
-
-      const int c0 = j * C::KT + half * C::HK;  // key of raw_s[0]
+      const int c0 = j * C::KT + half * C::HK;  // key of its first column
       float s[C::HK];
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
-      if (c0 + C::HK - 1 <= row_last) {  // every key of this half is visible to the row
+      __nv_bfloat16 mine = __float2bfloat16_rd(-INFINITY);
+      if (!bad) {
+        tc::fence_after_sync();
+        uint32_t raw_s[C::HK];
 #pragma unroll
-        for (int c = 0; c < C::HK; ++c) {
-          s[c] = __uint_as_float(raw_s[c]) * p.scale_log2;
-          mx[c & 3] = fmaxf(mx[c & 3], s[c]);
-        }
-      } else {  // the causal edge (or the row end) crosses it
+        for (int c = 0; c < C::HK; c += 32)
+          tc::ld_32x32b_x32(s_tmem + uint32_t(c), *reinterpret_cast<uint32_t(*)[32]>(raw_s + c));
+        tc::wait_ld();
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+        if (c0 + C::HK - 1 <= row_last) {  // every key of this half is visible to the row
 #pragma unroll
-        for (int c = 0; c < C::HK; ++c) {
-          const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
-          s[c] = c0 + c <= row_last ? x : -INFINITY;
-          mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+          for (int c = 0; c < C::HK; ++c) {
+            s[c] = __uint_as_float(raw_s[c]) * p.scale_log2;
+            mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+          }
+        } else {  // the causal edge (or the row end) crosses it
+#pragma unroll
+          for (int c = 0; c < C::HK; ++c) {
+            const float x = __uint_as_float(raw_s[c]) * p.scale_log2;
+            s[c] = c0 + c <= row_last ? x : -INFINITY;
+            mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+          }
         }
+        // post this half's maximum, rounded down (never above the true one)
+        mine = __float2bfloat16_rd(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+        maxes[((j & 1) * 2 + half) * TC_ROWS + r] = mine;
       }
-      // post this half's maximum (rounded down: never above the true one) and take the pair's
-      const __nv_bfloat16 mine = __float2bfloat16_rd(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
-      maxes[((j & 1) * 2 + half) * TC_ROWS + r] = mine;
-      if (!rendezvous(j)) {
+      // Both halves have read their S (so P may overwrite it) and posted their maxima. The
+      // partner can post tile j + 1's only after this warp reaches the next barrier, so two
+      // parities of slots suffice.
+      if (bar_any(pair_bar, 64, bad)) {
         ok = false;
         break;
       }
@@ -518,20 +528,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (rescale) {  // O *= alpha per row (this half's columns), once P.V of tile j - 1 landed
         if (!wait_pv(j - 1)) {
           ok = false;
-          break;
-        }
-        tc::fence_after_sync();
+        } else {
+          tc::fence_after_sync();
 #pragma unroll 1
-        for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
-          uint32_t o[32];
-          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
-          tc::wait_ld();
+          for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
+            uint32_t o[32];
+            tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
+            tc::wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tc::st_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tc::st_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
+          }
+          tc::wait_st();
         }
-        tc::wait_st();
       }
+      if (!ok) continue;  // the next pair barrier stops both warps
       if (move) m_run = tmax;
       l_run *= alpha;
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int s_st = j % C::STAGES;
         if (!warp_wait_phase(bar(TcBars::V_FULL + s_st), uint32_t((j / C::STAGES) & 1), wait_ns)) {
           ok = false;
-          break;
+          continue;
         }
         unsigned char* vs = smem + C::OFF_V + s_st * C::KV_BYTES;
         const int zrows = C::KT - valid;
@@ -577,41 +588,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       fence_proxy_async_smem();
       tc::wait_st();
       tc::fence_before_sync();
-      mbar_arrive(bar(TcBars::P_FULL + sb));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(TcBars::P_FULL + sb));
     }
     if (!ok) fail();
     // ---- epilogue: out = O / max(l, 1) for the rows of the chunk; l is the sum of the pair's
     // halves, exchanged through K stage 0 (free once the last P.V has completed: every copy has
-    // landed and been read by then)
-    if (ok && wait_pv(ntiles - 1)) {
-      float* lsum = reinterpret_cast<float*>(smem + C::OFF_K);
-      lsum[half * TC_ROWS + r] = l_run;
-      if (!rendezvous(ntiles)) {
-        fail();
-      } else {
-        tc::fence_after_sync();
-        const float inv = 1.f / fmaxf(l_run + lsum[(half ^ 1) * TC_ROWS + r], 1.f);
-        T* dst = og + int64_t(q_begin + tok0 + i) * p.o_st + int64_t(hq) * p.o_sh;
+    // landed and been read by then). Both warps of the pair reach this barrier exactly once.
+    const bool good = ok && wait_pv(ntiles - 1);
+    float* lsum = reinterpret_cast<float*>(smem + C::OFF_K);
+    if (good) lsum[half * TC_ROWS + r] = l_run;
+    if (bar_any(pair_bar, 64, !good)) {
+      if (ok && !good) fail();
+    } else {
+      tc::fence_after_sync();
+      const float inv = 1.f / fmaxf(l_run + lsum[(half ^ 1) * TC_ROWS + r], 1.f);
+      T* dst = og + int64_t(q_begin + tok0 + i) * p.o_st + int64_t(hq) * p.o_sh;
 #pragma unroll 1
-        for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
-          uint32_t o[32];
-          tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
-          tc::wait_ld();
-          if (i < ntok) {
+      for (int oc = half * (D / 2); oc < (half + 1) * (D / 2); oc += 32) {
+        uint32_t o[32];
+        tc::ld_32x32b_x32(lane_base + uint32_t(C::O_COL + oc), o);
+        tc::wait_ld();
+        if (i < ntok) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 w;
-              w.x = E::pack2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-              w.y = E::pack2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-              w.z = E::pack2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-              w.w = E::pack2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + oc + 8 * u) = w;
-            }
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = E::pack2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            w.y = E::pack2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            w.z = E::pack2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            w.w = E::pack2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + oc + 8 * u) = w;
           }
         }
       }
-    } else if (ok) {
-      fail();
     }
   }
 
