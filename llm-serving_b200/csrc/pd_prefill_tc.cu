@@ -255,23 +255,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // dependent table load; lane 0 issues the copies. K tile j is issued once the S MMA of tile
     // j - STAGES has read its stage, V tile j once the P.V of tile j - STAGES has.
     const int bs = p.block_size;
-    const int bt = p.box_tokens;  // tokens per copy: min(block_size, 64)
-    const int npages = (lk + bs - 1) / bs;
+    const int bt = p.box_tokens;  // tokens per copy: min(block_size, KT)
+    // Both are powers of two (pd_prefill checks): this warp's per-tile work is one dependent
+    // chain, so its page and box arithmetic uses shifts, not integer divisions.
+    const int bs_log = __ffs(bs) - 1, bt_log = __ffs(bt) - 1;
+    const int npages = (lk + bs - 1) >> bs_log;
     const uint32_t box_bytes = uint32_t(bt) * 128u;  // one piece of one box
     const int32_t* trow = p.table + int64_t(b) * p.bt_stride;
     auto entry = [&](int page) -> int {
       return page >= 0 && page < npages && page < p.max_blocks ? __ldg(trow + page) : 0;
     };
-    // 64-entry window [win_base, win_base + 64): lane l holds entries win_base + l and + 32 + l.
+    // Window [win_base, win_base + 64) of the table: lane l holds entries win_base + l and + 32 + l,
+    // and the 32 after them are already loading (a window advance never waits on a table read).
     // Tiles start on KT-token boundaries, so a tile spans at most KT / block_size <= 16 pages (a
     // block of KT tokens or more holds a whole tile); once the window starts at or below the
     // tile's first page and within 32 of it, every page of the tile is inside.
-    int win_base = 0, win_cur = pre_win0, win_nxt = pre_win1;
+    int win_base = 0, win_cur = pre_win0, win_nxt = pre_win1, win_far = entry(64 + lane);
     auto advance_window = [&](int first_page) {  // warp-collective
       while (first_page >= win_base + 32) {
         win_base += 32;
         win_cur = win_nxt;
-        win_nxt = entry(win_base + 32 + lane);
+        win_nxt = win_far;
+        win_far = entry(win_base + 64 + lane);
       }
     };
     auto block_of = [&](int page) -> int {  // per-lane page inside the window
@@ -290,21 +295,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     auto issue_tile = [&](int t, bool is_k, int blk) {
       const int t0 = t * C::KT;
       const int covered = kend - t0 < C::KT ? kend - t0 : C::KT;
-      const int boxes = (covered + bt - 1) / bt;
+      const int boxes = (covered + bt - 1) >> bt_log;
       const int s = t % C::STAGES;
       const uint32_t full = bar((is_k ? TcBars::K_FULL : TcBars::V_FULL) + s);
       const uint32_t dst0 = is_k ? k_addr(s) : v_addr(s);
       const CUtensorMap* map = is_k ? &kmap : &vmap;
       if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(boxes) * box_bytes * C::PIECES);
       __syncwarp();
-      const int tok = t0 + my_box * bt;
-      const int page = tok / bs;
+      const int tok = t0 + (my_box << bt_log);
+      const int in_block = tok & (bs - 1);
       if (my_box < boxes) {
         if (p.grouped)
-          tma_load_5d(dst0 + uint32_t(my_box * bt * 128 * C::PIECES), map, full, 0, 0, 0, h,
-                      blk * (bs >> 3) + ((tok - page * bs) >> 3));
+          tma_load_5d(dst0 + uint32_t((my_box << bt_log) * 128 * C::PIECES), map, full, 0, 0, 0, h,
+                      (blk << (bs_log - 3)) + (in_block >> 3));
         else
-          tma_load_5d(dst0 + uint32_t(my_piece * C::KT * 128 + my_box * bt * 128), map, full, 0, tok - page * bs, h,
+          tma_load_5d(dst0 + uint32_t(my_piece * C::KT * 128 + (my_box << bt_log) * 128), map, full, 0, in_block, h,
                       my_piece, blk);
       }
     };
@@ -318,8 +323,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (t >= C::STAGES &&
           !warp_wait_phase(bar(TcBars::K_EMPTY + s), uint32_t((t / C::STAGES - 1) & 1), wait_ns))
         return false;
-      advance_window(t * C::KT / bs);
-      const int blk = block_of((t * C::KT + my_box * bt) / bs);
+      advance_window((t * C::KT) >> bs_log);
+      const int blk = block_of((t * C::KT + (my_box << bt_log)) >> bs_log);
       const int r3 = t % 3;
       ring0 = r3 == 0 ? blk : ring0;
       ring1 = r3 == 1 ? blk : ring1;
