@@ -153,6 +153,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t raw = smem_addr(smem_raw);
+  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const uint32_t sbase = smem_addr(smem);
+  auto bar = [&](int slot) -> uint32_t { return sbase + uint32_t(slot) * 8u; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcBars::ABORT);
+  const unsigned long long wait_ns = p.wait_ns;
+
+  // Set-up first, before anything waits on memory, by the MMA warp: it has no loads in flight,
+  // so the fence after the barrier initialisation waits for none (the same fence in a thread
+  // that has just issued its Q loads waits for them), and TMEM allocation starts at entry. Every
+  // CTA allocates; one without work frees the columns at the common exit.
+  if (warp == TC_MMA_WARP) {
+    if (lane == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      for (int s = 0; s < C::STAGES; ++s) {
+        mbar_init(bar(TcBars::K_FULL + s), 1);
+        mbar_init(bar(TcBars::V_FULL + s), 1);
+        mbar_init(bar(TcBars::K_EMPTY + s), 1);
+        mbar_init(bar(TcBars::V_EMPTY + s), 1);
+      }
+      for (int i = 0; i < C::NSB; ++i) {
+        mbar_init(bar(TcBars::S_FULL + i), 1);
+        mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX / 32);
+        mbar_init(bar(TcBars::O_DONE + i), 1);
+      }
+      mbar_init(bar(TcBars::Q_FULL), TC_SOFTMAX / 32);
+      mbar_init(bar(TcBars::DRAIN), 1);
+      *abort_flag = 0;
+      fence_barrier_init();
+    }
+    __syncwarp();
+    tc::tmem_alloc(sbase + TcBars::TMEM_SLOT, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+
   // 1-D grid, query tile slowest: the CTAs of the last (heaviest, causal) query tiles of every
   // (row, kv head) are launched first, so the lighter ones fill the later waves.
   const int pairs = p.batch * p.n_kv_head;
@@ -164,33 +200,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int lk = __ldg(p.seqlen_k + b);
   lk = lk < 0 ? 0 : (lk > p.capacity ? p.capacity : lk);
   const int tok0 = qtile * TQ;
-  if (sq <= 0 || tok0 >= sq) return;
-  const int ntok = sq - tok0 < TQ ? sq - tok0 : TQ;
+  const bool has_rows = sq > 0 && tok0 < sq;
+  const int ntok = !has_rows ? 0 : (sq - tok0 < TQ ? sq - tok0 : TQ);
   const int ctx = lk - sq;
   int kend = ctx + tok0 + ntok;  // keys this CTA needs: 0 .. kend - 1
   if (kend > lk) kend = lk;
-  if (kend < 0) kend = 0;
+  if (kend < 0 || !has_rows) kend = 0;
   const int ntiles = (kend + C::KT - 1) / C::KT;
   T* og = reinterpret_cast<T*>(p.out);
 
-  if (ntiles == 0) {  // no visible key for any row of the CTA: exact zeros
+  if (has_rows && ntiles == 0) {  // no visible key for any row of the CTA: exact zeros
     if (tid < TC_ROWS && tid / G < ntok) {
       T* dst = og + int64_t(q_begin + tok0 + tid / G) * p.o_st + int64_t(h * G + tid % G) * p.o_sh;
       for (int u = 0; u < D / 8; ++u) reinterpret_cast<uint4*>(dst)[u] = make_uint4(0u, 0u, 0u, 0u);
     }
-    return;
   }
+  const bool run = ntiles > 0;
 
-  // Loads that nothing else waits for are issued before the barrier set-up: the TMA warp's first
+  // Loads that nothing else waits for are issued before the CTA's barrier: the TMA warp's first
   // block-table window (entries past the row's pages are loaded but never used) and each softmax
   // thread's half of its Q row (zeros past the chunk).
   int pre_win0 = 0, pre_win1 = 0;
   uint4 qv[D / 16];
-  if (warp == TC_TMA_WARP) {
+  if (run && warp == TC_TMA_WARP) {
     const int32_t* trow0 = p.table + int64_t(b) * p.bt_stride;
     pre_win0 = lane < p.max_blocks ? __ldg(trow0 + lane) : 0;
     pre_win1 = 32 + lane < p.max_blocks ? __ldg(trow0 + 32 + lane) : 0;
-  } else if (warp < TC_SOFTMAX / 32) {
+  } else if (run && warp < TC_SOFTMAX / 32) {
     const int r = (warp & 3) * 32 + lane, i = r / G;
     const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st +
                    int64_t(h * G + r % G) * p.q_sh;
@@ -200,36 +236,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         : make_uint4(0u, 0u, 0u, 0u);
   }
 
-  const uint32_t raw = smem_addr(smem_raw);
-  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const uint32_t sbase = smem_addr(smem);
-  auto bar = [&](int slot) -> uint32_t { return sbase + uint32_t(slot) * 8u; };
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcBars::ABORT);
-  const unsigned long long wait_ns = p.wait_ns;
-
-  if (tid == 0) {
-    tma_prefetch_desc(&kmap);
-    tma_prefetch_desc(&vmap);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar(TcBars::K_FULL + s), 1);
-      mbar_init(bar(TcBars::V_FULL + s), 1);
-      mbar_init(bar(TcBars::K_EMPTY + s), 1);
-      mbar_init(bar(TcBars::V_EMPTY + s), 1);
-    }
-    for (int i = 0; i < C::NSB; ++i) {
-      mbar_init(bar(TcBars::S_FULL + i), 1);
-      mbar_init(bar(TcBars::P_FULL + i), TC_SOFTMAX / 32);
-      mbar_init(bar(TcBars::O_DONE + i), 1);
-    }
-    mbar_init(bar(TcBars::Q_FULL), TC_SOFTMAX / 32);
-    mbar_init(bar(TcBars::DRAIN), 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == TC_MMA_WARP) {
-    tc::tmem_alloc(sbase + TcBars::TMEM_SLOT, C::TMEM_COLS);
-    tc::tmem_relinquish();
-  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -248,7 +254,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t gstride = p.grouped ? uint32_t(C::PIECES * 1024) : 1024u;
   const uint32_t pstride = p.grouped ? 1024u : uint32_t(C::KT * 128);
 
-  if (warp == TC_TMA_WARP) {
+  if (!run) {
+    // no key tile: nothing to stream (the rows, if any, were zeroed above)
+  } else if (warp == TC_TMA_WARP) {
     // ---------------------------------------------------------------- TMA producer
     // The whole warp runs the loop (its waits are warp-collective) and keeps the row's block
     // table in a 32-entry register window, the next window prefetched, so no copy waits on a
