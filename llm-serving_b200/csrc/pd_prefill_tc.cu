@@ -217,25 +217,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   const bool run = ntiles > 0;
 
-  // Loads that nothing else waits for are issued before the CTA's barrier: the TMA warp's first
-  // block-table window (entries past the row's pages are loaded but never used) and each softmax
-  // thread's half of its Q row (zeros past the chunk).
-  int pre_win0 = 0, pre_win1 = 0;
-  uint4 qv[D / 16];
-  if (run && warp == TC_TMA_WARP) {
-    const int32_t* trow0 = p.table + int64_t(b) * p.bt_stride;
-    pre_win0 = lane < p.max_blocks ? __ldg(trow0 + lane) : 0;
-    pre_win1 = 32 + lane < p.max_blocks ? __ldg(trow0 + 32 + lane) : 0;
-  } else if (run && warp < TC_SOFTMAX / 32) {
-    const int r = (warp & 3) * 32 + lane, i = r / G;
-    const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st +
-                   int64_t(h * G + r % G) * p.q_sh;
-#pragma unroll
-    for (int uu = 0; uu < D / 16; ++uu)
-      qv[uu] = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + (warp >> 2) * (D / 16) + uu)
-                        : make_uint4(0u, 0u, 0u, 0u);
-  }
-
+  // A barrier waits for the loads its threads have in flight, so the Q rows and the block
+  // table are loaded after this one, by the roles that use them.
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -274,13 +257,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       return page >= 0 && page < npages && page < p.max_blocks ? __ldg(trow + page) : 0;
     };
     // Window [win_base, win_base + 64) of the table: lane l holds entries win_base + l and + 32 + l,
-    // and the 32 after them are already loading (a window advance never waits on a table read).
+    // and the 32 after them are already loading (a window advance never waits on a table read;
+    // the first of those loads goes out after the first tile's copies, which then do not wait
+    // for it).
     // Tiles start on KT-token boundaries, so a tile spans at most KT / block_size <= 16 pages (a
     // block of KT tokens or more holds a whole tile); once the window starts at or below the
     // tile's first page and within 32 of it, every page of the tile is inside.
-    int win_base = 0, win_cur = pre_win0, win_nxt = pre_win1, win_far = entry(64 + lane);
+    int win_base = 0, win_cur = entry(lane), win_nxt = entry(32 + lane), win_far = 0;
+    bool far_pending = true;  // win_far is loaded once the first tile's copies are out
     auto advance_window = [&](int first_page) {  // warp-collective
       while (first_page >= win_base + 32) {
+        if (far_pending) {
+          win_far = entry(win_base + 64 + lane);
+          far_pending = false;
+        }
         win_base += 32;
         win_cur = win_nxt;
         win_nxt = win_far;
@@ -308,8 +298,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t full = bar((is_k ? TcBars::K_FULL : TcBars::V_FULL) + s);
       const uint32_t dst0 = is_k ? k_addr(s) : v_addr(s);
       const CUtensorMap* map = is_k ? &kmap : &vmap;
+      // Lane 0's expect-tx need not precede the other lanes' copies: until that single arrival
+      // the phase cannot complete, whatever the transaction count (which may go negative)
+      // reads. No warp barrier here, since one would wait for the table loads in flight.
       if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(boxes) * box_bytes * C::PIECES);
-      __syncwarp();
       const int tok = t0 + (my_box << bt_log);
       const int in_block = tok & (bs - 1);
       if (my_box < boxes) {
@@ -369,6 +361,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         break;
       }
       v_issued = j + 1;
+      if (far_pending) {
+        win_far = entry(win_base + 64 + lane);
+        far_pending = false;
+      }
     }
     if (!ok && lane == 0) fail();
     // never leave with a copy in flight: the last STAGES tiles' copies must have landed
@@ -466,7 +462,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int r = (warp & 3) * 32 + lane;  // query row = TMEM lane
     const int i = r / G;
     const int hq = h * G + r % G;
-    {  // this thread's half of the Q row (loaded at entry) -> the swizzled K-major Q tile
+    {  // this thread's half of the Q row -> the swizzled K-major Q tile (zeros past the chunk)
+      const T* src = reinterpret_cast<const T*>(p.q) + int64_t(q_begin + tok0 + i) * p.q_st + int64_t(hq) * p.q_sh;
+      uint4 qv[D / 16];
+#pragma unroll
+      for (int uu = 0; uu < D / 16; ++uu)
+        qv[uu] = i < ntok ? __ldg(reinterpret_cast<const uint4*>(src) + half * (D / 16) + uu)
+                          : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
       for (int uu = 0; uu < D / 16; ++uu) {
         const int u = half * (D / 16) + uu;

@@ -186,6 +186,26 @@ def test_strided_pool_views(cuda_device, kernel, pad, D, bs):
 
 
 @pytest.mark.gpu
+def test_queries_that_see_no_key_give_zeros(cuda_device, kernel):
+    """seqlen_k below the chunk length puts the first query tokens at negative positions: they
+    see no key and their output is exact zeros (acc / max(l, 1) with l = 0), whole query tiles
+    of them included; a row with seqlen_k 0 is all zeros."""
+    from model import _native
+    from model.triton_decode import paged_prefill
+
+    q, k, v, table, cu, sk = prefill_case(16, 8, 128, 16, [0, 0, 5], [200, 70, 10], seed=12)
+    sk = torch.tensor([50, 0, 12], dtype=torch.int32)
+    ref_f32, _ = oracle.paged_prefill(q, k, v, table, cu, sk)
+    got = paged_prefill(*[t.to(cuda_device) for t in (q, k, v, table, cu, sk)], 200)
+    torch.cuda.synchronize()
+    assert_output_close(got, ref_f32, torch.bfloat16)
+    assert torch.count_nonzero(got[:150].float()) == 0  # row 0's tokens 0..149
+    assert torch.count_nonzero(got[200:270].float()) == 0  # row 1
+    assert torch.count_nonzero(got[150:200].float()) > 0
+    assert _native.device_error() == 0
+
+
+@pytest.mark.gpu
 def test_a_larger_max_seqlen_q_bound_changes_nothing(cuda_device, kernel):
     """Engines pass a bucketed bound; the extra query tiles of the grid have no tokens."""
     from model import _native
