@@ -33,6 +33,9 @@
 //    the normaliser. The running max is rescaled lazily: only when a row's tile max exceeds it
 //    by more than 2^8 is O rescaled in TMEM (P then stays below 2^8, which the hi + lo operands
 //    carry exactly as well as smaller values); the final out = O / max(l, 1) is unchanged.
+//  * Set-up: warp 9 initialises the barriers and allocates TMEM at entry, before any thread
+//    waits on memory; the Q rows and the block table are loaded only after the CTA barrier
+//    that follows (a barrier waits for its threads' loads in flight).
 //  * Key tiles past the CTA's last query position are never loaded. V rows past the row end
 //    are zeroed in shared memory before use, so stale or NaN pool bytes never reach O.
 //  * Every wait is bounded (the launch's wait limit). A role whose wait runs out records
