@@ -31,6 +31,8 @@ the reference's seat (dense slab) step restated in torch, both as CUDA graphs; `
 1024 rows sharded by index over the ranks (strong scaling, no collective); ``config4_cp`` =
 32 x 8192 rows split by context over the ranks with one NCCL all-gather per layer-step,
 compute and collective timed apart. Both sharded blocks carry an fp32 parity field.
+``prefill`` = the block-table-aware chunked prefill on tcgen05 (4 rows x 512 new tokens after
+2,048 cached, 28 layers, rank 0) with its fraction of the measured sustained bf16 peak.
 
 ``--impl reference`` times that CPU port alone (the reference's own CPU implementation of this
 path; rank 0 only) and prints the same line with ``"impl": "reference"``.
@@ -264,6 +266,9 @@ def run_gpu(args) -> dict | None:
     config5 = run_config5(device, rank, world, dist, reps=sharded_reps)
     config4_cp = run_config4_cp(device, rank, world, dist, steps=sharded_reps)
     seat = seat_case(device, "config2_b32_ctx2048", [CONTEXT] * BATCH) if rank == 0 else None
+    # the block-table-aware chunked prefill on tcgen05 (one GPU, rank 0): 4 rows x 512 new tokens
+    # after 2,048 cached ones, 28 layers
+    prefill = prefill_case(device, _peaks(), 5, "tcgen05", *PREFILL_CASES[0]) if rank == 0 else None
 
     if rank != 0:
         _finish(dist)
@@ -315,6 +320,7 @@ def run_gpu(args) -> dict | None:
         "seat": seat,
         "config5": config5,
         "config4_cp": config4_cp,
+        "prefill": prefill,
     }
     line["cpu_baseline"] = cpu_baseline(sample_layers=args.cpu_sample_layers)
     _finish(dist)
@@ -815,63 +821,76 @@ def prefill_sweep(reps: int = 5) -> None:
             _native.set_prefill_mode(0)
 
 
+PREFILL_CASES = (
+    # name, rows, cached context, chunk, layers, (q heads, kv heads, head_dim)
+    ("chunk512_ctx2048", 4, 2048, 512, 28, (16, 8, 128)),
+    ("chunk2048_ctx0", 4, 0, 2048, 28, (16, 8, 128)),
+    ("chunk128_ctx4096", 16, 4096, 128, 8, (16, 8, 128)),
+    ("qwen35_chunk512_ctx2048", 4, 2048, 512, 6, (8, 2, 256)),
+)
+
+
 def _prefill_cases(device, peaks, reps, kernel) -> None:
+    for case in PREFILL_CASES:
+        print(json.dumps(prefill_case(device, peaks, reps, kernel, *case)), flush=True)
+
+
+def prefill_case(device, peaks, reps, kernel, name, rows, ctx, chunk, n_layer, heads) -> dict:
+    """One chunked-prefill case: every layer's ``paged_prefill`` launch once per replay of a
+    CUDA graph over distinct per-layer pools, best of ``reps`` replays."""
     from model import _native
     from model.triton_decode import paged_prefill
 
+    H, H_KV, D = heads
     gen = torch.Generator(device=device).manual_seed(11)
-    for name, rows, ctx, chunk, n_layer, (H, H_KV, D) in (
-            ("chunk512_ctx2048", 4, 2048, 512, 28, (16, 8, 128)),
-            ("chunk2048_ctx0", 4, 0, 2048, 28, (16, 8, 128)),
-            ("chunk128_ctx4096", 16, 4096, 128, 8, (16, 8, 128)),
-            ("qwen35_chunk512_ctx2048", 4, 2048, 512, 6, (8, 2, 256))):
-        total = ctx + chunk
-        pages = -(-total // BS)
-        n_blocks = rows * pages + 1
-        pools_k = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
-                   for _ in range(n_layer)]
-        pools_v = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
-                   for _ in range(n_layer)]
-        perm = torch.randperm(n_blocks, generator=gen, device=device)[: rows * pages]
-        table = perm.view(rows, pages).to(torch.int32)
-        q = [torch.randn(rows * chunk, H, D, generator=gen, device=device, dtype=torch.bfloat16)
-             for _ in range(n_layer)]
-        cu = torch.arange(rows + 1, device=device, dtype=torch.int32) * chunk
-        sk = torch.full((rows,), total, device=device, dtype=torch.int32)
+    total = ctx + chunk
+    pages = -(-total // BS)
+    n_blocks = rows * pages + 1
+    pools_k = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+               for _ in range(n_layer)]
+    pools_v = [torch.randn(n_blocks, BS, H_KV, D, generator=gen, device=device, dtype=torch.bfloat16)
+               for _ in range(n_layer)]
+    perm = torch.randperm(n_blocks, generator=gen, device=device)[: rows * pages]
+    table = perm.view(rows, pages).to(torch.int32)
+    q = [torch.randn(rows * chunk, H, D, generator=gen, device=device, dtype=torch.bfloat16)
+         for _ in range(n_layer)]
+    cu = torch.arange(rows + 1, device=device, dtype=torch.int32) * chunk
+    sk = torch.full((rows,), total, device=device, dtype=torch.int32)
+    outs = [paged_prefill(q[i], pools_k[i], pools_v[i], table, cu, sk, chunk) for i in range(n_layer)]
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         outs = [paged_prefill(q[i], pools_k[i], pools_v[i], table, cu, sk, chunk) for i in range(n_layer)]
-        torch.cuda.synchronize(device)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            outs = [paged_prefill(q[i], pools_k[i], pools_v[i], table, cu, sk, chunk) for i in range(n_layer)]
+    graph.replay()
+    times = []
+    for _ in range(reps):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
         graph.replay()
-        times = []
-        for _ in range(reps):
-            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            graph.replay()
-            stop.record()
-            torch.cuda.synchronize(device)
-            times.append(start.elapsed_time(stop) * 1e3 / n_layer)
-        if _native.device_error() != 0:
-            raise SystemExit(f"{name}: device error word set")
-        best = min(times)
-        pairs = rows * (chunk * ctx + chunk * (chunk + 1) // 2)  # visible (query, key) pairs
-        flops = 4.0 * D * H * pairs
-        kv_bytes = rows * total * H_KV * D * 2 * 2
-        tflops = flops / (best * 1e-6) / 1e12
-        print(json.dumps({
-            "prefill_case": name, "kernel": kernel, "rows": rows, "context": ctx, "chunk": chunk, "layers": n_layer,
-            "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
-            "us_per_launch_best": round(best, 2), "us_per_launch_median": round(statistics.median(times), 2),
-            "causal_tflops": round(tflops, 1),
-            "tensor_roofline_frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
-            "tensor_peak_tflops": peaks["bf16_tflops_sustained"], "kv_gbs": round(kv_bytes / best / 1e3, 1),
-            "hbm_roofline_frac": round(kv_bytes / best / 1e3 / peaks["hbm_gbs"], 4),
-            "peak_source": peaks["source"],
-            "note": "P as hi+lo 16-bit operands: 3 tensor products per (query, key, d) where a "
-                    "16-bit-P kernel needs 2; tcgen05: S and O in TMEM, mma_sync: warp-level tiles"}), flush=True)
-        del graph, outs, pools_k, pools_v, q
-        torch.cuda.empty_cache()
+        stop.record()
+        torch.cuda.synchronize(device)
+        times.append(start.elapsed_time(stop) * 1e3 / n_layer)
+    if _native.device_error() != 0:
+        raise SystemExit(f"{name}: device error word set")
+    best = min(times)
+    pairs = rows * (chunk * ctx + chunk * (chunk + 1) // 2)  # visible (query, key) pairs
+    flops = 4.0 * D * H * pairs
+    kv_bytes = rows * total * H_KV * D * 2 * 2
+    tflops = flops / (best * 1e-6) / 1e12
+    result = {
+        "prefill_case": name, "kernel": kernel, "rows": rows, "context": ctx, "chunk": chunk, "layers": n_layer,
+        "heads": f"{H}q/{H_KV}kv", "head_dim": D, "dtype": "bf16",
+        "us_per_launch_best": round(best, 2), "us_per_launch_median": round(statistics.median(times), 2),
+        "causal_tflops": round(tflops, 1),
+        "tensor_roofline_frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
+        "tensor_peak_tflops": peaks["bf16_tflops_sustained"], "kv_gbs": round(kv_bytes / best / 1e3, 1),
+        "hbm_roofline_frac": round(kv_bytes / best / 1e3 / peaks["hbm_gbs"], 4),
+        "peak_source": peaks["source"],
+        "note": "P as hi+lo 16-bit operands: 3 tensor products per (query, key, d) where a "
+                "16-bit-P kernel needs 2; tcgen05: S and O in TMEM, mma_sync: warp-level tiles"}
+    del graph, outs, pools_k, pools_v, q
+    torch.cuda.empty_cache()
+    return result
 
 
 class _SeatStep:
