@@ -78,85 +78,89 @@ def _require_cuda_tensors(tensors) -> None:
             )
 
 
-def _validate(q, k_cache, v_cache, block_table, seqlen) -> None:
-    """The reference's layout contract: structural errors are ValueError."""
-    if q.dim() != 3:
-        raise ValueError(f"q must be (B, H, D), got shape {tuple(q.shape)}")
-    if k_cache.dim() != 4 or v_cache.dim() != 4:
-        raise ValueError(
-            "k_cache/v_cache must be (n_blocks, block_size, H_kv, D), got "
-            f"{tuple(k_cache.shape)} / {tuple(v_cache.shape)}"
-        )
-    if tuple(k_cache.shape) != tuple(v_cache.shape):
-        raise ValueError(
-            f"k_cache/v_cache shapes differ: {tuple(k_cache.shape)} vs {tuple(v_cache.shape)}"
-        )
-    if q.dtype not in (torch.float16, torch.bfloat16, torch.float32):
-        raise ValueError(f"q dtype must be fp16, bf16 or fp32, got {q.dtype}")
-    if not (k_cache.dtype == v_cache.dtype == q.dtype):
-        raise ValueError(
-            f"q/k_cache/v_cache must share one dtype, got {q.dtype}, {k_cache.dtype}, {v_cache.dtype}"
-        )
-    B, H, D = q.shape
-    _, block_size, H_kv, cache_d = k_cache.shape
-    if D < 1:
-        raise ValueError(f"head_dim must be positive, got {D}")
-    if D != cache_d:
-        raise ValueError(f"q head_dim {D} != cache head_dim {cache_d}")
-    if H_kv < 1 or H % H_kv != 0:
-        raise ValueError(f"n_head ({H}) must be a multiple of n_kv_head ({H_kv})")
-    if block_size < 1:
-        raise ValueError(f"block_size must be positive, got {block_size}")
-    if block_size & (block_size - 1):
-        raise ValueError(
-            f"block_size must be a power of two (16 and 32 are the supported sizes), got {block_size}"
-        )
-    if D & (D - 1):
-        raise ValueError(f"head_dim must be a power of two for the kernel, got {D}")
-    if not _MIN_HEAD_DIM <= D <= _MAX_HEAD_DIM:
-        raise ValueError(
-            f"head_dim {D} is outside the sm_100a kernel's range {_MIN_HEAD_DIM}..{_MAX_HEAD_DIM}"
-        )
-    if block_table.dim() != 2:
-        raise ValueError(f"block_table must be (B, max_blocks), got shape {tuple(block_table.shape)}")
-    B_bt, max_blocks = block_table.shape
-    if B_bt != B:
-        raise ValueError(f"block_table batch {B_bt} does not match q batch {B}")
-    if block_table.dtype != torch.int32:
-        raise ValueError(
-            "paged_decode requires an int32 block_table (the kernel's indexing contract); "
-            f"got {block_table.dtype}. Cast at the allocator boundary, not per step."
-        )
-    if seqlen.dim() != 1:
-        raise ValueError(f"seqlen must be (B,), got shape {tuple(seqlen.shape)}")
-    if seqlen.shape[0] != B:
-        raise ValueError(f"seqlen has {seqlen.shape[0]} entries for a batch of {B}")
-    if seqlen.dtype not in (torch.int32, torch.int64):
-        raise ValueError(f"seqlen must be int32 or int64, got {seqlen.dtype}")
-    device = q.device
+def _contract(q, k_cache, v_cache, block_table, seqlen):
+    """The kernel's layout contract as (violated, message) rules, in the order they are checked.
+
+    The messages are the reference's (model/triton_decode.py:120-231), which its callers and
+    tests match on. A rule may rely on every rule before it holding (shapes are unpacked only
+    after their ranks are checked), so the rules are produced lazily and the caller stops at
+    the first violation.
+    """
+    yield q.dim() != 3, lambda: f"q must be (B, H, D), got shape {tuple(q.shape)}"
+    pools = (k_cache, v_cache)
+    yield any(t.dim() != 4 for t in pools), lambda: (
+        "k_cache/v_cache must be (n_blocks, block_size, H_kv, D), got "
+        f"{tuple(k_cache.shape)} / {tuple(v_cache.shape)}")
+    yield k_cache.shape != v_cache.shape, lambda: (
+        f"k_cache/v_cache shapes differ: {tuple(k_cache.shape)} vs {tuple(v_cache.shape)}")
+    yield q.dtype not in _DTYPES, lambda: f"q dtype must be fp16, bf16 or fp32, got {q.dtype}"
+    yield any(t.dtype != q.dtype for t in pools), lambda: (
+        f"q/k_cache/v_cache must share one dtype, got {q.dtype}, {k_cache.dtype}, {v_cache.dtype}")
+
+    n_head, head_dim = q.shape[1], q.shape[2]
+    block_size, n_kv, cache_d = k_cache.shape[1], k_cache.shape[2], k_cache.shape[3]
+    yield head_dim < 1, lambda: f"head_dim must be positive, got {head_dim}"
+    yield head_dim != cache_d, lambda: f"q head_dim {head_dim} != cache head_dim {cache_d}"
+    yield n_kv < 1 or n_head % n_kv != 0, lambda: f"n_head ({n_head}) must be a multiple of n_kv_head ({n_kv})"
+    yield block_size < 1, lambda: f"block_size must be positive, got {block_size}"
+    yield not _pow2(block_size), lambda: (
+        f"block_size must be a power of two (16 and 32 are the supported sizes), got {block_size}")
+    yield not _pow2(head_dim), lambda: f"head_dim must be a power of two for the kernel, got {head_dim}"
+    yield not _MIN_HEAD_DIM <= head_dim <= _MAX_HEAD_DIM, lambda: (
+        f"head_dim {head_dim} is outside the sm_100a kernel's range {_MIN_HEAD_DIM}..{_MAX_HEAD_DIM}")
+
+    batch = q.shape[0]
+    yield block_table.dim() != 2, lambda: (
+        f"block_table must be (B, max_blocks), got shape {tuple(block_table.shape)}")
+    yield block_table.shape[0] != batch, lambda: (
+        f"block_table batch {block_table.shape[0]} does not match q batch {batch}")
+    yield block_table.dtype != torch.int32, lambda: (
+        "paged_decode requires an int32 block_table (the kernel's indexing contract); "
+        f"got {block_table.dtype}. Cast at the allocator boundary, not per step.")
+    yield seqlen.dim() != 1, lambda: f"seqlen must be (B,), got shape {tuple(seqlen.shape)}"
+    yield seqlen.shape[0] != batch, lambda: f"seqlen has {seqlen.shape[0]} entries for a batch of {batch}"
+    yield seqlen.dtype not in (torch.int32, torch.int64), lambda: f"seqlen must be int32 or int64, got {seqlen.dtype}"
     for name, tensor in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
                          ("block_table", block_table), ("seqlen", seqlen)):
-        if tensor.device != device:
-            raise ValueError(
-                f"{name} is on {tensor.device} but q is on {device}; all paged_decode tensors "
-                "must share one device"
-            )
-    if B == 0:
+        yield tensor.device != q.device, lambda name=name, tensor=tensor: (
+            f"{name} is on {tensor.device} but q is on {q.device}; all paged_decode tensors "
+            "must share one device")
+
+
+_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+
+
+def _pow2(n: int) -> bool:
+    return n > 0 and n & (n - 1) == 0
+
+
+def _validate(q, k_cache, v_cache, block_table, seqlen) -> None:
+    """Raise ValueError for the first violated rule of the layout contract, then range-check
+    seqlen against the table's capacity.
+
+    The range check needs the lengths on the host, so it is skipped while the same seqlen
+    tensor, unmodified since it last passed (same version counter; an inference tensor has
+    none and keeps its first pass), meets the same capacity: an engine that updates seqlen in
+    place once per step pays one host read per step, not one per layer.
+    """
+    for violated, message in _contract(q, k_cache, v_cache, block_table, seqlen):
+        if violated:
+            raise ValueError(message())
+    if q.shape[0] == 0:
         return
-    capacity = max_blocks * block_size
     global _SEQ_CHECK
+    capacity = block_table.shape[1] * k_cache.shape[1]
     version = -1 if seqlen.is_inference() else int(seqlen._version)
-    cached = _SEQ_CHECK
-    if cached is not None and cached[0] is seqlen and cached[1] == version and cached[2] == capacity:
+    last = _SEQ_CHECK
+    if last is not None and last[0] is seqlen and last[1:] == (version, capacity):
         return
-    low = int(seqlen.min())
-    high = int(seqlen.max())
+    low, high = int(seqlen.min()), int(seqlen.max())
     if low < 0:
         raise ValueError(f"seqlen values must be >= 0, got {low}")
     if high > capacity:
         raise ValueError(
             f"seqlen {high} exceeds the block table capacity {capacity} "
-            f"({max_blocks} blocks x {block_size} tokens)"
+            f"({block_table.shape[1]} blocks x {k_cache.shape[1]} tokens)"
         )
     _SEQ_CHECK = (seqlen, version, capacity)
 
