@@ -246,6 +246,37 @@ def _fusable_rows(t: torch.Tensor, dtype: torch.dtype) -> bool:
             and (t.stride(1) * es) % 16 == 0 and t.data_ptr() % 16 == 0)
 
 
+def _container_rules(pool, block_tables, lengths, rope_len: int, n_head, seats):
+    """The arguments' contract for a decode container as (violated, exception, message) rules,
+    in the order they are checked (the reference's ``PagedKV.__init__`` contract and messages,
+    model/paged.py:334-451; its callers match on them). Later rules rely on earlier ones
+    holding, so the rules are produced lazily and the caller stops at the first violation."""
+    yield not isinstance(pool, PagedPool), TypeError, lambda: f"PagedKV needs a PagedPool, got {type(pool).__name__}"
+    yield pool.device.type != "cuda", ValueError, lambda: (
+        "paged decode is the sm_100a CUDA block-table kernel; the gather control arm was "
+        f"deleted. The pool is on {pool.device}. Run the paged arm on CUDA, or use the seat "
+        "arm on CPU. The dense numeric oracle lives in oracle/.")
+    yield not TRITON_AVAILABLE, RuntimeError, lambda: (
+        "paged decode requires the sm_100a library that replaces the Triton kernel, but it "
+        f"could not be loaded ({_native.LOAD_ERROR}); there is no eager fallback.")
+    n_rows = len(block_tables)
+    yield n_rows < 1, ValueError, lambda: "PagedKV needs at least one row"
+    yield len(lengths) != n_rows, ValueError, lambda: (
+        f"PagedKV needs one length per block table, got {len(lengths)} for {n_rows}")
+    yield rope_len < 1, ValueError, lambda: f"rope_len (the run's position bound) must be >= 1, got {rope_len}"
+    n_head = pool.n_kv_head if n_head is None else int(n_head)
+    yield n_head % pool.n_kv_head != 0, ValueError, lambda: (
+        f"n_head ({n_head}) must be a multiple of n_kv_head ({pool.n_kv_head})")
+    yield len(seats) != n_rows, ValueError, lambda: f"PagedKV needs one seat per row, got {len(seats)} for {n_rows}"
+    for row, length in enumerate(lengths):
+        blocks = len(block_tables[row])
+        yield length < 0, ValueError, lambda row=row, length=length: f"row {row}: length must be >= 0, got {length}"
+        yield length > blocks * pool.block_size, IndexError, lambda row=row, length=length, blocks=blocks: (
+            f"row {row}: length {length} exceeds its block table's capacity ({blocks} blocks x {pool.block_size})")
+        yield length > rope_len, IndexError, lambda row=row, length=length: (
+            f"row {row}: length {length} exceeds the run's position bound {rope_len}")
+
+
 class PagedKV:
     """Decode-time container over a :class:`PagedPool` (the ``KvSlab`` step protocol).
 
@@ -262,58 +293,28 @@ class PagedKV:
     def __init__(self, pool: PagedPool, block_tables, lengths, *, rope_len: int, seats=None,
                  n_head: int | None = None, check_bounds: bool = True, fuse_append: bool = True,
                  overlap_layers: bool = True) -> None:
-        if not isinstance(pool, PagedPool):
-            raise TypeError(f"PagedKV needs a PagedPool, got {type(pool).__name__}")
-        if pool.device.type != "cuda":
-            raise ValueError(
-                "paged decode is the sm_100a CUDA block-table kernel; the gather control arm was "
-                f"deleted. The pool is on {pool.device}. Run the paged arm on CUDA, or use the seat "
-                "arm on CPU. The dense numeric oracle lives in oracle/."
-            )
-        if not TRITON_AVAILABLE:
-            raise RuntimeError(
-                "paged decode requires the sm_100a library that replaces the Triton kernel, but it "
-                f"could not be loaded ({_native.LOAD_ERROR}); there is no eager fallback."
-            )
-        n_rows = len(block_tables)
-        if n_rows < 1:
-            raise ValueError("PagedKV needs at least one row")
-        if len(lengths) != n_rows:
-            raise ValueError(f"PagedKV needs one length per block table, got {len(lengths)} for {n_rows}")
+        lengths = [int(n) for n in lengths]
         rope_len = int(rope_len)
-        if rope_len < 1:
-            raise ValueError(f"rope_len (the run's position bound) must be >= 1, got {rope_len}")
+        seats = list(range(len(block_tables))) if seats is None else list(seats)
+        for violated, error, message in _container_rules(pool, block_tables, lengths, rope_len, n_head, seats):
+            if violated:
+                raise error(message())
+        n_head = pool.n_kv_head if n_head is None else int(n_head)
 
         self.pool = pool
         self.n_layer = pool.n_layer
         self.n_kv_head = pool.n_kv_head
         self.head_dim = pool.head_dim
-        self.n_head = pool.n_kv_head if n_head is None else int(n_head)
-        if self.n_head % self.n_kv_head != 0:
-            raise ValueError(f"n_head ({self.n_head}) must be a multiple of n_kv_head ({self.n_kv_head})")
-        self.n_group = self.n_head // self.n_kv_head
+        self.n_head = n_head
+        self.n_group = n_head // pool.n_kv_head
         self.dtype = pool.dtype
         self.device = pool.device
         self.check_bounds = bool(check_bounds)
         self.block_tables = [list(bt) for bt in block_tables]
-        self.seats = list(range(n_rows)) if seats is None else list(seats)
-        if len(self.seats) != n_rows:
-            raise ValueError(f"PagedKV needs one seat per row, got {len(self.seats)} for {n_rows}")
-        self.row_of_seat = {seat: row for row, seat in enumerate(self.seats)}
-        self.batch = n_rows
+        self.seats = seats
+        self.row_of_seat = {seat: row for row, seat in enumerate(seats)}
+        self.batch = n_rows = len(block_tables)
         self.max_len = rope_len
-
-        lengths = [int(n) for n in lengths]
-        for row, (table, length) in enumerate(zip(self.block_tables, lengths)):
-            if length < 0:
-                raise ValueError(f"row {row}: length must be >= 0, got {length}")
-            if length > len(table) * pool.block_size:
-                raise IndexError(
-                    f"row {row}: length {length} exceeds its block table's capacity "
-                    f"({len(table)} blocks x {pool.block_size})"
-                )
-            if length > rope_len:
-                raise IndexError(f"row {row}: length {length} exceeds the run's position bound {rope_len}")
 
         self.pos = torch.tensor(lengths, dtype=torch.long, device=self.device)
         self.valid = torch.tensor(lengths, dtype=torch.long, device=self.device)
@@ -471,15 +472,15 @@ class PagedKV:
                out: torch.Tensor | None = None) -> torch.Tensor:
         """Block-table decode for one layer; ``q`` is ``(B, H, 1, D)``, output the same.
         ``out`` (optional) is a preallocated contiguous ``(B, H, 1, D)`` result buffer."""
-        if not self._seqlen_ready:
-            raise RuntimeError("PagedKV.attend() before build_mask(): seqlen is stale")
-        if not self._step_written:
-            raise RuntimeError("PagedKV.attend() before write(): this step has no token yet")
-        if dropout_p:
-            raise ValueError("paged decode is inference-only; dropout_p must be 0")
+        # The step protocol first (the reference's order and messages, model/paged.py:530-538).
         expected = (self.batch, self.n_head, 1, self.head_dim)
-        if tuple(q.shape) != expected:
-            raise ValueError(f"attend needs q {expected}, got {tuple(q.shape)}")
+        for violated, error, message in (
+                (not self._seqlen_ready, RuntimeError, "PagedKV.attend() before build_mask(): seqlen is stale"),
+                (not self._step_written, RuntimeError, "PagedKV.attend() before write(): this step has no token yet"),
+                (bool(dropout_p), ValueError, "paged decode is inference-only; dropout_p must be 0"),
+                (tuple(q.shape) != expected, ValueError, f"attend needs q {expected}, got {tuple(q.shape)}")):
+            if violated:
+                raise error(message)
         q3 = q[:, :, 0, :].contiguous()
         plan = self._plan_for(q3)
         out3 = None if out is None else out[:, :, 0, :]
