@@ -143,9 +143,7 @@ def _validate(q, k_cache, v_cache, block_table, seqlen) -> None:
     none and keeps its first pass), meets the same capacity: an engine that updates seqlen in
     place once per step pays one host read per step, not one per layer.
     """
-    for violated, message in _contract(q, k_cache, v_cache, block_table, seqlen):
-        if violated:
-            raise ValueError(message())
+    _raise_first(_contract(q, k_cache, v_cache, block_table, seqlen))
     if q.shape[0] == 0:
         return
     global _SEQ_CHECK
@@ -163,6 +161,46 @@ def _validate(q, k_cache, v_cache, block_table, seqlen) -> None:
             f"({block_table.shape[1]} blocks x {k_cache.shape[1]} tokens)"
         )
     _SEQ_CHECK = (seqlen, version, capacity)
+
+
+def _raise_first(rules) -> None:
+    """ValueError for the first violated (violated, message) rule of a contract."""
+    for violated, message in rules:
+        if violated:
+            raise ValueError(message())
+
+
+def _plan_contract(q, block_table, seqlen, k_caches, v_caches):
+    """What a plan needs beyond the per-call contract, as ordered (violated, message) rules
+    (the reference's plan messages, model/triton_decode.py:380-440): a contiguous query, int32
+    and unit-stride seqlen and block-table columns (both are held by reference, so in-place
+    updates must stay visible), and one K and one V pool per layer."""
+    yield q.dim() != 3, lambda: f"q must be (B, H, D), got shape {tuple(q.shape)}"
+    yield not q.is_contiguous(), lambda: (
+        f"paged_decode_plan needs a contiguous (B, H, D) query, got strides {q.stride()}; "
+        "call .contiguous() once, not per layer")
+    yield q.shape[0] == 0, lambda: "paged_decode_plan needs at least one row"
+    yield seqlen.dtype != torch.int32, lambda: (
+        "paged_decode_plan requires an int32 seqlen so in-place updates are visible; "
+        f"got {seqlen.dtype}. Cast once at the container boundary.")
+    yield seqlen.stride(0) != 1, lambda: (
+        f"paged_decode_plan requires a contiguous 1-D seqlen; got strides {seqlen.stride()}")
+    yield block_table.stride(1) != 1, lambda: (
+        f"paged_decode_plan requires a column-contiguous block table; got strides {block_table.stride()}")
+    yield len(k_caches) != len(v_caches) or not k_caches, lambda: (
+        f"paged_decode_plan needs one k_cache/v_cache per layer, got {len(k_caches)} / {len(v_caches)}")
+
+
+def _plan_layer_contract(k_cache, v_cache, k_first, v_first):
+    """Every layer's pools share the first layer's shapes and strides (the plan encodes one
+    launch geometry), and TMA can describe them as they are."""
+    yield k_cache.shape != k_first.shape or v_cache.shape != v_first.shape, lambda: (
+        "paged_decode_plan needs one pool shape for every layer")
+    yield k_cache.stride() != k_first.stride(), lambda: "paged_decode_plan needs one pool layout for every layer"
+    yield v_cache.stride() != v_first.stride(), lambda: "paged_decode_plan needs one v-pool layout for every layer"
+    yield not (_tma_ready(k_cache) and _tma_ready(v_cache)), lambda: (
+        "paged_decode_plan needs pools with a unit head_dim stride, 16-byte multiple strides and "
+        "a 16-byte aligned base (any contiguous pool qualifies)")
 
 
 def _tma_ready(pool: torch.Tensor) -> bool:
@@ -284,53 +322,14 @@ class PagedDecodePlan:
     def __init__(self, q, k_caches, v_caches, block_table, seqlen, *, scale: float | None = None):
         _require_backend()
         _require_cuda_tensors((("q", q), ("block_table", block_table), ("seqlen", seqlen)))
-        if q.dim() != 3:
-            raise ValueError(f"q must be (B, H, D), got shape {tuple(q.shape)}")
-        if not q.is_contiguous():
-            raise ValueError(
-                "paged_decode_plan needs a contiguous (B, H, D) query, got strides "
-                f"{q.stride()}; call .contiguous() once, not per layer"
-            )
+        k_caches, v_caches = list(k_caches), list(v_caches)
+        _raise_first(_plan_contract(q, block_table, seqlen, k_caches, v_caches))
         b, h, d = q.shape
-        if b == 0:
-            raise ValueError("paged_decode_plan needs at least one row")
-        if seqlen.dtype != torch.int32:
-            raise ValueError(
-                "paged_decode_plan requires an int32 seqlen so in-place updates are visible; "
-                f"got {seqlen.dtype}. Cast once at the container boundary."
-            )
-        if seqlen.stride(0) != 1:
-            raise ValueError(
-                f"paged_decode_plan requires a contiguous 1-D seqlen; got strides {seqlen.stride()}"
-            )
-        if block_table.stride(1) != 1:
-            raise ValueError(
-                "paged_decode_plan requires a column-contiguous block table; got strides "
-                f"{block_table.stride()}"
-            )
-        k_caches = list(k_caches)
-        v_caches = list(v_caches)
-        if len(k_caches) != len(v_caches) or not k_caches:
-            raise ValueError(
-                "paged_decode_plan needs one k_cache/v_cache per layer, got "
-                f"{len(k_caches)} / {len(v_caches)}"
-            )
         for layer, (k_cache, v_cache) in enumerate(zip(k_caches, v_caches)):
+            # the whole paged_decode contract once per layer, then the layers must agree
             _require_cuda_tensors(((f"k_cache[{layer}]", k_cache), (f"v_cache[{layer}]", v_cache)))
             _validate(q, k_cache, v_cache, block_table, seqlen)
-            if tuple(k_cache.shape) != tuple(k_caches[0].shape) or tuple(v_cache.shape) != tuple(
-                v_caches[0].shape
-            ):
-                raise ValueError("paged_decode_plan needs one pool shape for every layer")
-            if k_cache.stride() != k_caches[0].stride():
-                raise ValueError("paged_decode_plan needs one pool layout for every layer")
-            if v_cache.stride() != v_caches[0].stride():
-                raise ValueError("paged_decode_plan needs one v-pool layout for every layer")
-            if not (_tma_ready(k_cache) and _tma_ready(v_cache)):
-                raise ValueError(
-                    "paged_decode_plan needs pools with a unit head_dim stride, 16-byte multiple "
-                    "strides and a 16-byte aligned base (any contiguous pool qualifies)"
-                )
+            _raise_first(_plan_layer_contract(k_cache, v_cache, k_caches[0], v_caches[0]))
         self.n_layer = len(k_caches)
         self._k = k_caches
         self._v = v_caches
