@@ -337,8 +337,8 @@ int pd_set_decode_mode(int32_t mode, int32_t shared_stages, int32_t row_cost);
 int pd_get_decode_mode(int32_t* mode, int32_t* shared_stages, int32_t* row_cost);
 
 /* Prefill kernel for calls made afterwards: mode 0 (default) runs the tile math on the
- * 5th-generation tensor cores (tcgen05.mma with S and O accumulated in tensor memory, one
- * thread per query row for the softmax); mode 1 runs the warp-level mma.sync kernel. Both
+ * 5th-generation tensor cores (tcgen05.mma with S and O accumulated in tensor memory, two
+ * softmax threads per query row); mode 1 runs the warp-level mma.sync kernel. Both
  * compute pd_prefill's function; results agree within rounding. No reference counterpart. */
 int pd_set_prefill_mode(int32_t mode);
 int pd_get_prefill_mode(void);
