@@ -187,7 +187,7 @@ struct Launch {
 // stages with a full and an empty barrier each.
 size_t smem_for(bool cta, int warps, int stages, int rows, int stage_bytes, int* arrays_off, int* stage_off) {
   const size_t bars = round_up(size_t(cta ? 2 : warps) * stages * 8, 16);
-  const size_t arrays = round_up(size_t(1 + 32 + 64 + 3 * rows + 1) * 4, 16);
+  const size_t arrays = round_up(size_t(1 + 32 + 64 + 32 + 3 * rows + 1) * 4, 16);
   *arrays_off = int(bars);
   *stage_off = int(bars + arrays);
   return bars + arrays + 1024 /* run-time re-alignment slack */ + size_t(cta ? 1 : warps) * stages * stage_bytes;

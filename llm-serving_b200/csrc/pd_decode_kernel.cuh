@@ -261,8 +261,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   const int row_stride = CTA ? p.n_kv_head * C::ROW_BYTES : C::ROW_BYTES;       // token to token
 
   // Dynamic shared memory:
-  // [mbarriers | epoch | warp_sums[32] | key_lo[32] | key_hi[32] | lens[B] | pre[B+1] | apos[B] |
-  //  pad | stages].
+  // [mbarriers | epoch | warp_sums[32] | key_lo[32] | key_hi[32] | grp_cnt[32] | lens[B] | pre[B+1] |
+  //  apos[B] | pad | stages].
   // mbarriers: per-warp mode S per warp; CTA mode full[S] then empty[S].
   // The stage region is re-aligned to 1024 B at run time (the host adds the slack).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
@@ -270,7 +270,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   int* warp_sums = reinterpret_cast<int*>(smem + p.smem_arrays_off) + 1;
   unsigned* key_lo = reinterpret_cast<unsigned*>(warp_sums + 32);  // per warp: XOR of its rows' hashes
   unsigned* key_hi = key_lo + 32;
-  int* lens = reinterpret_cast<int*>(key_hi + 32);
+  int* grp_cnt = reinterpret_cast<int*>(key_hi + 32);  // arrivals per CTA group (unit mode), by first warp
+  int* lens = grp_cnt + 32;
   int* pre = lens + B;  // B + 1 entries: exclusive prefix of tiles per row
   int* apos = pre + B + 1;  // fused append: position to take from the source, or -1
   const uint32_t smem_base = smem_addr(smem);
@@ -391,6 +392,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     }
     if (lane == 31) warp_sums[warp] = incl;
     if (tid == 0) *reinterpret_cast<uint32_t*>(smem + p.smem_arrays_off) = ep;
+    if (tid < 32) grp_cnt[tid] = 0;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) key ^= __shfl_xor_sync(FULL_MASK, key, o);
     if (lane == 0) {
@@ -507,7 +509,6 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   // Step cache: this warp's record holds the split of these very lengths.
   const bool cached =
       use_step && __shfl_sync(FULL_MASK, lane == 0 && ((unsigned long long)rec_c.w << 32 | rec_c.z) == launch_key, 0);
-  if (!colmode) w = warp * int(gridDim.x) + int(blockIdx.x);  // spread low ids over all SMs
   if (cached) {
     u0 = __shfl_sync(FULL_MASK, (long long)rec_a.y << 32 | rec_a.x, 0);
     u1 = __shfl_sync(FULL_MASK, (long long)rec_a.w << 32 | rec_a.z, 0);
@@ -537,8 +538,18 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         if (int64_t(aligned) * 20 >= int64_t(workers) * 19) workers = aligned;
       }
     }
-    u0 = w < workers ? int64_t(w) * units / workers : 0;
-    u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
+  }
+  // Unit mode, worker numbering. When (nearly) every warp is a worker, consecutive workers
+  // share a CTA ("grouped"): the pieces of a split item then sit in few CTAs, and the pieces
+  // that end a range are folded in shared memory by the last warp of their CTA before one
+  // piece per CTA goes to the global merge. Otherwise low worker ids are spread over all SMs.
+  const bool grouped = !colmode && int64_t(workers) * 20 >= int64_t(gridDim.x) * nwarps * 19;
+  if (!colmode) {
+    w = grouped ? int(blockIdx.x) * nwarps + warp : warp * int(gridDim.x) + int(blockIdx.x);
+    if (!cached) {
+      u0 = w < workers ? int64_t(w) * units / workers : 0;
+      u1 = w < workers ? int64_t(w + 1) * units / workers : 0;
+    }
   }
   // Records this launch's split of its warp (when it computed it): header by lane 0, the
   // table windows the first copies used by every lane, made visible before the launch lets the
@@ -653,6 +664,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     return __shfl_sync(FULL_MASK, win_cur, page - win_base);
   };
 
+  const uint64_t kv_policy = l2_policy_evict_first();
   auto issue = [&](const Cursor& c, int s) {
     const int h = c.h;
     const int tok0 = c.tile << C::LOG_TILE;
@@ -669,12 +681,14 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       const int off = tok & (bs - 1);
       const int blk = block_of(c.b, page, npages);
       if (lane == 0) {
+        // K/V bytes are read once per launch: evict-first keeps the stream from evicting the
+        // split partials that the merges read back at the end.
         if constexpr (MMA) {  // swizzled map: (64 elements, token, head, 128-byte piece, block)
-          tma_load_5d(kdst + j * box_bytes, &kmap, bar, 0, off, h, 0, blk);
-          tma_load_5d(vdst + j * box_bytes, &vmap, bar, 0, off, h, 0, blk);
+          tma_load_5d_hint(kdst + j * box_bytes, &kmap, bar, 0, off, h, 0, blk, kv_policy);
+          tma_load_5d_hint(vdst + j * box_bytes, &vmap, bar, 0, off, h, 0, blk, kv_policy);
         } else {
-          tma_load_4d(kdst + j * box_bytes, &kmap, bar, 0, CTA ? 0 : h, off, blk);
-          tma_load_4d(vdst + j * box_bytes, &vmap, bar, 0, CTA ? 0 : h, off, blk);
+          tma_load_4d_hint(kdst + j * box_bytes, &kmap, bar, 0, CTA ? 0 : h, off, blk, kv_policy);
+          tma_load_4d_hint(vdst + j * box_bytes, &vmap, bar, 0, CTA ? 0 : h, off, blk, kv_policy);
         }
       }
     }
@@ -971,30 +985,43 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     }
   };
 
-  // Merge of split item (mb, mitem) by the piece that arrived last (ticket == pieces - 1).
-  // Pieces are the item's workers c_first..c_last in order; each lane owns NG consecutive
-  // float4 groups of the GT x D output (all of one q head) and folds the pieces in batches
-  // of MB with a running maximum, every load of a batch in flight together.
-  auto merge_if_last = [&](int mb, int mitem, int ticket) {
-    // The item's pieces: in unit mode the workers whose unit ranges overlap it, in column
-    // mode the CTAs whose column ranges overlap its row (slot pair of that CTA's warp mitem).
-    // (Column mode: the ranges holding the row's real tiles, virtual columns
-    // [vpre(mb) + row_cost, vpre(mb + 1)); a range of only the extra columns is not a piece.)
-    const int mntile = pre[mb + 1] - pre[mb];
-    const int64_t us = colmode ? vpre(mb) + rc : int64_t(items_per_row) * pre[mb] + int64_t(mitem) * mntile;
-    const int64_t total = colmode ? vcols : units;
-    const int nparts = colmode ? col_parts : workers;
-    const int c_first = worker_of(us, total, nparts);
-    const int c_last = worker_of(us + mntile - 1, total, nparts);
-    if (ticket != c_last - c_first) return;
-    __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
-    const int npieces = c_last - c_first + 1;
-    auto pair_of = [&](int c) -> int64_t { return colmode ? int64_t(c) * nwarps + mitem : int64_t(c); };
-    // Its first piece's slot: the range's first segment if the range starts at the item.
-    const bool first_starts_here = colmode ? range_start(c_first) == pre[mb]
-                                           : int64_t(c_first) * units / workers == us;
-    const int64_t first_slot = pair_of(c_first) * 2 + (first_starts_here ? 0 : 1);
-    auto slot_of = [&](int i) -> int64_t { return i == 0 ? first_slot : pair_of(c_first + i) * 2; };
+  // Unit mode: the workers whose ranges overlap item (b, item) are w_a .. w_b. Every piece ends
+  // its worker's range except possibly w_b's: when w_b's range runs past the item (mid), the
+  // item is that range's first segment, parked in slot 0 and arrived at once. w_t is the last
+  // worker whose piece ends its range (slot 1, or its CTA group's shared memory when grouped).
+  struct ItemSpan {
+    int w_a, w_b, w_t;
+    bool mid;
+  };
+  auto item_span = [&](int b, int item) -> ItemSpan {
+    const int nt = pre[b + 1] - pre[b];
+    const int64_t us = int64_t(items_per_row) * pre[b] + int64_t(item) * nt;
+    ItemSpan r;
+    r.w_a = worker_of(us, units, workers);
+    r.w_b = worker_of(us + nt - 1, units, workers);
+    r.mid = int64_t(r.w_b + 1) * units / workers > us + nt;
+    r.w_t = r.mid ? r.w_b - 1 : r.w_b;
+    return r;
+  };
+  // Pieces of a split item that reach the global merge (unit mode): one per CTA group of
+  // range-ending pieces (grouped numbering) or one per range-ending piece, then the mid piece.
+  auto global_reps = [&](const ItemSpan& sp) -> int {
+    return grouped ? sp.w_t / nwarps - sp.w_a / nwarps + 1 : sp.w_t - sp.w_a + 1;
+  };
+  // A range-ending piece parked in shared memory: warp j's own stages hold its accumulators
+  // (GT x D floats, head-major) followed by m[GT] and l[GT].
+  auto smem_piece = [&](int j) -> float* {
+    return reinterpret_cast<float*>(stage_base + size_t(j) * S * C::STAGE_BYTES);
+  };
+
+  // Folds npieces partial triples of item (mb, mitem) in piece order (piece i: m at ml_of(i),
+  // l at ml_of(i) + GT, accumulators at acc_of(i)) with a running maximum, and writes the
+  // result: the normalised output (mode 0) or the item's triple (mode 1) when dst_ml is null,
+  // otherwise one partial triple at dst_ml / dst_acc (a CTA group's piece). Each lane owns NG
+  // consecutive float4 groups of the GT x D output and folds the pieces in batches of MB,
+  // every load of a batch in flight together.
+  auto fold_pieces = [&](int mb, int mitem, int npieces, auto ml_of, auto acc_of, bool from_global,
+                         float* dst_ml, float* dst_acc) {
     const int mh = mitem / p.n_gchunks;
     const int mhq0 = mh * p.group + (mitem - mh * p.n_gchunks) * GT;
     // The item's output is GROUPS float4 groups, head-major; lane l owns groups t * 32 + l,
@@ -1015,6 +1042,10 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         if (g == gg) r = v[gg];
       return r;
     };
+    auto ld1 = [&](const float* q) -> float { return from_global ? __ldcg(q) : *q; };
+    auto ld4 = [&](const float* q) -> float4 {
+      return from_global ? __ldcg(reinterpret_cast<const float4*>(q)) : *reinterpret_cast<const float4*>(q);
+    };
     const int64_t hrow0 = int64_t(mb) * p.n_head + mhq0;
     for (int t0 = 0; t0 < NG; t0 += GB) {
       float M[GT], L[GT];
@@ -1031,16 +1062,18 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         float4 x[MB][GB];
 #pragma unroll
         for (int j = 0; j < MB; ++j) {
-          const int64_t sl = slot_of(i0 + j < npieces ? i0 + j : npieces - 1);
+          const int i = i0 + j < npieces ? i0 + j : npieces - 1;
+          const float* mlp = ml_of(i);
+          const float* ap = acc_of(i);
 #pragma unroll
           for (int g = 0; g < GT; ++g) {
-            mj[j][g] = __ldcg(p.ws_ml + sl * (2 * GT) + g);
-            lj[j][g] = __ldcg(p.ws_ml + sl * (2 * GT) + GT + g);
+            mj[j][g] = ld1(mlp + g);
+            lj[j][g] = ld1(mlp + GT + g);
           }
 #pragma unroll
           for (int t = 0; t < GB; ++t) {
             const int jg = (t0 + t) * 32 + lane;
-            x[j][t] = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + sl * (GT * D)) + (jg < GROUPS ? jg : 0));
+            x[j][t] = ld4(ap + 4 * (jg < GROUPS ? jg : 0));
           }
         }
         float Mn[GT], rs[GT];
@@ -1088,7 +1121,13 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         if (jg >= GROUPS) continue;
         const int g = head_of(t0 + t);
         const int col = (jg % GPH) * 4;
-        if (p.mode == 0) {
+        if (dst_ml != nullptr) {  // a CTA group's piece, same layout as the pieces
+          *reinterpret_cast<float4*>(dst_acc + g * D + col) = a[t];
+          if (col == 0) {
+            dst_ml[g] = pick(M, g);
+            dst_ml[GT + g] = pick(L, g);
+          }
+        } else if (p.mode == 0) {
           const float inv = 1.f / fmaxf(pick(L, g), 1.f);
           T* o = reinterpret_cast<T*>(p.out) + int64_t(mb) * p.o_sb + int64_t(mhq0 + g) * p.o_sh + col;
           o[0] = E::from_float(a[t].x * inv);
@@ -1104,6 +1143,46 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         }
       }
     }
+  };
+
+  // Merge of split item (mb, mitem) by the piece that arrived last (ticket == pieces - 1), from
+  // the pieces' workspace slots in piece order.
+  auto merge_if_last = [&](int mb, int mitem, int ticket) {
+    auto ml_at = [&](int64_t sl) -> const float* { return p.ws_ml + sl * (2 * GT); };
+    auto acc_at_slot = [&](int64_t sl) -> const float* { return p.ws_acc + sl * (GT * D); };
+    if (colmode) {
+      // Column mode: the pieces are the CTAs whose column ranges overlap the item's row (slot
+      // pair of that CTA's warp mitem): the ranges holding the row's real tiles, virtual
+      // columns [vpre(mb) + row_cost, vpre(mb + 1)); a range of only the extra columns is not a
+      // piece. A CTA's first segment sits in slot 0 of its pair, a later one in slot 1.
+      const int mntile = pre[mb + 1] - pre[mb];
+      const int64_t us = vpre(mb) + rc;
+      const int c_first = worker_of(us, vcols, col_parts);
+      const int c_last = worker_of(us + mntile - 1, vcols, col_parts);
+      if (ticket != c_last - c_first) return;
+      __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
+      const bool first_starts_here = range_start(c_first) == pre[mb];
+      auto slot_of = [&](int i) -> int64_t {
+        const int64_t pair = int64_t(c_first + i) * nwarps + mitem;
+        return pair * 2 + (i == 0 && !first_starts_here ? 1 : 0);
+      };
+      fold_pieces(mb, mitem, c_last - c_first + 1, [&](int i) { return ml_at(slot_of(i)); },
+                  [&](int i) { return acc_at_slot(slot_of(i)); }, true, nullptr, nullptr);
+      return;
+    }
+    const ItemSpan sp = item_span(mb, mitem);
+    const int nreps = global_reps(sp);
+    if (ticket != nreps + (sp.mid ? 1 : 0) - 1) return;
+    __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
+    // Piece i < nreps: the range-ending piece(s) of the i-th CTA group (grouped) or worker,
+    // in slot 1 of its first worker; then the mid piece in slot 0 of w_b.
+    auto slot_of = [&](int i) -> int64_t {
+      if (i >= nreps) return int64_t(sp.w_b) * 2;
+      const int rep = grouped ? (i == 0 ? sp.w_a : (sp.w_a / nwarps + i) * nwarps) : sp.w_a + i;
+      return int64_t(rep) * 2 + 1;
+    };
+    fold_pieces(mb, mitem, nreps + (sp.mid ? 1 : 0), [&](int i) { return ml_at(slot_of(i)); },
+                [&](int i) { return acc_at_slot(slot_of(i)); }, true, nullptr, nullptr);
   };
 
   // ---- pipelined tile loop: scores of tile k+1 overlap softmax + P.V of tile k ---------
@@ -1173,8 +1252,21 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     const bool seg_end = (k == nunits - 1) || (cur.tile == cur.ntile - 1);
     if (__builtin_expect(seg_end, 0)) {
       const bool whole = seg_first_tile == 0 && cur.tile == cur.ntile - 1;
-      // Split item: (m, l, acc) go to this worker's slot and the last arrival merges.
-      const int64_t slot = int64_t(wslot) * 2 + (first_segment ? 0 : 1);
+      // Split item: (m, l, acc) go to this worker's slot and the last arrival merges. Column
+      // mode: a range's first segment in slot 0, a later one in slot 1. Unit mode: a segment
+      // that ends inside the range in slot 0, the one that ends the range in slot 1 -- or, with
+      // grouped numbering when other warps of this CTA hold pieces of the item too, in this
+      // warp's own stages (no copy is in flight any more), folded there by the group's last.
+      const bool last_seg = k == nunits - 1;
+      const int64_t slot = int64_t(wslot) * 2 + (colmode ? (first_segment ? 0 : 1) : (last_seg ? 1 : 0));
+      bool local_piece = false;
+      if (!colmode && grouped && last_seg && !whole) {
+        const ItemSpan sp = item_span(cur.b, cur.item);
+        const int cta0 = int(blockIdx.x) * nwarps;
+        local_piece = min(sp.w_t, cta0 + nwarps - 1) > max(sp.w_a, cta0);
+      }
+      float* const piece_ml = local_piece ? smem_piece(warp) + GT * D : p.ws_ml + slot * (2 * GT);
+      float* const piece_acc = local_piece ? smem_piece(warp) : p.ws_acc + slot * (GT * D);
       if constexpr (MMA) {
         float lt[2];
         mw.total_l(lt);
@@ -1187,8 +1279,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
             mw.store_acc(p.part_acc + hrow * D);
           }
         } else {
-          mw.store_ml(p.ws_ml + slot * (2 * GT), p.ws_ml + slot * (2 * GT) + GT, lt);
-          mw.store_acc(p.ws_acc + slot * (GT * D));
+          mw.store_ml(piece_ml, piece_ml + GT, lt);
+          mw.store_acc(piece_acc);
         }
       } else {
         float l_tot[GT];
@@ -1253,8 +1345,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
           }
         } else {
           // Split item: park (m, l, acc) in this worker's slot, then the last arrival merges.
-          float* ml = p.ws_ml + slot * (2 * GT);
-          float* wa = p.ws_acc + slot * (GT * D);
+          float* ml = piece_ml;
+          float* wa = piece_acc;
           if (lane == 0) {
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
@@ -1315,8 +1407,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
   }
 
   // ---- arrivals of this range's split segments; the last piece of an item merges it ----
-  // No copy is in flight any more, so the fence only waits for the partial stores.
-  if (n_pend > 0) {
+  if (n_pend > 0 && colmode) {
+    // No copy is in flight any more, so the fence only waits for the partial stores.
     __threadfence();
     __syncwarp();
     int t0 = 0, t1 = 0;
@@ -1330,6 +1422,60 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     }
     merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0));
     if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0));
+  } else if (n_pend > 0) {
+    // Unit mode: the range's first segment when it ended inside the range (the mid piece,
+    // arrived early) and/or the segment that ends the range (the tail piece).
+    const uint32_t tag = counter_tag(epoch, p.tag_salt);
+    const bool has_mid = early;
+    const bool has_tail = n_pend > 1 || !early;
+    const int tb = n_pend > 1 ? pend_b1 : pend_b0;
+    const int ti = n_pend > 1 ? pend_item1 : pend_item0;
+    int t_mid = -1, t_tail = -1;
+    if (has_mid) {
+      const bool stale = uint32_t(early_old >> 32) != tag;  // lane 0's view; others unused
+      if (lane == 0 && stale) __threadfence();  // its re-arrival must release the partial again
+      if (lane == 0)
+        t_mid = !stale ? int(uint32_t(early_old))
+                       : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, tag, p.err,
+                                     p.wait_ns);
+    }
+    if (has_tail) {
+      const ItemSpan sp = item_span(tb, ti);
+      const int cta0 = int(blockIdx.x) * nwarps;
+      const int m0 = max(sp.w_a, cta0) - cta0;
+      const int m1 = min(sp.w_t, cta0 + nwarps - 1) - cta0;
+      bool arrive = true;  // this warp arrives on the item's counter with a piece in slot 1
+      if (grouped && m1 > m0) {
+        // The pieces of warps m0..m1 of this CTA sit in their stages: the last of them to
+        // arrive folds them, in warp order, into the CTA group's piece -- or into the output
+        // when the group holds the whole item.
+        __threadfence_block();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(grp_cnt + m0, 1);
+        old = __shfl_sync(FULL_MASK, old, 0);
+        arrive = old == m1 - m0;
+        if (arrive) {
+          __threadfence_block();
+          const bool whole_item = global_reps(sp) == 1 && !sp.mid;
+          const int64_t rslot = int64_t(cta0 + m0) * 2 + 1;
+          fold_pieces(
+              tb, ti, m1 - m0 + 1, [&](int i) -> const float* { return smem_piece(m0 + i) + GT * D; },
+              [&](int i) -> const float* { return smem_piece(m0 + i); }, false,
+              whole_item ? nullptr : p.ws_ml + rslot * (2 * GT), whole_item ? nullptr : p.ws_acc + rslot * (GT * D));
+          arrive = !whole_item;
+        }
+      }
+      if (arrive) {
+        __threadfence();  // release: the piece's partial stores (every lane's)
+        __syncwarp();
+        if (lane == 0) t_tail = take_ticket(p.counters + int64_t(tb) * items_per_row + ti, tag, p.err, p.wait_ns);
+      }
+    }
+    t_mid = __shfl_sync(FULL_MASK, t_mid, 0);
+    t_tail = __shfl_sync(FULL_MASK, t_tail, 0);
+    if (t_mid >= 0) merge_if_last(pend_b0, pend_item0, t_mid);
+    if (t_tail >= 0) merge_if_last(tb, ti, t_tail);
   }
   return epoch;
 }
