@@ -222,6 +222,17 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Atomic add at GPU scope with acquire-release semantics: it releases this thread's earlier
+// writes (and those that its warp ordered before it with __syncwarp) and, when its answer says
+// that every other piece has arrived, acquires theirs; after a __syncwarp the whole warp may
+// read them.
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu(unsigned long long* p,
+                                                                   unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+
 // Atomic add at GPU scope with release semantics: this thread's earlier writes (and those of
 // threads synchronised with it, e.g. by __syncwarp) are visible before the add is.
 __device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long* p,

@@ -180,15 +180,16 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 // Arrival on the counter shared by the pieces of one split item; returns how many pieces of
 // this launch arrived before. Counters live in workspace memory that is never cleared and hold
 // (tag << 32) | count. Every launch re-tags its item counters with its own tag in the
-// prologue (each CTA a share of them), so an arrival is one atomicAdd with no contention
-// beyond the hardware's. An arrival that beats its counter's re-tag sees another tag; its
+// prologue (each CTA a share of them), so an arrival is one acquire-release add (it releases
+// the partial the caller's warp stored, and the last piece's acquires the others'), with no
+// contention beyond the hardware's. An arrival that beats its counter's re-tag sees another tag; its
 // add lands on a value the re-tag overwrites, so it waits for the re-tag and adds again
 // (bounded: on expiry it records DEVERR_WAIT_TIMEOUT and returns -1, i.e. "not last").
 __device__ __forceinline__ int take_ticket(unsigned long long* counter, uint32_t tag, unsigned* err,
                                            unsigned long long limit_ns) {
   unsigned long long t0 = 0;
   for (;;) {
-    const unsigned long long old = atomicAdd(counter, 1ull);  // callers fence before arriving
+    const unsigned long long old = atom_add_acq_rel_gpu(counter, 1ull);
     if (uint32_t(old >> 32) == tag) return int(uint32_t(old));
     const unsigned long long now = global_timer_ns();
     if (t0 == 0 && limit_ns >= TEST_LIMIT_NS) {
@@ -1147,7 +1148,17 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
 
   // Merge of split item (mb, mitem) by the piece that arrived last (ticket == pieces - 1), from
   // the pieces' workspace slots in piece order.
-  auto merge_if_last = [&](int mb, int mitem, int ticket) {
+  // `acquired`: the ticket came from an acquire-release arrival (take_ticket) of this warp's
+  // lane 0, so the other pieces' partials are visible to the warp after a __syncwarp; an early
+  // arrival is release-only, and its merge fences instead.
+  auto acquire_pieces = [&](bool acquired) {
+    if (acquired) {
+      __syncwarp();
+    } else {
+      __threadfence();
+    }
+  };
+  auto merge_if_last = [&](int mb, int mitem, int ticket, bool acquired) {
     auto ml_at = [&](int64_t sl) -> const float* { return p.ws_ml + sl * (2 * GT); };
     auto acc_at_slot = [&](int64_t sl) -> const float* { return p.ws_acc + sl * (GT * D); };
     if (colmode) {
@@ -1160,7 +1171,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       const int c_first = worker_of(us, vcols, col_parts);
       const int c_last = worker_of(us + mntile - 1, vcols, col_parts);
       if (ticket != c_last - c_first) return;
-      __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
+      acquire_pieces(acquired);  // the other pieces' partials
       const bool first_starts_here = range_start(c_first) == pre[mb];
       auto slot_of = [&](int i) -> int64_t {
         const int64_t pair = int64_t(c_first + i) * nwarps + mitem;
@@ -1173,7 +1184,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     const ItemSpan sp = item_span(mb, mitem);
     const int nreps = global_reps(sp);
     if (ticket != nreps + (sp.mid ? 1 : 0) - 1) return;
-    __threadfence();  // acquire: the other pieces' partials (each fenced before arriving)
+    acquire_pieces(acquired);  // the other pieces' partials
     // Piece i < nreps: the range-ending piece(s) of the i-th CTA group (grouped) or worker,
     // in slot 1 of its first worker; then the mid piece in slot 0 of w_b.
     auto slot_of = [&](int i) -> int64_t {
@@ -1408,20 +1419,20 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
 
   // ---- arrivals of this range's split segments; the last piece of an item merges it ----
   if (n_pend > 0 && colmode) {
-    // No copy is in flight any more, so the fence only waits for the partial stores.
-    __threadfence();
+    // Every lane's partial stores precede lane 0's arrivals, which release them.
     __syncwarp();
-    int t0 = 0, t1 = 0;
+    int t0 = 0, t1 = 0, early_ok = 0;
     if (lane == 0) {
       // An early add that beat the counter's re-tag was overwritten by it: arrive again.
       const uint32_t tag = counter_tag(epoch, p.tag_salt);
-      t0 = early && uint32_t(early_old >> 32) == tag
-               ? int(uint32_t(early_old))
-               : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, tag, p.err, p.wait_ns);
+      early_ok = early && uint32_t(early_old >> 32) == tag;
+      t0 = early_ok ? int(uint32_t(early_old))
+                    : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, tag, p.err, p.wait_ns);
       if (n_pend > 1) t1 = take_ticket(p.counters + int64_t(pend_b1) * items_per_row + pend_item1, tag, p.err, p.wait_ns);
     }
-    merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0));
-    if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0));
+    early_ok = __shfl_sync(FULL_MASK, early_ok, 0);
+    merge_if_last(pend_b0, pend_item0, __shfl_sync(FULL_MASK, t0, 0), !early_ok);
+    if (n_pend > 1) merge_if_last(pend_b1, pend_item1, __shfl_sync(FULL_MASK, t1, 0), true);
   } else if (n_pend > 0) {
     // Unit mode: the range's first segment when it ended inside the range (the mid piece,
     // arrived early) and/or the segment that ends the range (the tail piece).
@@ -1430,14 +1441,14 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     const bool has_tail = n_pend > 1 || !early;
     const int tb = n_pend > 1 ? pend_b1 : pend_b0;
     const int ti = n_pend > 1 ? pend_item1 : pend_item0;
-    int t_mid = -1, t_tail = -1;
+    int t_mid = -1, t_tail = -1, mid_acq = 0;
     if (has_mid) {
       const bool stale = uint32_t(early_old >> 32) != tag;  // lane 0's view; others unused
-      if (lane == 0 && stale) __threadfence();  // its re-arrival must release the partial again
       if (lane == 0)
         t_mid = !stale ? int(uint32_t(early_old))
                        : take_ticket(p.counters + int64_t(pend_b0) * items_per_row + pend_item0, tag, p.err,
                                      p.wait_ns);
+      mid_acq = stale;  // a re-arrival through take_ticket acquires
     }
     if (has_tail) {
       const ItemSpan sp = item_span(tb, ti);
@@ -1467,15 +1478,15 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
         }
       }
       if (arrive) {
-        __threadfence();  // release: the piece's partial stores (every lane's)
-        __syncwarp();
+        __syncwarp();  // every lane's partial stores precede lane 0's releasing arrival
         if (lane == 0) t_tail = take_ticket(p.counters + int64_t(tb) * items_per_row + ti, tag, p.err, p.wait_ns);
       }
     }
     t_mid = __shfl_sync(FULL_MASK, t_mid, 0);
     t_tail = __shfl_sync(FULL_MASK, t_tail, 0);
-    if (t_mid >= 0) merge_if_last(pend_b0, pend_item0, t_mid);
-    if (t_tail >= 0) merge_if_last(tb, ti, t_tail);
+    mid_acq = __shfl_sync(FULL_MASK, mid_acq, 0);
+    if (t_mid >= 0) merge_if_last(pend_b0, pend_item0, t_mid, mid_acq != 0);
+    if (t_tail >= 0) merge_if_last(tb, ti, t_tail, true);
   }
   return epoch;
 }
