@@ -1015,14 +1015,41 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     return reinterpret_cast<float*>(stage_base + size_t(j) * S * C::STAGE_BYTES);
   };
 
-  // Folds npieces partial triples of item (mb, mitem) in piece order (piece i: m at ml_of(i),
-  // l at ml_of(i) + GT, accumulators at acc_of(i)) with a running maximum, and writes the
+  // Where the pieces of a fold live. One fold routine serves every kind, so that its code
+  // exists once in the kernel. kind 0: column mode, the slot pairs of CTAs a = c_first ..
+  // (b = whether the first CTA's range starts at the row, c = the item's warp); kind 1: unit
+  // mode, the item's global pieces (a = w_a, b = nreps, c = w_b; see merge_if_last); kind 2: the
+  // range-ending pieces of a CTA group in the stages of warps a, a + 1, ...
+  struct FoldSrc {
+    int kind, a, b, c;
+  };
+  auto piece_ptr = [&](const FoldSrc& src, int i, const float*& ml, const float*& acc) {
+    if (src.kind == 2) {
+      acc = smem_piece(src.a + i);
+      ml = acc + GT * D;
+      return;
+    }
+    int64_t sl;
+    if (src.kind == 0) {
+      sl = (int64_t(src.a + i) * nwarps + src.c) * 2 + (i == 0 && !src.b ? 1 : 0);
+    } else if (i >= src.b) {
+      sl = int64_t(src.c) * 2;
+    } else {
+      const int rep = grouped ? (i == 0 ? src.a : (src.a / nwarps + i) * nwarps) : src.a + i;
+      sl = int64_t(rep) * 2 + 1;
+    }
+    ml = p.ws_ml + sl * (2 * GT);
+    acc = p.ws_acc + sl * (GT * D);
+  };
+
+  // Folds npieces partial triples of item (mb, mitem) in piece order (piece i's m at ml, its l
+  // at ml + GT, its accumulators at acc, from piece_ptr) with a running maximum, and writes the
   // result: the normalised output (mode 0) or the item's triple (mode 1) when dst_ml is null,
   // otherwise one partial triple at dst_ml / dst_acc (a CTA group's piece). Each lane owns NG
   // consecutive float4 groups of the GT x D output and folds the pieces in batches of MB,
   // every load of a batch in flight together.
-  auto fold_pieces = [&](int mb, int mitem, int npieces, auto ml_of, auto acc_of, bool from_global,
-                         float* dst_ml, float* dst_acc) {
+  auto fold_pieces = [&](int mb, int mitem, int npieces, const FoldSrc& src, float* dst_ml, float* dst_acc) {
+    const bool from_global = src.kind != 2;
     const int mh = mitem / p.n_gchunks;
     const int mhq0 = mh * p.group + (mitem - mh * p.n_gchunks) * GT;
     // The item's output is GROUPS float4 groups, head-major; lane l owns groups t * 32 + l,
@@ -1064,8 +1091,9 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
 #pragma unroll
         for (int j = 0; j < MB; ++j) {
           const int i = i0 + j < npieces ? i0 + j : npieces - 1;
-          const float* mlp = ml_of(i);
-          const float* ap = acc_of(i);
+          const float* mlp;
+          const float* ap;
+          piece_ptr(src, i, mlp, ap);
 #pragma unroll
           for (int g = 0; g < GT; ++g) {
             mj[j][g] = ld1(mlp + g);
@@ -1159,8 +1187,6 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     }
   };
   auto merge_if_last = [&](int mb, int mitem, int ticket, bool acquired) {
-    auto ml_at = [&](int64_t sl) -> const float* { return p.ws_ml + sl * (2 * GT); };
-    auto acc_at_slot = [&](int64_t sl) -> const float* { return p.ws_acc + sl * (GT * D); };
     if (colmode) {
       // Column mode: the pieces are the CTAs whose column ranges overlap the item's row (slot
       // pair of that CTA's warp mitem): the ranges holding the row's real tiles, virtual
@@ -1173,12 +1199,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
       if (ticket != c_last - c_first) return;
       acquire_pieces(acquired);  // the other pieces' partials
       const bool first_starts_here = range_start(c_first) == pre[mb];
-      auto slot_of = [&](int i) -> int64_t {
-        const int64_t pair = int64_t(c_first + i) * nwarps + mitem;
-        return pair * 2 + (i == 0 && !first_starts_here ? 1 : 0);
-      };
-      fold_pieces(mb, mitem, c_last - c_first + 1, [&](int i) { return ml_at(slot_of(i)); },
-                  [&](int i) { return acc_at_slot(slot_of(i)); }, true, nullptr, nullptr);
+      fold_pieces(mb, mitem, c_last - c_first + 1, FoldSrc{0, c_first, first_starts_here ? 1 : 0, mitem}, nullptr,
+                  nullptr);
       return;
     }
     const ItemSpan sp = item_span(mb, mitem);
@@ -1187,13 +1209,7 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
     acquire_pieces(acquired);  // the other pieces' partials
     // Piece i < nreps: the range-ending piece(s) of the i-th CTA group (grouped) or worker,
     // in slot 1 of its first worker; then the mid piece in slot 0 of w_b.
-    auto slot_of = [&](int i) -> int64_t {
-      if (i >= nreps) return int64_t(sp.w_b) * 2;
-      const int rep = grouped ? (i == 0 ? sp.w_a : (sp.w_a / nwarps + i) * nwarps) : sp.w_a + i;
-      return int64_t(rep) * 2 + 1;
-    };
-    fold_pieces(mb, mitem, nreps + (sp.mid ? 1 : 0), [&](int i) { return ml_at(slot_of(i)); },
-                [&](int i) { return acc_at_slot(slot_of(i)); }, true, nullptr, nullptr);
+    fold_pieces(mb, mitem, nreps + (sp.mid ? 1 : 0), FoldSrc{1, sp.w_a, nreps, sp.w_b}, nullptr, nullptr);
   };
 
   // ---- pipelined tile loop: scores of tile k+1 overlap softmax + P.V of tile k ---------
@@ -1470,10 +1486,8 @@ __device__ __forceinline__ uint32_t decode_body(const DecodeParams& p, const CUt
           __threadfence_block();
           const bool whole_item = global_reps(sp) == 1 && !sp.mid;
           const int64_t rslot = int64_t(cta0 + m0) * 2 + 1;
-          fold_pieces(
-              tb, ti, m1 - m0 + 1, [&](int i) -> const float* { return smem_piece(m0 + i) + GT * D; },
-              [&](int i) -> const float* { return smem_piece(m0 + i); }, false,
-              whole_item ? nullptr : p.ws_ml + rslot * (2 * GT), whole_item ? nullptr : p.ws_acc + rslot * (GT * D));
+          fold_pieces(tb, ti, m1 - m0 + 1, FoldSrc{2, m0, 0, 0}, whole_item ? nullptr : p.ws_ml + rslot * (2 * GT),
+                      whole_item ? nullptr : p.ws_acc + rslot * (GT * D));
           arrive = !whole_item;
         }
       }
